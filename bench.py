@@ -1,0 +1,392 @@
+"""Benchmark of the B200 hot path (one JSON line on rank 0).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+
+Headline workload (BASELINE second config): fused residual add + RMSNorm +
+per-token FP8 (e4m3) quantisation of bf16 x, residual [8192, 8192] ~ N(0, 1) with
+weight ~ N(1, 0.02), eps 1e-6.  A step is one call of that operator over one
+[8192, 8192] batch; under torchrun every rank processes its own batch (rows are
+sharded across GPUs with no collective on the data path: weak scaling).
+
+* ``value``: whole-job HBM throughput (algorithmic bytes of all ranks / the
+  slowest rank's device time), inputs resident in HBM.  Per step the kernel
+  reads x, residual (2 x 134 MB) and the weight and writes the updated residual,
+  the codes and the scales: 469,811,200 B.  Inputs are larger than L2, so no L2
+  flush is needed between steps.
+* ``e2e``: the same metric through the public op with HOST buffers: each step
+  copies x, residual and weight from pinned host memory, runs the op and copies
+  residual_out, codes and scales back.
+* ``roofline``: the fused kernel's achieved GB/s against the measured HBM copy
+  bandwidth; ``traffic`` is the DRAM bytes of one launch from the committed ncu
+  summary.
+* ``cpu_baseline``: the numpy oracle (a port of the reference's CPU algorithm)
+  timed on this host's cores on a bounded row sample.
+* ``secondary``: the other hot-path kernels at their BASELINE configs (N=1 only).
+
+``--impl reference`` times the reference algorithm's CPU port on the host cores
+(rank 0 only) for the same metric and prints it with ``"impl": "reference"``.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import re
+import statistics
+import subprocess
+import sys
+import threading
+import time
+from concurrent.futures import ThreadPoolExecutor
+from pathlib import Path
+
+import numpy as np
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+
+METRIC = "HBM TB/s & int8 TOPS as % of B200 peak at 1/2/4/8 GPU; µs/call vs CPU ref"
+M_ROWS, HIDDEN, EPS = 8192, 8192, 1e-6
+FALLBACK_HBM_GBS = 6650.0
+
+
+def c2_bytes(rows: int, hidden: int) -> int:
+    # x + residual (bf16) + weight (bf16) + residual_out (bf16) + e4m3 codes + fp32 scales
+    return 2 * rows * hidden * 2 + hidden * 2 + rows * hidden * 2 + rows * hidden + rows * 4
+
+
+def peaks():
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        d = json.loads(p.read_text())
+        return float(d["hbm_gbs"]), float(d.get("bf16_tflops", 1590.0)), "measured"
+    return FALLBACK_HBM_GBS, 1590.0, "fallback"
+
+
+def profile_traffic(name: str):
+    """DRAM bytes per launch recorded in profiles/<name> (line `traffic_per_launch_bytes: N`)."""
+    p = ROOT / "profiles" / name
+    if not p.exists():
+        return None
+    m = re.search(r"traffic_per_launch_bytes:\s*([0-9]+)", p.read_text())
+    return int(m.group(1)) if m else None
+
+
+# ------------------------------------------------------------------------------------------ clocks
+class ClockSampler:
+    """nvidia-smi clock / throttle-reason sampler for the timed region."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index: int):
+        self.gpu = gpu_index
+        self.samples = []
+        self.proc = None
+        self.thread = None
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--id={self.gpu}", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                 "-lms", "100"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except OSError:
+            self.proc = None
+            return self
+        self.thread = threading.Thread(target=self._read, daemon=True)
+        self.thread.start()
+        t0 = time.time()
+        while not self.samples and time.time() - t0 < 5:
+            time.sleep(0.02)
+        return self
+
+    def _read(self):
+        for line in self.proc.stdout:
+            parts = [p.strip() for p in line.split(",")]
+            if len(parts) >= 9:
+                self.samples.append((time.time(), parts))
+
+    def stop(self):
+        if self.proc:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+
+    def summary(self, t0: float, t1: float, window: str):
+        inside = [p for (t, p) in self.samples if t0 <= t <= t1]
+        if not inside:
+            return None
+        def num(x):
+            try:
+                return float(x)
+            except ValueError:
+                return None
+        sm = [num(p[1]) for p in inside if num(p[1]) is not None]
+        reasons = set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for p in inside:
+            for name, v in zip(names, p[5:9]):
+                if v.strip().lower() == "active":
+                    reasons.add(name)
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": num(inside[0][2]),
+                "reasons": sorted(reasons), "samples": len(inside), "window": window,
+                "power_w_max": max((num(p[3]) or 0.0) for p in inside)}
+
+
+# ------------------------------------------------------------------------------------------ CPU leg
+def cpu_port_throughput(budget_s: float = 12.0, rows_per_task: int = 64):
+    """Time the oracle (numpy port of the reference algorithm) on a bounded row sample.
+
+    Rows of the headline workload are quantised in parallel chunks (numpy releases the GIL
+    inside its kernels) until ``budget_s`` of wall time is used or every row is done.
+    Returns (TB/s of algorithmic bytes, threads, sample description).
+    """
+    from oracle import rmsnorm
+    from oracle.numerics import round_bf16
+
+    threads = len(os.sched_getaffinity(0)) if hasattr(os, "sched_getaffinity") else (os.cpu_count() or 1)
+    rng = np.random.default_rng(1234)
+    w = round_bf16((1.0 + 0.02 * rng.standard_normal(HIDDEN)).astype(np.float32))
+    chunk_x = round_bf16(rng.standard_normal((rows_per_task, HIDDEN)).astype(np.float32))
+    chunk_r = round_bf16(rng.standard_normal((rows_per_task, HIDDEN)).astype(np.float32))
+    rmsnorm.add_rmsnorm_quant(chunk_x[:4], chunk_r[:4], w, EPS, "e4m3")        # warm-up
+
+    def task(_):
+        rmsnorm.add_rmsnorm_quant(chunk_x, chunk_r, w, EPS, "e4m3")
+        return rows_per_task
+
+    done = 0
+    t0 = time.perf_counter()
+    with ThreadPoolExecutor(max_workers=threads) as ex:
+        while done < M_ROWS and time.perf_counter() - t0 < budget_s:
+            n = min(threads, (M_ROWS - done) // rows_per_task)
+            done += sum(ex.map(task, range(max(n, 1))))
+    dt = time.perf_counter() - t0
+    tbs = c2_bytes(done, HIDDEN) / dt / 1e12
+    return tbs, threads, f"{done} of {M_ROWS} rows x {HIDDEN} of the headline workload, {dt:.2f} s wall"
+
+
+# ------------------------------------------------------------------------------------------ GPU leg
+def make_c2_inputs(torch, dev, seed: int, rows: int = M_ROWS, hidden: int = HIDDEN):
+    g = torch.Generator(device=dev).manual_seed(seed)
+    x = torch.randn((rows, hidden), generator=g, device=dev).to(torch.bfloat16)
+    r = torch.randn((rows, hidden), generator=g, device=dev).to(torch.bfloat16)
+    w = (1.0 + 0.02 * torch.randn((hidden,), generator=g, device=dev)).to(torch.bfloat16)
+    return x, r, w
+
+
+def time_region(torch, fn, steps: int, dist, world: int):
+    """Barrier + sync on both sides; CUDA events on the launching stream; max over ranks."""
+    stream = torch.cuda.current_stream()
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    t_wall0 = time.time()
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    start.record(stream)
+    for _ in range(steps):
+        fn()
+    end.record(stream)
+    torch.cuda.synchronize()
+    t_wall1 = time.time()
+    ms = start.elapsed_time(end)
+    if world > 1:
+        t = torch.tensor([ms], device="cuda", dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        dist.barrier()
+        ms = float(t.item())
+    return ms, t_wall0, t_wall1
+
+
+def secondary_benchmarks(torch, ops, hbm_peak):
+    """Other hot-path kernels at their BASELINE configs (1 GPU)."""
+    out = []
+    dev = torch.device("cuda")
+    # first config: per-token int8 quant of bf16 [2048, 4096]
+    g = torch.Generator(device=dev).manual_seed(7)
+    x = torch.randn((2048, 4096), generator=g, device=dev)
+    mask = torch.rand((2048, 4096), generator=g, device=dev) < 1e-3
+    x = torch.where(mask, x * 50.0, x).to(torch.bfloat16)
+    nbytes = 2048 * 4096 * 2 + 2048 * 4096 + 2048 * 4
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
+    stream = torch.cuda.current_stream()
+    for _ in range(5):
+        ops.per_token_group_quant_int8(x, 4096, 1e-6)
+    times = []
+    for _ in range(20):
+        flush.zero_()
+        s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        s.record(stream)
+        ops.per_token_group_quant_int8(x, 4096, 1e-6)
+        e.record(stream)
+        torch.cuda.synchronize()
+        times.append(s.elapsed_time(e))
+    us = statistics.median(times) * 1e3
+    # back-to-back (amortised launch) number
+    torch.cuda.synchronize()
+    s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    s.record(stream)
+    for _ in range(200):
+        ops.per_token_group_quant_int8(x, 4096, 1e-6)
+    e.record(stream)
+    torch.cuda.synchronize()
+    us_b2b = s.elapsed_time(e) / 200 * 1e3
+    out.append({"workload": "per-token int8 quant bf16 [2048,4096] (BASELINE config 1)", "kernel": "group_quant_rowblock_kernel",
+                "us_per_call_cold_l2": round(us, 3), "us_per_call_back_to_back": round(us_b2b, 3),
+                "bytes_per_call": nbytes, "achieved_gbs_cold_l2": round(nbytes / us / 1e3, 1),
+                "frac_cold_l2": round(nbytes / us / 1e3 / hbm_peak, 4)})
+    del flush
+    return out
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=200)
+    ap.add_argument("--warmup", type=int, default=10)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--no-secondary", action="store_true")
+    ap.add_argument("--no-cpu", action="store_true")
+    ap.add_argument("--profile-only", action="store_true",
+                    help="run W warm-up + K steps of the headline kernel and exit (for ncu captures)")
+    args = ap.parse_args()
+    if args.warmup < 3:
+        args.warmup = 3
+
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    hbm_peak, _, peak_kind = peaks()
+    config = {"workload": "fused residual add + RMSNorm + per-token e4m3 quant, bf16 [8192, 8192] per GPU "
+                          "(BASELINE config 2)",
+              "rows_per_gpu": M_ROWS, "hidden": HIDDEN, "eps": EPS, "global_rows": M_ROWS * world,
+              "parallelism": f"row-sharded x{world} (no data-path collective)",
+              "l2": "inputs larger than L2 (268 MB read per step); no flush needed"}
+    per_step_bytes = c2_bytes(M_ROWS, HIDDEN)
+
+    if args.impl == "reference":
+        if rank != 0:
+            return
+        tbs, cores, sample = cpu_port_throughput()
+        ms = per_step_bytes / (tbs * 1e12) * 1e3
+        print(json.dumps({"impl": "reference", "metric": METRIC, "value": round(tbs, 6), "unit": "TB/s",
+                          "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
+                          "ms_per_step": round(ms, 3), "higher_is_better": True, "scaling": "weak",
+                          "vs_baseline": None, "dtype": "bf16->e4m3", "data": "synthetic (seeded N(0,1))",
+                          "config": config,
+                          "cpu_baseline": {"value": round(tbs, 6), "unit": "TB/s", "cores": cores, "kind": "port",
+                                           "sample": sample},
+                          "e2e": {"value": round(tbs, 6), "unit": "TB/s", "h2d_bytes_per_step": 0,
+                                  "d2h_bytes_per_step": 0}}))
+        return
+
+    import torch
+    dist = None
+    if world > 1:
+        import torch.distributed as dist
+        from datetime import timedelta
+        torch.cuda.set_device(local)
+        dist.init_process_group("nccl", timeout=timedelta(seconds=300), device_id=torch.device("cuda", local))
+    else:
+        torch.cuda.set_device(local)
+    from kernelverse_b200 import ops
+
+    dev = torch.device("cuda", local)
+    x, r, w = make_c2_inputs(torch, dev, seed=1000 + rank)
+    step = lambda: ops.add_rmsnorm_quant(x, r, w, EPS)   # noqa: E731
+
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize()
+    if args.profile_only:
+        for _ in range(args.steps):
+            step()
+        torch.cuda.synchronize()
+        return
+
+    phys = torch.cuda.get_device_properties(dev)
+    visible = os.environ.get("CUDA_VISIBLE_DEVICES")
+    smi_id = visible.split(",")[local].strip() if visible else str(local)   # index or UUID, as nvidia-smi --id takes
+    sampler = ClockSampler(smi_id).start()
+    ms, tw0, tw1 = time_region(torch, step, args.steps, dist, world)
+    clocks = sampler.summary(tw0, tw1, "timed region")
+    if clocks is None:   # timed region shorter than the sampling interval: soak the same kernel
+        t0 = time.time()
+        while time.time() - t0 < 1.0:
+            for _ in range(50):
+                step()
+            torch.cuda.synchronize()
+        clocks = sampler.summary(t0, time.time(), "1 s soak of the same kernel right after the timed region")
+    sampler.stop()
+
+    ms_step = ms / args.steps
+    value_tbs = world * per_step_bytes / (ms_step * 1e-3) / 1e12
+    achieved_gbs = per_step_bytes / (ms_step * 1e-3) / 1e9
+
+    # e2e through the public op with host buffers
+    e2e_steps = max(3, min(args.steps, 20))
+    hx, hr, hw = x.cpu().pin_memory(), r.cpu().pin_memory(), w.cpu().pin_memory()
+    h_rout = torch.empty(x.shape, dtype=torch.bfloat16).pin_memory()
+    h_codes = torch.empty(x.shape, dtype=torch.float8_e4m3fn).pin_memory()
+    h_scales = torch.empty((M_ROWS,), dtype=torch.float32).pin_memory()
+    dx, dr, dw = torch.empty_like(x), torch.empty_like(r), torch.empty_like(w)
+
+    def e2e_step():
+        dx.copy_(hx, non_blocking=True)
+        dr.copy_(hr, non_blocking=True)
+        dw.copy_(hw, non_blocking=True)
+        ro, codes, scales = ops.add_rmsnorm_quant(dx, dr, dw, EPS)
+        h_rout.copy_(ro, non_blocking=True)
+        h_codes.copy_(codes, non_blocking=True)
+        h_scales.copy_(scales, non_blocking=True)
+
+    for _ in range(2):
+        e2e_step()
+    e2e_ms, _, _ = time_region(torch, e2e_step, e2e_steps, dist, world)
+    e2e_tbs = world * per_step_bytes / (e2e_ms / e2e_steps * 1e-3) / 1e12
+    h2d = hx.numel() * 2 + hr.numel() * 2 + hw.numel() * 2
+    d2h = h_rout.numel() * 2 + h_codes.numel() + h_scales.numel() * 4
+
+    secondary = None
+    if world == 1 and not args.no_secondary:
+        secondary = secondary_benchmarks(torch, ops, hbm_peak)
+
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu:
+        tbs, cores, sample = cpu_port_throughput()
+        cpu = {"value": round(tbs, 6), "unit": "TB/s", "cores": cores, "kind": "port", "sample": sample}
+
+    if world > 1:
+        dist.barrier()
+    if rank == 0:
+        traffic = profile_traffic("add_rmsnorm_quant_c2.md")
+        line = {
+            "metric": METRIC, "value": round(value_tbs, 4), "unit": "TB/s", "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": round(ms_step, 5), "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "bf16->e4m3", "data": "synthetic (seeded N(0,1) on device)",
+            "config": config,
+            "roofline": {"bound": "hbm", "achieved": round(achieved_gbs, 1), "peak": hbm_peak, "unit": "GB/s",
+                         "frac": round(achieved_gbs / hbm_peak, 4), "traffic": traffic,
+                         "peak_source": f"{peak_kind} (MEASURED_PEAKS.json hbm_gbs)" if peak_kind == "measured"
+                         else "fallback 6.65 TB/s", "algorithmic_bytes_per_launch": per_step_bytes,
+                         "kernel": "add_rmsnorm_kernel<bf16,4,e4m3>"},
+            "e2e": {"value": round(e2e_tbs, 5), "unit": "TB/s", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
+                    "ms_per_step": round(e2e_ms / e2e_steps, 4), "steps": e2e_steps,
+                    "path": "kernelverse_b200.ops.add_rmsnorm_quant with pinned host buffers"},
+            "gpu_launches": args.steps,
+            "clocks": clocks,
+            "cpu_baseline": cpu,
+            "device": phys.name,
+        }
+        if secondary:
+            line["secondary"] = secondary
+        print(json.dumps(line))
+    if world > 1:
+        dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

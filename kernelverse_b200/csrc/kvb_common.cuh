@@ -1,0 +1,128 @@
+// Shared device/host helpers for the kvb sm_100a kernels.
+#pragma once
+
+#include <cuda_runtime.h>
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
+#include <cuda_fp8.h>
+#include <stdint.h>
+
+#include "../../include/kvb.h"
+
+namespace kvb {
+
+// ------------------------------------------------------------------ host-side error reporting
+// Sets the thread-local message returned by kvb_last_error() and returns `code`.
+int set_error(int code, const char* fmt, ...);
+// Checks the launch that was just issued (no synchronisation).
+int check_launch(const char* what);
+
+inline bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+inline bool aligned8(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 7u) == 0; }
+inline int dtype_size(int dt) {
+  switch (dt) {
+    case KVB_F32: case KVB_I32: return 4;
+    case KVB_F16: case KVB_BF16: return 2;
+    case KVB_I8: case KVB_U8: case KVB_E4M3: return 1;
+    case KVB_I64: return 8;
+    default: return 0;
+  }
+}
+inline bool is_float_dtype(int dt) { return dt == KVB_F32 || dt == KVB_F16 || dt == KVB_BF16; }
+inline cudaStream_t as_stream(void* s) { return reinterpret_cast<cudaStream_t>(s); }
+
+constexpr float kInt8Max = 127.0f;
+constexpr float kE4m3Max = 448.0f;
+// operators/quantization/dynamic_scaled_int8_quant/helpers.py:8 -- 1 / (448 * 512) as float32
+constexpr float kMinScalingFactor = 1.0f / (448.0f * 512.0f);
+
+// ------------------------------------------------------------------ element conversion
+template <typename T> struct Elem;
+template <> struct Elem<float> {
+  static __device__ __forceinline__ float to_f(float v) { return v; }
+  static __device__ __forceinline__ float from_f(float v) { return v; }
+};
+template <> struct Elem<__half> {
+  static __device__ __forceinline__ float to_f(__half v) { return __half2float(v); }
+  static __device__ __forceinline__ __half from_f(float v) { return __float2half_rn(v); }
+};
+template <> struct Elem<__nv_bfloat16> {
+  static __device__ __forceinline__ float to_f(__nv_bfloat16 v) { return __bfloat162float(v); }
+  static __device__ __forceinline__ __nv_bfloat16 from_f(float v) { return __float2bfloat16_rn(v); }
+};
+
+// Eight consecutive elements of T, moved with 128-bit (16-bit T) or 2x128-bit (float) accesses.
+template <typename T> struct Vec8 {
+  static constexpr int kBytes = 8 * sizeof(T);
+  static constexpr int kWords = kBytes / 16;   // uint4 words: 1 for 16-bit types, 2 for float
+  uint4 w[kWords];
+  __device__ __forceinline__ void load(const T* p) {
+    const uint4* s = reinterpret_cast<const uint4*>(p);
+#pragma unroll
+    for (int i = 0; i < kWords; ++i) w[i] = __ldg(s + i);
+  }
+  __device__ __forceinline__ void load_stream(const T* p) {   // read-once data: evict-first
+    const uint4* s = reinterpret_cast<const uint4*>(p);
+#pragma unroll
+    for (int i = 0; i < kWords; ++i) w[i] = __ldcs(s + i);
+  }
+  __device__ __forceinline__ void store(T* p) const {
+    uint4* d = reinterpret_cast<uint4*>(p);
+#pragma unroll
+    for (int i = 0; i < kWords; ++i) d[i] = w[i];
+  }
+  __device__ __forceinline__ float get(int i) const {
+    const T* e = reinterpret_cast<const T*>(w);
+    return Elem<T>::to_f(e[i]);
+  }
+  __device__ __forceinline__ void set(int i, float v) {
+    T* e = reinterpret_cast<T*>(w);
+    e[i] = Elem<T>::from_f(v);
+  }
+};
+
+// ------------------------------------------------------------------ reductions
+__device__ __forceinline__ float warp_max(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+  return v;
+}
+__device__ __forceinline__ float warp_sum(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  return v;
+}
+// Max over `width` consecutive lanes (width a power of two <= 32).
+__device__ __forceinline__ float group_max(float v, int width) {
+  for (int o = width >> 1; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+  return v;
+}
+
+// Block-wide reduction; `scratch` holds >= 32 floats.  All threads get the result.
+template <bool kMax>
+__device__ __forceinline__ float block_reduce(float v, float* scratch) {
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nwarps = (blockDim.x + 31) >> 5;
+  v = kMax ? warp_max(v) : warp_sum(v);
+  __syncthreads();               // scratch may still be read by a previous reduction
+  if (lane == 0) scratch[warp] = v;
+  __syncthreads();
+  float r = lane < nwarps ? scratch[lane] : (kMax ? 0.0f : 0.0f);
+  r = kMax ? warp_max(r) : warp_sum(r);
+  return r;
+}
+
+// ------------------------------------------------------------------ quantisation primitives
+// int8 code: round-half-even of an IEEE float32 quotient, clamped to +-127.
+__device__ __forceinline__ int8_t quant_int8(float x, float scale) {
+  float q = rintf(__fdiv_rn(x, scale));
+  q = fminf(fmaxf(q, -kInt8Max), kInt8Max);
+  return static_cast<int8_t>(__float2int_rn(q));
+}
+// e4m3fn code of clamp(x / scale, +-448): hardware RNE conversion (cvt.rn.satfinite.e4m3x2.f32).
+__device__ __forceinline__ uint16_t quant_e4m3x2(float a, float b, float scale) {
+  float qa = fminf(fmaxf(__fdiv_rn(a, scale), -kE4m3Max), kE4m3Max);
+  float qb = fminf(fmaxf(__fdiv_rn(b, scale), -kE4m3Max), kE4m3Max);
+  return static_cast<uint16_t>(__nv_cvt_float2_to_fp8x2(make_float2(qa, qb), __NV_SATFINITE, __NV_E4M3));
+}
+
+}  // namespace kvb

@@ -1,0 +1,258 @@
+// Dynamic int8 quantisation kernels: per-tensor and per-(token, group).
+//
+// Memory-bound: every kernel reads x once from HBM (the per-tensor form reads it
+// twice, the second pass normally from L2) and writes 1 byte per element plus
+// one float32 scale per group.  Loads are 128-bit, group amax reductions use
+// warp shuffles (groups of <= 256 elements live inside one warp) or one block
+// reduction per group (larger groups, e.g. whole tokens), and the quotient is
+// an IEEE division so the codes are bit-identical to the reference's
+// round(x / scale).
+#include "kvb_common.cuh"
+
+namespace kvb {
+namespace {
+
+// Packs eight int8 codes of one Vec8 into a 64-bit word (little-endian order).
+template <typename T>
+__device__ __forceinline__ uint2 quant8(const Vec8<T>& v, float scale) {
+  uint32_t lo = 0, hi = 0;
+#pragma unroll
+  for (int i = 0; i < 4; ++i) lo |= (uint32_t)(uint8_t)quant_int8(v.get(i), scale) << (8 * i);
+#pragma unroll
+  for (int i = 0; i < 4; ++i) hi |= (uint32_t)(uint8_t)quant_int8(v.get(4 + i), scale) << (8 * i);
+  return make_uint2(lo, hi);
+}
+
+template <typename T>
+__device__ __forceinline__ float vec_amax(const Vec8<T>& v) {
+  float m = 0.0f;
+#pragma unroll
+  for (int i = 0; i < 8; ++i) m = fmaxf(m, fabsf(v.get(i)));
+  return m;
+}
+
+// ---------------------------------------------------------------- per-tensor
+// Pass 1: amax(|x|) -> *amax_bits (float bits; non-negative floats order like uint32).
+template <typename T>
+__global__ void __launch_bounds__(256) tensor_amax_kernel(const T* __restrict__ x, int64_t numel, int64_t nvec,
+                                                          unsigned int* __restrict__ amax_bits) {
+  __shared__ float scratch[32];
+  float m = 0.0f;
+  const int64_t stride = (int64_t)gridDim.x * blockDim.x;
+  for (int64_t v = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; v < nvec; v += stride) {
+    Vec8<T> a;
+    a.load(x + v * 8);
+    m = fmaxf(m, vec_amax(a));
+  }
+  for (int64_t i = nvec * 8 + (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < numel; i += stride)
+    m = fmaxf(m, fabsf(Elem<T>::to_f(x[i])));
+  m = block_reduce<true>(m, scratch);
+  if (threadIdx.x == 0) atomicMax(amax_bits, __float_as_uint(m));
+}
+
+// Pass 2: scale = max(float(T(amax / 127)), MIN_SCALING_FACTOR); q = round(clamp(x / scale)).
+template <typename T>
+__global__ void __launch_bounds__(256) tensor_quant_kernel(const T* __restrict__ x, int64_t numel, int64_t nvec,
+                                                           const unsigned int* __restrict__ amax_bits,
+                                                           int8_t* __restrict__ q, float* __restrict__ scale_out,
+                                                           int32_t* __restrict__ azp_out) {
+  const float amax = __uint_as_float(*amax_bits);
+  // amax / 127 is evaluated in float32 and rounded to the input dtype, as the reference's
+  // input-dtype arithmetic does (dynamic_scaled_int8_quant.py:22).
+  const float s_in = Elem<T>::to_f(Elem<T>::from_f(__fdiv_rn(amax, kInt8Max)));
+  const float scale = fmaxf(s_in, kMinScalingFactor);
+  if (blockIdx.x == 0 && threadIdx.x == 0) {
+    *scale_out = scale;
+    if (azp_out) *azp_out = 0;
+  }
+  const int64_t stride = (int64_t)gridDim.x * blockDim.x;
+  for (int64_t v = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; v < nvec; v += stride) {
+    Vec8<T> a;
+    a.load(x + v * 8);
+    reinterpret_cast<uint2*>(q)[v] = quant8(a, scale);
+  }
+  for (int64_t i = nvec * 8 + (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < numel; i += stride)
+    q[i] = quant_int8(Elem<T>::to_f(x[i]), scale);
+}
+
+// ---------------------------------------------------------------- per-group, small groups
+// One 8-element vector per thread; a group of G = 8*L elements spans L consecutive lanes
+// (L a power of two <= 32), so its amax is an L-lane shuffle reduction.
+template <typename T>
+__global__ void __launch_bounds__(256) group_quant_subwarp_kernel(const T* __restrict__ x, int64_t nvec, int lanes,
+                                                                  float eps, int8_t* __restrict__ q,
+                                                                  float* __restrict__ scales) {
+  const int64_t stride = (int64_t)gridDim.x * blockDim.x;
+  // The loop bound is warp-uniform so every lane joins each shuffle.
+  for (int64_t base = (int64_t)blockIdx.x * blockDim.x + (threadIdx.x & ~31); base < nvec; base += stride) {
+    const int64_t v = base + (threadIdx.x & 31);
+    const bool live = v < nvec;
+    Vec8<T> a;
+    float m = 0.0f;
+    if (live) {
+      a.load_stream(x + v * 8);
+      m = vec_amax(a);
+    }
+    m = group_max(m, lanes);
+    const float scale = fmaxf(__fdiv_rn(m, kInt8Max), eps);
+    if (live) {
+      reinterpret_cast<uint2*>(q)[v] = quant8(a, scale);
+      if ((v & (lanes - 1)) == 0) scales[v / lanes] = scale;
+    }
+  }
+}
+
+// ---------------------------------------------------------------- per-group, large groups
+// One CTA per group (e.g. one token row); the group stays in registers between the
+// amax reduction and the quantisation, so x is read from HBM exactly once.
+template <typename T, int VPT>
+__global__ void __launch_bounds__(1024) group_quant_rowblock_kernel(const T* __restrict__ x, int64_t group_vecs, float eps,
+                                            int8_t* __restrict__ q, float* __restrict__ scales) {
+  __shared__ float scratch[32];
+  const int64_t g = blockIdx.x;
+  const T* xg = x + g * group_vecs * 8;
+  Vec8<T> a[VPT];
+  float m = 0.0f;
+#pragma unroll
+  for (int j = 0; j < VPT; ++j) {
+    const int64_t v = threadIdx.x + (int64_t)j * blockDim.x;
+    if (v < group_vecs) {
+      a[j].load_stream(xg + v * 8);
+      m = fmaxf(m, vec_amax(a[j]));
+    }
+  }
+  m = block_reduce<true>(m, scratch);
+  const float scale = fmaxf(__fdiv_rn(m, kInt8Max), eps);
+  uint2* qg = reinterpret_cast<uint2*>(q + g * group_vecs * 8);
+#pragma unroll
+  for (int j = 0; j < VPT; ++j) {
+    const int64_t v = threadIdx.x + (int64_t)j * blockDim.x;
+    if (v < group_vecs) qg[v] = quant8(a[j], scale);
+  }
+  if (threadIdx.x == 0) scales[g] = scale;
+}
+
+// ---------------------------------------------------------------- any shape / alignment
+// One warp per group, two passes over global memory (correctness path for odd sizes).
+template <typename T>
+__global__ void __launch_bounds__(256) group_quant_scalar_kernel(const T* __restrict__ x, int64_t ngroups,
+                                                                 int64_t group_size, float eps,
+                                                                 int8_t* __restrict__ q, float* __restrict__ scales) {
+  const int64_t warps = (int64_t)gridDim.x * (blockDim.x >> 5);
+  const int lane = threadIdx.x & 31;
+  for (int64_t g = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5); g < ngroups; g += warps) {
+    const T* xg = x + g * group_size;
+    float m = 0.0f;
+    for (int64_t i = lane; i < group_size; i += 32) m = fmaxf(m, fabsf(Elem<T>::to_f(xg[i])));
+    m = warp_max(m);
+    const float scale = fmaxf(__fdiv_rn(m, kInt8Max), eps);
+    for (int64_t i = lane; i < group_size; i += 32) q[g * group_size + i] = quant_int8(Elem<T>::to_f(xg[i]), scale);
+    if (lane == 0) scales[g] = scale;
+  }
+}
+
+int sm_count() {
+  static int n = 0;
+  if (n == 0) {
+    int dev = 0;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
+    if (n <= 0) n = 148;
+  }
+  return n;
+}
+
+template <typename T>
+int launch_tensor_quant(const void* xv, int64_t numel, int8_t* q, float* scale, int32_t* azp,
+                        unsigned int* amax, cudaStream_t st) {
+  const T* x = static_cast<const T*>(xv);
+  const bool vec = aligned16(x) && aligned8(q);
+  const int64_t nvec = vec ? numel / 8 : 0;
+  const int64_t work = nvec > 0 ? nvec : numel;
+  int blocks = (int)std::min<int64_t>((work + 255) / 256, (int64_t)sm_count() * 8);
+  if (blocks < 1) blocks = 1;
+  cudaError_t e = cudaMemsetAsync(amax, 0, sizeof(unsigned int), st);
+  if (e != cudaSuccess) return set_error(KVB_E_LAUNCH, "memset amax: %s", cudaGetErrorString(e));
+  tensor_amax_kernel<T><<<blocks, 256, 0, st>>>(x, numel, nvec, amax);
+  int rc = check_launch("tensor_amax_kernel");
+  if (rc) return rc;
+  tensor_quant_kernel<T><<<blocks, 256, 0, st>>>(x, numel, nvec, amax, q, scale, azp);
+  return check_launch("tensor_quant_kernel");
+}
+
+template <typename T, int VPT>
+int launch_rowblock(const T* x, int64_t ngroups, int64_t gvec, float eps, int8_t* q, float* scales, cudaStream_t st) {
+  int threads = (int)((gvec + VPT - 1) / VPT);
+  threads = ((threads + 31) / 32) * 32;
+  if (threads > 1024) return set_error(KVB_E_SHAPE, "group too large for the register-resident path");
+  group_quant_rowblock_kernel<T, VPT><<<(unsigned)ngroups, threads, 0, st>>>(x, gvec, eps, q, scales);
+  return check_launch("group_quant_rowblock_kernel");
+}
+
+template <typename T>
+int launch_group_quant(const void* xv, int64_t tokens, int64_t hidden, int64_t G, float eps, int8_t* q,
+                       float* scales, cudaStream_t st) {
+  const T* x = static_cast<const T*>(xv);
+  const int64_t ngroups = tokens * (hidden / G);
+  if (ngroups == 0) return KVB_OK;
+  const bool vec = (G % 8 == 0) && aligned16(x) && aligned8(q);
+  if (vec) {
+    const int64_t lanes = G / 8;
+    if (lanes <= 32 && (lanes & (lanes - 1)) == 0) {
+      const int64_t nvec = tokens * hidden / 8;
+      int blocks = (int)std::min<int64_t>((nvec + 255) / 256, (int64_t)sm_count() * 8);
+      group_quant_subwarp_kernel<T><<<blocks, 256, 0, st>>>(x, nvec, (int)lanes, eps, q, scales);
+      return check_launch("group_quant_subwarp_kernel");
+    }
+    if (ngroups <= 0x7fffffff) {
+      if (lanes <= 4 * 1024) return launch_rowblock<T, 4>(x, ngroups, lanes, eps, q, scales, st);
+      if (lanes <= 8 * 1024) return launch_rowblock<T, 8>(x, ngroups, lanes, eps, q, scales, st);
+    }
+  }
+  const int64_t warps_needed = ngroups;
+  int blocks = (int)std::min<int64_t>((warps_needed + 7) / 8, (int64_t)sm_count() * 16);
+  group_quant_scalar_kernel<T><<<blocks, 256, 0, st>>>(x, ngroups, G, eps, q, scales);
+  return check_launch("group_quant_scalar_kernel");
+}
+
+}  // namespace
+}  // namespace kvb
+
+using namespace kvb;
+
+extern "C" size_t kvb_dynamic_scaled_int8_quant_workspace_size(void) { return 256; }
+
+extern "C" int kvb_dynamic_scaled_int8_quant(const void* x, int x_dtype, int64_t numel, int8_t* q, float* scale,
+                                             int32_t* azp, void* workspace, size_t workspace_bytes, void* stream) {
+  if (numel < 0) return set_error(KVB_E_ARG, "dynamic_scaled_int8_quant: numel < 0");
+  if (!x || !q || !scale) return set_error(KVB_E_ARG, "dynamic_scaled_int8_quant: null pointer");
+  if (!workspace || workspace_bytes < sizeof(unsigned int))
+    return set_error(KVB_E_WORKSPACE, "dynamic_scaled_int8_quant: workspace of >= 4 bytes required");
+  if (((uintptr_t)workspace & 3u) != 0) return set_error(KVB_E_ALIGN, "dynamic_scaled_int8_quant: workspace not 4-byte aligned");
+  unsigned int* amax = static_cast<unsigned int*>(workspace);
+  cudaStream_t st = as_stream(stream);
+  switch (x_dtype) {
+    case KVB_F32: return launch_tensor_quant<float>(x, numel, q, scale, azp, amax, st);
+    case KVB_F16: return launch_tensor_quant<__half>(x, numel, q, scale, azp, amax, st);
+    case KVB_BF16: return launch_tensor_quant<__nv_bfloat16>(x, numel, q, scale, azp, amax, st);
+    default: return set_error(KVB_E_DTYPE, "dynamic_scaled_int8_quant: x dtype %d unsupported", x_dtype);
+  }
+}
+
+extern "C" int kvb_per_token_group_quant_int8(const void* x, int x_dtype, int64_t tokens, int64_t hidden,
+                                              int64_t group_size, float eps, int8_t* q, float* scales, void* stream) {
+  if (tokens < 0 || hidden < 0) return set_error(KVB_E_ARG, "per_token_group_quant_int8: negative size");
+  if (group_size <= 0 || (hidden % group_size) != 0)
+    return set_error(KVB_E_SHAPE, "per_token_group_quant_int8: hidden (%lld) must be a multiple of group_size (%lld)",
+                     (long long)hidden, (long long)group_size);
+  if (!(eps > 0.0f)) return set_error(KVB_E_ARG, "per_token_group_quant_int8: eps must be positive");
+  if (tokens * hidden == 0) return KVB_OK;
+  if (!x || !q || !scales) return set_error(KVB_E_ARG, "per_token_group_quant_int8: null pointer");
+  cudaStream_t st = as_stream(stream);
+  switch (x_dtype) {
+    case KVB_F32: return launch_group_quant<float>(x, tokens, hidden, group_size, eps, q, scales, st);
+    case KVB_F16: return launch_group_quant<__half>(x, tokens, hidden, group_size, eps, q, scales, st);
+    case KVB_BF16: return launch_group_quant<__nv_bfloat16>(x, tokens, hidden, group_size, eps, q, scales, st);
+    default: return set_error(KVB_E_DTYPE, "per_token_group_quant_int8: x dtype %d unsupported", x_dtype);
+  }
+}

@@ -1,0 +1,239 @@
+// Residual add + RMSNorm, optionally fused with dynamic per-row int8 / e4m3 quantisation.
+//
+// One CTA owns one row.  The row's x and residual are read once with 128-bit
+// loads, the float32 sum s = x + r stays in registers through both block
+// reductions (sum of squares, then amax of the normalised row), and the
+// outputs (updated residual, codes, scale -- or the normalised row itself) are
+// written once: the kernel moves exactly the algorithmic bytes.
+//
+// Arithmetic order follows operators/normalization/add_rmsnorm/add_rmsnorm.py:30-35
+// in its float32 "correctness" mode: s = x + r; var = sum(s^2) / H;
+// rinv = 1 / sqrt(var + eps); y = (s * rinv) * w.  Every quotient is IEEE (no
+// fast-math), so only the float32 summation order of sum(s^2) differs from the
+// reference.
+#include "kvb_common.cuh"
+
+namespace kvb {
+namespace {
+
+enum Mode { kOutY = 0, kQuantE4m3 = 1, kQuantInt8 = 2 };
+
+template <typename T, int VPT, int MODE>
+__global__ void __launch_bounds__(256) add_rmsnorm_kernel(const T* __restrict__ x, const T* __restrict__ res, const T* __restrict__ w,
+                                   int64_t nvec, float hidden_f, float eps, T* __restrict__ out,
+                                   uint8_t* __restrict__ codes, float* __restrict__ scales) {
+  __shared__ float scratch[32];
+  const int64_t row = blockIdx.x;
+  const T* xr = x + row * nvec * 8;
+  const T* rr = res + row * nvec * 8;
+  float s[VPT][8];
+  float ss = 0.0f;
+#pragma unroll
+  for (int j = 0; j < VPT; ++j) {
+    const int64_t v = threadIdx.x + (int64_t)j * blockDim.x;
+    if (v < nvec) {
+      Vec8<T> a, b;
+      a.load_stream(xr + v * 8);
+      b.load_stream(rr + v * 8);
+#pragma unroll
+      for (int k = 0; k < 8; ++k) {
+        s[j][k] = a.get(k) + b.get(k);
+        ss = fmaf(s[j][k], s[j][k], ss);
+      }
+    } else {
+#pragma unroll
+      for (int k = 0; k < 8; ++k) s[j][k] = 0.0f;
+    }
+  }
+  ss = block_reduce<false>(ss, scratch);
+  const float rinv = 1.0f / sqrtf(__fdiv_rn(ss, hidden_f) + eps);
+
+  if (MODE == kOutY) {
+    T* orow = out + row * nvec * 8;
+#pragma unroll
+    for (int j = 0; j < VPT; ++j) {
+      const int64_t v = threadIdx.x + (int64_t)j * blockDim.x;
+      if (v < nvec) {
+        Vec8<T> wv, o;
+        wv.load(w + v * 8);
+#pragma unroll
+        for (int k = 0; k < 8; ++k) o.set(k, __fmul_rn(__fmul_rn(s[j][k], rinv), wv.get(k)));
+        o.store(orow + v * 8);
+      }
+    }
+    return;
+  }
+
+  // Fused quantisation: write the updated residual, turn s into y in place, reduce amax.
+  float amax = 0.0f;
+#pragma unroll
+  for (int j = 0; j < VPT; ++j) {
+    const int64_t v = threadIdx.x + (int64_t)j * blockDim.x;
+    if (v < nvec) {
+      Vec8<T> wv;
+      wv.load(w + v * 8);
+      if (out) {
+        Vec8<T> o;
+#pragma unroll
+        for (int k = 0; k < 8; ++k) o.set(k, s[j][k]);
+        o.store(out + row * nvec * 8 + v * 8);
+      }
+#pragma unroll
+      for (int k = 0; k < 8; ++k) {
+        s[j][k] = __fmul_rn(__fmul_rn(s[j][k], rinv), wv.get(k));
+        amax = fmaxf(amax, fabsf(s[j][k]));
+      }
+    }
+  }
+  amax = block_reduce<true>(amax, scratch);
+  const float qmax = MODE == kQuantE4m3 ? kE4m3Max : kInt8Max;
+  const float scale = fmaxf(__fdiv_rn(amax, qmax), kMinScalingFactor);
+  uint2* crow = reinterpret_cast<uint2*>(codes + row * nvec * 8);
+#pragma unroll
+  for (int j = 0; j < VPT; ++j) {
+    const int64_t v = threadIdx.x + (int64_t)j * blockDim.x;
+    if (v < nvec) {
+      uint32_t lo, hi;
+      if (MODE == kQuantE4m3) {
+        lo = quant_e4m3x2(s[j][0], s[j][1], scale) | ((uint32_t)quant_e4m3x2(s[j][2], s[j][3], scale) << 16);
+        hi = quant_e4m3x2(s[j][4], s[j][5], scale) | ((uint32_t)quant_e4m3x2(s[j][6], s[j][7], scale) << 16);
+      } else {
+        lo = hi = 0;
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+          lo |= (uint32_t)(uint8_t)quant_int8(s[j][k], scale) << (8 * k);
+          hi |= (uint32_t)(uint8_t)quant_int8(s[j][4 + k], scale) << (8 * k);
+        }
+      }
+      __stcs(crow + v, make_uint2(lo, hi));
+    }
+  }
+  if (threadIdx.x == 0) scales[row] = scale;
+}
+
+// Any hidden size / alignment: three passes over the row through L1/L2 (correctness path).
+template <typename T, int MODE>
+__global__ void __launch_bounds__(256) add_rmsnorm_scalar_kernel(const T* __restrict__ x, const T* __restrict__ res,
+                                                                 const T* __restrict__ w, int64_t hidden, float eps,
+                                                                 T* __restrict__ out, uint8_t* __restrict__ codes,
+                                                                 float* __restrict__ scales) {
+  __shared__ float scratch[32];
+  const int64_t base = (int64_t)blockIdx.x * hidden;
+  float ss = 0.0f;
+  for (int64_t i = threadIdx.x; i < hidden; i += blockDim.x) {
+    const float s = Elem<T>::to_f(x[base + i]) + Elem<T>::to_f(res[base + i]);
+    ss = fmaf(s, s, ss);
+  }
+  ss = block_reduce<false>(ss, scratch);
+  const float rinv = 1.0f / sqrtf(__fdiv_rn(ss, (float)hidden) + eps);
+  float amax = 0.0f;
+  for (int64_t i = threadIdx.x; i < hidden; i += blockDim.x) {
+    const float s = Elem<T>::to_f(x[base + i]) + Elem<T>::to_f(res[base + i]);
+    const float y = __fmul_rn(__fmul_rn(s, rinv), Elem<T>::to_f(w[i]));
+    if (MODE == kOutY) {
+      out[base + i] = Elem<T>::from_f(y);
+    } else {
+      amax = fmaxf(amax, fabsf(y));
+    }
+  }
+  if (MODE == kOutY) return;
+  amax = block_reduce<true>(amax, scratch);
+  const float qmax = MODE == kQuantE4m3 ? kE4m3Max : kInt8Max;
+  const float scale = fmaxf(__fdiv_rn(amax, qmax), kMinScalingFactor);
+  __syncthreads();   // every thread has re-read x/res before the residual may be overwritten in place
+  for (int64_t i = threadIdx.x; i < hidden; i += blockDim.x) {
+    const float s = Elem<T>::to_f(x[base + i]) + Elem<T>::to_f(res[base + i]);
+    const float y = __fmul_rn(__fmul_rn(s, rinv), Elem<T>::to_f(w[i]));
+    if (MODE == kQuantE4m3) {
+      codes[base + i] = (uint8_t)(quant_e4m3x2(y, 0.0f, scale) & 0xff);
+    } else {
+      codes[base + i] = (uint8_t)quant_int8(y, scale);
+    }
+  }
+  if (out) {
+    __syncthreads();
+    for (int64_t i = threadIdx.x; i < hidden; i += blockDim.x)
+      out[base + i] = Elem<T>::from_f(Elem<T>::to_f(x[base + i]) + Elem<T>::to_f(res[base + i]));
+  }
+  if (threadIdx.x == 0) scales[blockIdx.x] = scale;
+}
+
+template <typename T, int MODE, int VPT>
+int launch_vec(const T* x, const T* r, const T* w, int64_t rows, int64_t nvec, float eps, T* out, uint8_t* codes,
+               float* scales, cudaStream_t st) {
+  int threads = (int)((nvec + VPT - 1) / VPT);
+  threads = ((threads + 31) / 32) * 32;
+  add_rmsnorm_kernel<T, VPT, MODE><<<(unsigned)rows, threads, 0, st>>>(x, r, w, nvec, (float)(nvec * 8), eps, out,
+                                                                         codes, scales);
+  return check_launch("add_rmsnorm_kernel");
+}
+
+template <typename T, int MODE>
+int launch(const void* xv, const void* rv, const void* wv, int64_t rows, int64_t hidden, float eps, void* outv,
+           void* codesv, float* scales, cudaStream_t st) {
+  const T* x = static_cast<const T*>(xv);
+  const T* r = static_cast<const T*>(rv);
+  const T* w = static_cast<const T*>(wv);
+  T* out = static_cast<T*>(outv);
+  uint8_t* codes = static_cast<uint8_t*>(codesv);
+  if (rows == 0 || hidden == 0) return KVB_OK;
+  if (rows > 0x7fffffffLL) return set_error(KVB_E_SHAPE, "add_rmsnorm: too many rows");
+  // The fused form may write the updated residual over `residual` in place: the vector
+  // kernel reads its row fully into registers before writing, so aliasing is safe there.
+  const bool vec = hidden % 8 == 0 && aligned16(x) && aligned16(r) && aligned16(w) && (!out || aligned16(out)) &&
+                   (!codes || aligned8(codes)) && hidden / 8 <= 16 * 256;
+  if (vec) {
+    const int64_t nvec = hidden / 8;
+    if (nvec <= 256) return launch_vec<T, MODE, 1>(x, r, w, rows, nvec, eps, out, codes, scales, st);
+    if (nvec <= 512) return launch_vec<T, MODE, 2>(x, r, w, rows, nvec, eps, out, codes, scales, st);
+    if (nvec <= 1024) return launch_vec<T, MODE, 4>(x, r, w, rows, nvec, eps, out, codes, scales, st);
+    if (nvec <= 2048) return launch_vec<T, MODE, 8>(x, r, w, rows, nvec, eps, out, codes, scales, st);
+    return launch_vec<T, MODE, 16>(x, r, w, rows, nvec, eps, out, codes, scales, st);
+  }
+  add_rmsnorm_scalar_kernel<T, MODE><<<(unsigned)rows, 256, 0, st>>>(x, r, w, hidden, eps, out, codes, scales);
+  return check_launch("add_rmsnorm_scalar_kernel");
+}
+
+}  // namespace
+}  // namespace kvb
+
+using namespace kvb;
+
+extern "C" int kvb_add_rmsnorm(const void* x, const void* residual, const void* weight, int dtype, int64_t rows,
+                               int64_t hidden, float eps, void* out, void* stream) {
+  if (rows < 0 || hidden < 0) return set_error(KVB_E_ARG, "add_rmsnorm: negative size");
+  if (rows * hidden == 0) return KVB_OK;
+  if (!x || !residual || !weight || !out) return set_error(KVB_E_ARG, "add_rmsnorm: null pointer");
+  if (!(eps > 0.0f)) return set_error(KVB_E_ARG, "add_rmsnorm: eps must be positive");
+  cudaStream_t st = as_stream(stream);
+  switch (dtype) {
+    case KVB_F32: return launch<float, kOutY>(x, residual, weight, rows, hidden, eps, out, nullptr, nullptr, st);
+    case KVB_F16: return launch<__half, kOutY>(x, residual, weight, rows, hidden, eps, out, nullptr, nullptr, st);
+    case KVB_BF16: return launch<__nv_bfloat16, kOutY>(x, residual, weight, rows, hidden, eps, out, nullptr, nullptr, st);
+    default: return set_error(KVB_E_DTYPE, "add_rmsnorm: dtype %d unsupported", dtype);
+  }
+}
+
+extern "C" int kvb_add_rmsnorm_quant(const void* x, const void* residual, const void* weight, int dtype, int64_t rows,
+                                     int64_t hidden, float eps, void* residual_out, void* codes, int code_dtype,
+                                     float* scales, void* stream) {
+  if (rows < 0 || hidden < 0) return set_error(KVB_E_ARG, "add_rmsnorm_quant: negative size");
+  if (rows * hidden == 0) return KVB_OK;
+  if (!x || !residual || !weight || !codes || !scales) return set_error(KVB_E_ARG, "add_rmsnorm_quant: null pointer");
+  if (!(eps > 0.0f)) return set_error(KVB_E_ARG, "add_rmsnorm_quant: eps must be positive");
+  if (residual_out == x) return set_error(KVB_E_ARG, "add_rmsnorm_quant: residual_out may alias residual, not x");
+  cudaStream_t st = as_stream(stream);
+#define KVB_RMS_CASE(T)                                                                                        \
+  if (code_dtype == KVB_E4M3)                                                                                  \
+    return launch<T, kQuantE4m3>(x, residual, weight, rows, hidden, eps, residual_out, codes, scales, st);    \
+  if (code_dtype == KVB_I8)                                                                                    \
+    return launch<T, kQuantInt8>(x, residual, weight, rows, hidden, eps, residual_out, codes, scales, st);    \
+  return set_error(KVB_E_DTYPE, "add_rmsnorm_quant: code dtype %d unsupported", code_dtype);
+  switch (dtype) {
+    case KVB_F32: { KVB_RMS_CASE(float) }
+    case KVB_F16: { KVB_RMS_CASE(__half) }
+    case KVB_BF16: { KVB_RMS_CASE(__nv_bfloat16) }
+    default: return set_error(KVB_E_DTYPE, "add_rmsnorm_quant: dtype %d unsupported", dtype);
+  }
+#undef KVB_RMS_CASE
+}

@@ -1,0 +1,63 @@
+"""CPU checks of the C ABI: libkvb.so loads, exports every symbol include/kvb.h declares,
+the ctypes table mirrors the header, and argument validation fails cleanly without a GPU."""
+import ctypes
+import re
+from pathlib import Path
+
+import pytest
+
+from kernelverse_b200 import _lib
+
+HEADER = Path(__file__).resolve().parents[1] / "include" / "kvb.h"
+
+
+def header_functions():
+    text = HEADER.read_text()
+    return re.findall(r"KVB_API\s+[\w\s\*]+?\b(kvb_\w+)\s*\(", text)
+
+
+def test_header_declares_functions():
+    names = header_functions()
+    assert "kvb_last_error" in names and len(names) >= 6
+    assert len(names) == len(set(names))
+
+
+def test_library_exports_every_header_symbol():
+    lib = _lib.lib()
+    for name in header_functions():
+        assert hasattr(lib, name), name
+
+
+def test_ctypes_table_matches_header():
+    assert set(_lib.SIGNATURES) == set(header_functions())
+    text = re.sub(r"/\*.*?\*/", "", HEADER.read_text(), flags=re.S)
+    for name, (_, argtypes) in _lib.SIGNATURES.items():
+        m = re.search(rf"\b{name}\s*\(([^)]*)\)", text)
+        params = [p for p in m.group(1).split(",") if p.strip() and p.strip() != "void"]
+        assert len(params) == len(argtypes), name
+
+
+def test_abi_version_and_error_string():
+    lib = _lib.lib()
+    assert lib.kvb_abi_version() >= 1
+    assert isinstance(lib.kvb_last_error(), bytes)
+
+
+def test_validation_errors_need_no_gpu():
+    lib = _lib.lib()
+    # hidden not divisible by group: rejected before any CUDA call
+    rc = lib.kvb_per_token_group_quant_int8(None, _lib.BF16, 4, 100, 64, 1e-6, None, None, None)
+    assert rc == 2 and b"multiple of group_size" in lib.kvb_last_error()
+    rc = lib.kvb_dynamic_scaled_int8_quant(None, _lib.F32, -1, None, None, None, None, 0, None)
+    assert rc == 1
+    rc = lib.kvb_add_rmsnorm_quant(None, None, None, _lib.BF16, 2, 8, 1e-6, None, None, _lib.E4M3, None, None)
+    assert rc == 1
+    with pytest.raises(_lib.KvbError):
+        _lib.call("kvb_per_token_group_quant_int8", None, _lib.F32, 1, 10, 3, 1e-6, None, None, None)
+
+
+def test_ops_reject_cpu_tensors():
+    import torch
+    from kernelverse_b200 import ops
+    with pytest.raises(ValueError, match="CUDA tensors only"):
+        ops.per_token_group_quant_int8(torch.zeros(2, 8), 8, 1e-6)
