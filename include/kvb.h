@@ -56,6 +56,17 @@ KVB_API const char* kvb_last_error(void);
 /* ABI version: bumped on any signature change. */
 KVB_API int kvb_abi_version(void);
 
+/*
+ * Diagnostics (no reference counterpart).  kvb_device_status synchronises the
+ * current device and returns the OR of the library's device status words:
+ * bit 0 = a bounded device-side wait gave up (its kernel drained and exited
+ * early; outputs of that launch are invalid).  reset != 0 clears the words.
+ * Returns 0x80000000 if the device itself reports an error.
+ */
+KVB_API unsigned int kvb_device_status(int reset);
+/* out[i] = a[i] / b[i] through the kernels' FMA-corrected division (test hook). */
+KVB_API int kvb_selftest_div_rn(const float* a, const float* b, float* out, int64_t n, void* stream);
+
 /* ---------------------------------------------------------------- quantisation */
 
 /* Bytes of workspace kvb_dynamic_scaled_int8_quant needs (a 256-byte-aligned block). */

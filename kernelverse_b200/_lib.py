@@ -22,6 +22,8 @@ _P, _I, _I64, _F, _SZ = ctypes.c_void_p, ctypes.c_int, ctypes.c_int64, ctypes.c_
 SIGNATURES = {
     "kvb_last_error": (ctypes.c_char_p, []),
     "kvb_abi_version": (_I, []),
+    "kvb_device_status": (ctypes.c_uint, [_I]),
+    "kvb_selftest_div_rn": (_I, [_P, _P, _P, _I64, _P]),
     "kvb_dynamic_scaled_int8_quant_workspace_size": (_SZ, []),
     "kvb_dynamic_scaled_int8_quant": (_I, [_P, _I, _I64, _P, _P, _P, _P, _SZ, _P]),
     "kvb_per_token_group_quant_int8": (_I, [_P, _I, _I64, _I64, _I64, _F, _P, _P, _P]),

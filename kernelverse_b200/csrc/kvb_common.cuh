@@ -112,16 +112,46 @@ __device__ __forceinline__ float block_reduce(float v, float* scratch) {
 }
 
 // ------------------------------------------------------------------ quantisation primitives
-// int8 code: round-half-even of an IEEE float32 quotient, clamped to +-127.
-__device__ __forceinline__ int8_t quant_int8(float x, float scale) {
-  float q = rintf(__fdiv_rn(x, scale));
+// Correctly rounded a / b from a precomputed y = RN(1/b), by Markstein's method
+// (P. Markstein, "IA-64 and Elementary Functions", 2000, Thm. 8.10): with y the
+// correctly rounded reciprocal and q0 = RN(a*y) within an ulp of a/b, the remainder
+// r = a - b*q0 is exact in one FMA and q1 = RN(q0 + r*y) is the round-to-nearest
+// quotient.  The theorem assumes no underflow or overflow in the intermediate
+// steps, so a quotient takes the IEEE division instead when |a| < 2^-96 (zero
+// included, which keeps the quotient's sign) or when b lies outside
+// [2^-120, 2^120] (then every element of the group does).  A divisor is set up
+// once per quantisation group and reused for every element.
+// tests/test_gpu_numerics.py checks div_rn against CUDA's __fdiv_rn bit for bit.
+struct Divisor {
+  float b, y, thresh;
+};
+__device__ __forceinline__ Divisor make_divisor(float b) {
+  Divisor d;
+  d.b = b;
+  d.y = __frcp_rn(b);
+  d.thresh = (b >= 0x1p-120f && b <= 0x1p120f) ? 0x1p-96f : __int_as_float(0x7f800000);
+  return d;
+}
+__device__ __forceinline__ float div_rn(float a, const Divisor& d) {
+  if (fabsf(a) < d.thresh) return __fdiv_rn(a, d.b);
+  const float q0 = __fmul_rn(a, d.y);
+  const float r = __fmaf_rn(-d.b, q0, a);
+  return __fmaf_rn(r, d.y, q0);
+}
+
+// int8 code: round-half-even of the IEEE float32 quotient x / scale, clamped to +-127.
+__device__ __forceinline__ int8_t quant_int8(float x, const Divisor& d) {
+  float q = rintf(div_rn(x, d));
   q = fminf(fmaxf(q, -kInt8Max), kInt8Max);
   return static_cast<int8_t>(__float2int_rn(q));
 }
-// e4m3fn code of clamp(x / scale, +-448): hardware RNE conversion (cvt.rn.satfinite.e4m3x2.f32).
-__device__ __forceinline__ uint16_t quant_e4m3x2(float a, float b, float scale) {
-  float qa = fminf(fmaxf(__fdiv_rn(a, scale), -kE4m3Max), kE4m3Max);
-  float qb = fminf(fmaxf(__fdiv_rn(b, scale), -kE4m3Max), kE4m3Max);
+
+// e4m3fn codes of clamp(x / scale, +-448) for two values (a in the low byte).  The
+// hardware conversion (cvt.rn.satfinite.e4m3x2.f32) rounds to nearest even and
+// saturates to +-448, which is exactly clamp-then-cast.
+__device__ __forceinline__ uint16_t quant_e4m3x2(float a, float b, const Divisor& d) {
+  const float qa = div_rn(a, d);
+  const float qb = div_rn(b, d);
   return static_cast<uint16_t>(__nv_cvt_float2_to_fp8x2(make_float2(qa, qb), __NV_SATFINITE, __NV_E4M3));
 }
 

@@ -14,12 +14,12 @@ namespace {
 
 // Packs eight int8 codes of one Vec8 into a 64-bit word (little-endian order).
 template <typename T>
-__device__ __forceinline__ uint2 quant8(const Vec8<T>& v, float scale) {
+__device__ __forceinline__ uint2 quant8(const Vec8<T>& v, const Divisor& d) {
   uint32_t lo = 0, hi = 0;
 #pragma unroll
-  for (int i = 0; i < 4; ++i) lo |= (uint32_t)(uint8_t)quant_int8(v.get(i), scale) << (8 * i);
+  for (int i = 0; i < 4; ++i) lo |= (uint32_t)(uint8_t)quant_int8(v.get(i), d) << (8 * i);
 #pragma unroll
-  for (int i = 0; i < 4; ++i) hi |= (uint32_t)(uint8_t)quant_int8(v.get(4 + i), scale) << (8 * i);
+  for (int i = 0; i < 4; ++i) hi |= (uint32_t)(uint8_t)quant_int8(v.get(4 + i), d) << (8 * i);
   return make_uint2(lo, hi);
 }
 
@@ -61,6 +61,7 @@ __global__ void __launch_bounds__(256) tensor_quant_kernel(const T* __restrict__
   // input-dtype arithmetic does (dynamic_scaled_int8_quant.py:22).
   const float s_in = Elem<T>::to_f(Elem<T>::from_f(__fdiv_rn(amax, kInt8Max)));
   const float scale = fmaxf(s_in, kMinScalingFactor);
+  const Divisor d = make_divisor(scale);
   if (blockIdx.x == 0 && threadIdx.x == 0) {
     *scale_out = scale;
     if (azp_out) *azp_out = 0;
@@ -69,10 +70,10 @@ __global__ void __launch_bounds__(256) tensor_quant_kernel(const T* __restrict__
   for (int64_t v = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; v < nvec; v += stride) {
     Vec8<T> a;
     a.load(x + v * 8);
-    reinterpret_cast<uint2*>(q)[v] = quant8(a, scale);
+    reinterpret_cast<uint2*>(q)[v] = quant8(a, d);
   }
   for (int64_t i = nvec * 8 + (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < numel; i += stride)
-    q[i] = quant_int8(Elem<T>::to_f(x[i]), scale);
+    q[i] = quant_int8(Elem<T>::to_f(x[i]), d);
 }
 
 // ---------------------------------------------------------------- per-group, small groups
@@ -96,7 +97,7 @@ __global__ void __launch_bounds__(256) group_quant_subwarp_kernel(const T* __res
     m = group_max(m, lanes);
     const float scale = fmaxf(__fdiv_rn(m, kInt8Max), eps);
     if (live) {
-      reinterpret_cast<uint2*>(q)[v] = quant8(a, scale);
+      reinterpret_cast<uint2*>(q)[v] = quant8(a, make_divisor(scale));
       if ((v & (lanes - 1)) == 0) scales[v / lanes] = scale;
     }
   }
@@ -123,11 +124,12 @@ __global__ void __launch_bounds__(1024) group_quant_rowblock_kernel(const T* __r
   }
   m = block_reduce<true>(m, scratch);
   const float scale = fmaxf(__fdiv_rn(m, kInt8Max), eps);
+  const Divisor d = make_divisor(scale);
   uint2* qg = reinterpret_cast<uint2*>(q + g * group_vecs * 8);
 #pragma unroll
   for (int j = 0; j < VPT; ++j) {
     const int64_t v = threadIdx.x + (int64_t)j * blockDim.x;
-    if (v < group_vecs) qg[v] = quant8(a[j], scale);
+    if (v < group_vecs) qg[v] = quant8(a[j], d);
   }
   if (threadIdx.x == 0) scales[g] = scale;
 }
@@ -146,7 +148,8 @@ __global__ void __launch_bounds__(256) group_quant_scalar_kernel(const T* __rest
     for (int64_t i = lane; i < group_size; i += 32) m = fmaxf(m, fabsf(Elem<T>::to_f(xg[i])));
     m = warp_max(m);
     const float scale = fmaxf(__fdiv_rn(m, kInt8Max), eps);
-    for (int64_t i = lane; i < group_size; i += 32) q[g * group_size + i] = quant_int8(Elem<T>::to_f(xg[i]), scale);
+    const Divisor d = make_divisor(scale);
+    for (int64_t i = lane; i < group_size; i += 32) q[g * group_size + i] = quant_int8(Elem<T>::to_f(xg[i]), d);
     if (lane == 0) scales[g] = scale;
   }
 }

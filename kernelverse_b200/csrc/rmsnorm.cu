@@ -1,10 +1,17 @@
 // Residual add + RMSNorm, optionally fused with dynamic per-row int8 / e4m3 quantisation.
 //
-// One CTA owns one row.  The row's x and residual are read once with 128-bit
-// loads, the float32 sum s = x + r stays in registers through both block
-// reductions (sum of squares, then amax of the normalised row), and the
-// outputs (updated residual, codes, scale -- or the normalised row itself) are
-// written once: the kernel moves exactly the algorithmic bytes.
+// Main path (rows of up to 24 KB per input): a persistent kernel, 2-3 CTAs per
+// SM, each looping over rows.  One thread streams the next rows' x and residual
+// into a double-buffered shared-memory ring with 1-D bulk copies
+// (cp.async.bulk, completion on an mbarrier, L2 evict-first), so HBM reads of
+// row k+1 and k+2 overlap the reductions and stores of row k.  The float32 sum
+// s = x + r stays in registers through both block reductions (sum of squares,
+// then amax of the normalised row) and every output is written once: the
+// kernel moves exactly the algorithmic bytes.  The weight slice a thread needs
+// is loaded into registers once per CTA.
+//
+// Fallbacks: a one-CTA-per-row register kernel for longer rows and a scalar
+// kernel for unaligned or odd sizes.
 //
 // Arithmetic order follows operators/normalization/add_rmsnorm/add_rmsnorm.py:30-35
 // in its float32 "correctness" mode: s = x + r; var = sum(s^2) / H;
@@ -12,6 +19,7 @@
 // fast-math), so only the float32 summation order of sum(s^2) differs from the
 // reference.
 #include "kvb_common.cuh"
+#include "kvb_async.cuh"
 
 namespace kvb {
 namespace {
@@ -88,6 +96,7 @@ __global__ void __launch_bounds__(256) add_rmsnorm_kernel(const T* __restrict__ 
   amax = block_reduce<true>(amax, scratch);
   const float qmax = MODE == kQuantE4m3 ? kE4m3Max : kInt8Max;
   const float scale = fmaxf(__fdiv_rn(amax, qmax), kMinScalingFactor);
+  const Divisor dv = make_divisor(scale);
   uint2* crow = reinterpret_cast<uint2*>(codes + row * nvec * 8);
 #pragma unroll
   for (int j = 0; j < VPT; ++j) {
@@ -95,14 +104,14 @@ __global__ void __launch_bounds__(256) add_rmsnorm_kernel(const T* __restrict__ 
     if (v < nvec) {
       uint32_t lo, hi;
       if (MODE == kQuantE4m3) {
-        lo = quant_e4m3x2(s[j][0], s[j][1], scale) | ((uint32_t)quant_e4m3x2(s[j][2], s[j][3], scale) << 16);
-        hi = quant_e4m3x2(s[j][4], s[j][5], scale) | ((uint32_t)quant_e4m3x2(s[j][6], s[j][7], scale) << 16);
+        lo = quant_e4m3x2(s[j][0], s[j][1], dv) | ((uint32_t)quant_e4m3x2(s[j][2], s[j][3], dv) << 16);
+        hi = quant_e4m3x2(s[j][4], s[j][5], dv) | ((uint32_t)quant_e4m3x2(s[j][6], s[j][7], dv) << 16);
       } else {
         lo = hi = 0;
 #pragma unroll
         for (int k = 0; k < 4; ++k) {
-          lo |= (uint32_t)(uint8_t)quant_int8(s[j][k], scale) << (8 * k);
-          hi |= (uint32_t)(uint8_t)quant_int8(s[j][4 + k], scale) << (8 * k);
+          lo |= (uint32_t)(uint8_t)quant_int8(s[j][k], dv) << (8 * k);
+          hi |= (uint32_t)(uint8_t)quant_int8(s[j][4 + k], dv) << (8 * k);
         }
       }
       __stcs(crow + v, make_uint2(lo, hi));
@@ -140,14 +149,15 @@ __global__ void __launch_bounds__(256) add_rmsnorm_scalar_kernel(const T* __rest
   amax = block_reduce<true>(amax, scratch);
   const float qmax = MODE == kQuantE4m3 ? kE4m3Max : kInt8Max;
   const float scale = fmaxf(__fdiv_rn(amax, qmax), kMinScalingFactor);
+  const Divisor dv = make_divisor(scale);
   __syncthreads();   // every thread has re-read x/res before the residual may be overwritten in place
   for (int64_t i = threadIdx.x; i < hidden; i += blockDim.x) {
     const float s = Elem<T>::to_f(x[base + i]) + Elem<T>::to_f(res[base + i]);
     const float y = __fmul_rn(__fmul_rn(s, rinv), Elem<T>::to_f(w[i]));
     if (MODE == kQuantE4m3) {
-      codes[base + i] = (uint8_t)(quant_e4m3x2(y, 0.0f, scale) & 0xff);
+      codes[base + i] = (uint8_t)(quant_e4m3x2(y, 0.0f, dv) & 0xff);
     } else {
-      codes[base + i] = (uint8_t)quant_int8(y, scale);
+      codes[base + i] = (uint8_t)quant_int8(y, dv);
     }
   }
   if (out) {
@@ -156,6 +166,192 @@ __global__ void __launch_bounds__(256) add_rmsnorm_scalar_kernel(const T* __rest
       out[base + i] = Elem<T>::from_f(Elem<T>::to_f(x[base + i]) + Elem<T>::to_f(res[base + i]));
   }
   if (threadIdx.x == 0) scales[blockIdx.x] = scale;
+}
+
+
+// ---------------------------------------------------------------------------------------------
+// Persistent, bulk-copy-pipelined kernel.  Dynamic shared memory holds kStages stages of
+// [x row | residual row]; full[s] completes when both bulk copies of stage s have landed.
+constexpr int kStages = 2;
+
+template <typename T>
+__device__ __forceinline__ void issue_row(const T* x, const T* res, int64_t row, int nvec, uint8_t* stage,
+                                          uint32_t row_bytes, uint64_t* bar, uint64_t pol) {
+  mbar_arrive_expect_tx(bar, 2 * row_bytes);
+  bulk_g2s(stage, x + row * (int64_t)nvec * 8, row_bytes, bar, pol);
+  bulk_g2s(stage + row_bytes, res + row * (int64_t)nvec * 8, row_bytes, bar, pol);
+}
+
+template <typename T, int VPT, int MODE>
+__global__ void __launch_bounds__(256) add_rmsnorm_pipe_kernel(const T* __restrict__ x, const T* __restrict__ res,
+                                                               const T* __restrict__ w, int64_t rows, int nvec,
+                                                               float hidden_f, float eps, T* __restrict__ out,
+                                                               uint8_t* __restrict__ codes, float* __restrict__ scales) {
+  extern __shared__ __align__(128) uint8_t smem[];
+  __shared__ uint64_t full[kStages];
+  __shared__ float scratch[32];
+  const uint32_t row_bytes = (uint32_t)nvec * 8u * (uint32_t)sizeof(T);
+  const int64_t G = gridDim.x;
+  const int tid = threadIdx.x;
+
+  if (tid == 0) {
+#pragma unroll
+    for (int s = 0; s < kStages; ++s) mbar_init(&full[s], 1);
+    fence_mbar_init();
+  }
+  __syncthreads();
+  const uint64_t pol = policy_evict_first();
+  if (tid == 0) {
+#pragma unroll
+    for (int s = 0; s < kStages; ++s) {
+      const int64_t row = blockIdx.x + s * G;
+      if (row < rows) issue_row(x, res, row, nvec, smem + s * 2 * row_bytes, row_bytes, &full[s], pol);
+    }
+  }
+  Vec8<T> wv[VPT];
+#pragma unroll
+  for (int j = 0; j < VPT; ++j) {
+    const int v = tid + j * blockDim.x;
+    if (v < nvec) wv[j].load(w + (int64_t)v * 8);
+  }
+
+  int k = 0;
+  bool failed = false;
+  for (int64_t row = blockIdx.x; row < rows; row += G, ++k) {
+    const int st = k % kStages;
+    const uint32_t par = (uint32_t)(k / kStages) & 1u;
+    const bool ok = mbar_wait_bounded(&full[st], par);
+    if (__syncthreads_or(!ok)) {
+      failed = true;
+      break;
+    }
+    const T* sx = reinterpret_cast<const T*>(smem + st * 2 * row_bytes);
+    const T* sr = reinterpret_cast<const T*>(smem + st * 2 * row_bytes + row_bytes);
+    float s[VPT][8];
+    float ss = 0.0f;
+#pragma unroll
+    for (int j = 0; j < VPT; ++j) {
+      const int v = tid + j * blockDim.x;
+      if (v < nvec) {
+        Vec8<T> a, b;
+#pragma unroll
+        for (int i = 0; i < Vec8<T>::kWords; ++i) {
+          a.w[i] = reinterpret_cast<const uint4*>(sx + v * 8)[i];
+          b.w[i] = reinterpret_cast<const uint4*>(sr + v * 8)[i];
+        }
+#pragma unroll
+        for (int e = 0; e < 8; ++e) {
+          s[j][e] = a.get(e) + b.get(e);
+          ss = fmaf(s[j][e], s[j][e], ss);
+        }
+      } else {
+#pragma unroll
+        for (int e = 0; e < 8; ++e) s[j][e] = 0.0f;
+      }
+    }
+    ss = block_reduce<false>(ss, scratch);     // after this every thread has finished reading stage st
+    if (tid == 0) {
+      const int64_t next = row + kStages * G;
+      if (next < rows) issue_row(x, res, next, nvec, smem + st * 2 * row_bytes, row_bytes, &full[st], pol);
+    }
+    const float rinv = 1.0f / sqrtf(__fdiv_rn(ss, hidden_f) + eps);
+
+    if (MODE == kOutY) {
+#pragma unroll
+      for (int j = 0; j < VPT; ++j) {
+        const int v = tid + j * blockDim.x;
+        if (v < nvec) {
+          Vec8<T> o;
+#pragma unroll
+          for (int e = 0; e < 8; ++e) o.set(e, __fmul_rn(__fmul_rn(s[j][e], rinv), wv[j].get(e)));
+          o.store(out + row * (int64_t)nvec * 8 + (int64_t)v * 8);
+        }
+      }
+      continue;
+    }
+    float amax = 0.0f;
+#pragma unroll
+    for (int j = 0; j < VPT; ++j) {
+      const int v = tid + j * blockDim.x;
+      if (v < nvec) {
+        if (out) {
+          Vec8<T> o;
+#pragma unroll
+          for (int e = 0; e < 8; ++e) o.set(e, s[j][e]);
+          o.store(out + row * (int64_t)nvec * 8 + (int64_t)v * 8);
+        }
+#pragma unroll
+        for (int e = 0; e < 8; ++e) {
+          s[j][e] = __fmul_rn(__fmul_rn(s[j][e], rinv), wv[j].get(e));
+          amax = fmaxf(amax, fabsf(s[j][e]));
+        }
+      }
+    }
+    amax = block_reduce<true>(amax, scratch);
+    const float qmax = MODE == kQuantE4m3 ? kE4m3Max : kInt8Max;
+    const float scale = fmaxf(__fdiv_rn(amax, qmax), kMinScalingFactor);
+    const Divisor dv = make_divisor(scale);
+    uint2* crow = reinterpret_cast<uint2*>(codes + row * (int64_t)nvec * 8);
+#pragma unroll
+    for (int j = 0; j < VPT; ++j) {
+      const int v = tid + j * blockDim.x;
+      if (v < nvec) {
+        uint32_t lo, hi;
+        if (MODE == kQuantE4m3) {
+          lo = quant_e4m3x2(s[j][0], s[j][1], dv) | ((uint32_t)quant_e4m3x2(s[j][2], s[j][3], dv) << 16);
+          hi = quant_e4m3x2(s[j][4], s[j][5], dv) | ((uint32_t)quant_e4m3x2(s[j][6], s[j][7], dv) << 16);
+        } else {
+          lo = hi = 0;
+#pragma unroll
+          for (int e = 0; e < 4; ++e) {
+            lo |= (uint32_t)(uint8_t)quant_int8(s[j][e], dv) << (8 * e);
+            hi |= (uint32_t)(uint8_t)quant_int8(s[j][4 + e], dv) << (8 * e);
+          }
+        }
+        __stcs(crow + v, make_uint2(lo, hi));
+      }
+    }
+    if (tid == 0) scales[row] = scale;
+  }
+  if (failed && tid == 0) {
+    // Drain: wait (bounded) for the copies this CTA still has in flight before exiting.
+    for (int i = 0; i < kStages; ++i) {
+      const int kk = k + i;
+      if (blockIdx.x + (int64_t)kk * G < rows) mbar_wait_bounded(&full[kk % kStages], (uint32_t)(kk / kStages) & 1u);
+    }
+  }
+}
+
+struct PipeConfig {
+  int grid;
+  size_t smem;
+};
+
+// Grid = (resident CTAs per SM) x (SM count), computed once per instantiation and device.
+template <typename T, int VPT, int MODE>
+int launch_pipe(const T* x, const T* r, const T* w, int64_t rows, int64_t nvec, float eps, T* out, uint8_t* codes,
+                float* scales, cudaStream_t st) {
+  const size_t smem = (size_t)kStages * 2 * nvec * 8 * sizeof(T);
+  static int cached_dev = -1, cached_blocks = 0;
+  static size_t cached_smem = 0;
+  int dev = 0;
+  cudaGetDevice(&dev);
+  auto kern = add_rmsnorm_pipe_kernel<T, VPT, MODE>;
+  if (dev != cached_dev || smem != cached_smem) {
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    if (e != cudaSuccess) return set_error(KVB_E_LAUNCH, "add_rmsnorm: smem attribute: %s", cudaGetErrorString(e));
+    int nb = 0;
+    e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&nb, kern, 256, smem);
+    if (e != cudaSuccess || nb < 1) return set_error(KVB_E_LAUNCH, "add_rmsnorm: occupancy query failed");
+    cached_dev = dev;
+    cached_smem = smem;
+    cached_blocks = nb;
+  }
+  int sms = 0;
+  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  const int64_t grid = std::min<int64_t>(rows, (int64_t)cached_blocks * sms);
+  kern<<<(unsigned)grid, 256, smem, st>>>(x, r, w, rows, (int)nvec, (float)(nvec * 8), eps, out, codes, scales);
+  return check_launch("add_rmsnorm_pipe_kernel");
 }
 
 template <typename T, int MODE, int VPT>
@@ -182,6 +378,15 @@ int launch(const void* xv, const void* rv, const void* wv, int64_t rows, int64_t
   // kernel reads its row fully into registers before writing, so aliasing is safe there.
   const bool vec = hidden % 8 == 0 && aligned16(x) && aligned16(r) && aligned16(w) && (!out || aligned16(out)) &&
                    (!codes || aligned8(codes)) && hidden / 8 <= 16 * 256;
+  // Persistent pipelined path: rows of 1..24 KB per input, at least 256 vectors of work.
+  const int64_t row_bytes = hidden * (int64_t)sizeof(T);
+  if (vec && hidden / 8 >= 256 && row_bytes <= 24 * 1024) {
+    const int64_t nvec = hidden / 8;
+    if (nvec <= 256) return launch_pipe<T, 1, MODE>(x, r, w, rows, nvec, eps, out, codes, scales, st);
+    if (nvec <= 512) return launch_pipe<T, 2, MODE>(x, r, w, rows, nvec, eps, out, codes, scales, st);
+    if (nvec <= 1024) return launch_pipe<T, 4, MODE>(x, r, w, rows, nvec, eps, out, codes, scales, st);
+    return launch_pipe<T, 6, MODE>(x, r, w, rows, nvec, eps, out, codes, scales, st);
+  }
   if (vec) {
     const int64_t nvec = hidden / 8;
     if (nvec <= 256) return launch_vec<T, MODE, 1>(x, r, w, rows, nvec, eps, out, codes, scales, st);

@@ -44,3 +44,17 @@ def golden_names(prefix: str):
 @pytest.fixture
 def golden():
     return load_golden
+
+
+@pytest.fixture(autouse=True)
+def _device_status_clean(request):
+    """GPU tests: no bounded device-side wait may have given up during the test."""
+    yield
+    if request.node.get_closest_marker("gpu") is None:
+        return
+    import torch
+    if not torch.cuda.is_available():
+        return
+    from kernelverse_b200 import _lib
+    status = _lib.lib().kvb_device_status(1)
+    assert status == 0, f"kvb_device_status = {status:#x} after {request.node.name}"
