@@ -79,7 +79,52 @@ template <typename T> struct Vec8 {
     T* e = reinterpret_cast<T*>(w);
     e[i] = Elem<T>::from_f(v);
   }
+  // All eight elements as float32 / from float32 (round-to-nearest-even), using packed
+  // conversions for the 16-bit types.
+  __device__ __forceinline__ void unpack(float f[8]) const;
+  __device__ __forceinline__ void pack(const float f[8]);
 };
+
+template <> __device__ __forceinline__ void Vec8<__nv_bfloat16>::unpack(float f[8]) const {
+  const uint32_t* u = reinterpret_cast<const uint32_t*>(w);
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    f[2 * i] = __uint_as_float(u[i] << 16);
+    f[2 * i + 1] = __uint_as_float(u[i] & 0xffff0000u);
+  }
+}
+template <> __device__ __forceinline__ void Vec8<__nv_bfloat16>::pack(const float f[8]) {
+  uint32_t* u = reinterpret_cast<uint32_t*>(w);
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    __nv_bfloat162 h = __floats2bfloat162_rn(f[2 * i], f[2 * i + 1]);
+    u[i] = *reinterpret_cast<uint32_t*>(&h);
+  }
+}
+template <> __device__ __forceinline__ void Vec8<__half>::unpack(float f[8]) const {
+  const __half2* h = reinterpret_cast<const __half2*>(w);
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    float2 t = __half22float2(h[i]);
+    f[2 * i] = t.x;
+    f[2 * i + 1] = t.y;
+  }
+}
+template <> __device__ __forceinline__ void Vec8<__half>::pack(const float f[8]) {
+  __half2* h = reinterpret_cast<__half2*>(w);
+#pragma unroll
+  for (int i = 0; i < 4; ++i) h[i] = __floats2half2_rn(f[2 * i], f[2 * i + 1]);
+}
+template <> __device__ __forceinline__ void Vec8<float>::unpack(float f[8]) const {
+  const float* e = reinterpret_cast<const float*>(w);
+#pragma unroll
+  for (int i = 0; i < 8; ++i) f[i] = e[i];
+}
+template <> __device__ __forceinline__ void Vec8<float>::pack(const float f[8]) {
+  float* e = reinterpret_cast<float*>(w);
+#pragma unroll
+  for (int i = 0; i < 8; ++i) e[i] = f[i];
+}
 
 // ------------------------------------------------------------------ reductions
 __device__ __forceinline__ float warp_max(float v) {
@@ -116,11 +161,13 @@ __device__ __forceinline__ float block_reduce(float v, float* scratch) {
 // (P. Markstein, "IA-64 and Elementary Functions", 2000, Thm. 8.10): with y the
 // correctly rounded reciprocal and q0 = RN(a*y) within an ulp of a/b, the remainder
 // r = a - b*q0 is exact in one FMA and q1 = RN(q0 + r*y) is the round-to-nearest
-// quotient.  The theorem assumes no underflow or overflow in the intermediate
-// steps, so a quotient takes the IEEE division instead when |a| < 2^-96 (zero
-// included, which keeps the quotient's sign) or when b lies outside
-// [2^-120, 2^120] (then every element of the group does).  A divisor is set up
-// once per quantisation group and reused for every element.
+// quotient.  The theorem assumes that nothing underflows or overflows in the
+// intermediate steps.  Domain of the fast path: 2^-120 <= b <= 2^120 and
+// max(2^-96, b * 2^-100) <= |a| <= 2^100 * b -- the quantisers always have
+// |a| <= 448 * b because b is the group's amax / 448 (or / 127) or larger.
+// Below the lower bound (zero included, which keeps the quotient's sign) the
+// IEEE division is used; when b is out of range every element of the group is.
+// A divisor is set up once per quantisation group and reused for every element.
 // tests/test_gpu_numerics.py checks div_rn against CUDA's __fdiv_rn bit for bit.
 struct Divisor {
   float b, y, thresh;
@@ -129,19 +176,25 @@ __device__ __forceinline__ Divisor make_divisor(float b) {
   Divisor d;
   d.b = b;
   d.y = __frcp_rn(b);
-  d.thresh = (b >= 0x1p-120f && b <= 0x1p120f) ? 0x1p-96f : __int_as_float(0x7f800000);
+  d.thresh = (b >= 0x1p-120f && b <= 0x1p120f) ? fmaxf(0x1p-96f, b * 0x1p-100f) : __int_as_float(0x7f800000);
   return d;
 }
-__device__ __forceinline__ float div_rn(float a, const Divisor& d) {
-  if (fabsf(a) < d.thresh) return __fdiv_rn(a, d.b);
+// Fast path only: the caller has checked |a| >= d.thresh.
+__device__ __forceinline__ float div_rn_fast(float a, const Divisor& d) {
   const float q0 = __fmul_rn(a, d.y);
   const float r = __fmaf_rn(-d.b, q0, a);
   return __fmaf_rn(r, d.y, q0);
 }
+__device__ __forceinline__ float div_rn(float a, const Divisor& d) {
+  if (fabsf(a) < d.thresh) return __fdiv_rn(a, d.b);
+  return div_rn_fast(a, d);
+}
 
 // int8 code: round-half-even of the IEEE float32 quotient x / scale, clamped to +-127.
+// kChecked = false: the caller has verified |x| >= d.thresh for the values passed.
+template <bool kChecked = true>
 __device__ __forceinline__ int8_t quant_int8(float x, const Divisor& d) {
-  float q = rintf(div_rn(x, d));
+  float q = rintf(kChecked ? div_rn(x, d) : div_rn_fast(x, d));
   q = fminf(fmaxf(q, -kInt8Max), kInt8Max);
   return static_cast<int8_t>(__float2int_rn(q));
 }
@@ -149,9 +202,10 @@ __device__ __forceinline__ int8_t quant_int8(float x, const Divisor& d) {
 // e4m3fn codes of clamp(x / scale, +-448) for two values (a in the low byte).  The
 // hardware conversion (cvt.rn.satfinite.e4m3x2.f32) rounds to nearest even and
 // saturates to +-448, which is exactly clamp-then-cast.
+template <bool kChecked = true>
 __device__ __forceinline__ uint16_t quant_e4m3x2(float a, float b, const Divisor& d) {
-  const float qa = div_rn(a, d);
-  const float qb = div_rn(b, d);
+  const float qa = kChecked ? div_rn(a, d) : div_rn_fast(a, d);
+  const float qb = kChecked ? div_rn(b, d) : div_rn_fast(b, d);
   return static_cast<uint16_t>(__nv_cvt_float2_to_fp8x2(make_float2(qa, qb), __NV_SATFINITE, __NV_E4M3));
 }
 

@@ -13,21 +13,38 @@ namespace kvb {
 namespace {
 
 // Packs eight int8 codes of one Vec8 into a 64-bit word (little-endian order).
-template <typename T>
+template <bool kChecked, typename T>
 __device__ __forceinline__ uint2 quant8(const Vec8<T>& v, const Divisor& d) {
+  float f[8];
+  v.unpack(f);
   uint32_t lo = 0, hi = 0;
 #pragma unroll
-  for (int i = 0; i < 4; ++i) lo |= (uint32_t)(uint8_t)quant_int8(v.get(i), d) << (8 * i);
+  for (int i = 0; i < 4; ++i) lo |= (uint32_t)(uint8_t)quant_int8<kChecked>(f[i], d) << (8 * i);
 #pragma unroll
-  for (int i = 0; i < 4; ++i) hi |= (uint32_t)(uint8_t)quant_int8(v.get(4 + i), d) << (8 * i);
+  for (int i = 0; i < 4; ++i) hi |= (uint32_t)(uint8_t)quant_int8<kChecked>(f[4 + i], d) << (8 * i);
   return make_uint2(lo, hi);
+}
+// Quantises one vector, skipping the per-element division guard when the vector's
+// smallest magnitude already satisfies it (the common case).
+template <typename T>
+__device__ __forceinline__ uint2 quant8(const Vec8<T>& v, const Divisor& d, float vmin) {
+  return vmin >= d.thresh ? quant8<false>(v, d) : quant8<true>(v, d);
 }
 
 template <typename T>
 __device__ __forceinline__ float vec_amax(const Vec8<T>& v) {
-  float m = 0.0f;
+  float f[8], m = 0.0f;
+  v.unpack(f);
 #pragma unroll
-  for (int i = 0; i < 8; ++i) m = fmaxf(m, fabsf(v.get(i)));
+  for (int i = 0; i < 8; ++i) m = fmaxf(m, fabsf(f[i]));
+  return m;
+}
+template <typename T>
+__device__ __forceinline__ float vec_amin(const Vec8<T>& v) {
+  float f[8], m = __int_as_float(0x7f800000);
+  v.unpack(f);
+#pragma unroll
+  for (int i = 0; i < 8; ++i) m = fminf(m, fabsf(f[i]));
   return m;
 }
 
@@ -70,7 +87,7 @@ __global__ void __launch_bounds__(256) tensor_quant_kernel(const T* __restrict__
   for (int64_t v = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; v < nvec; v += stride) {
     Vec8<T> a;
     a.load(x + v * 8);
-    reinterpret_cast<uint2*>(q)[v] = quant8(a, d);
+    reinterpret_cast<uint2*>(q)[v] = quant8(a, d, vec_amin(a));
   }
   for (int64_t i = nvec * 8 + (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < numel; i += stride)
     q[i] = quant_int8(Elem<T>::to_f(x[i]), d);
@@ -97,7 +114,7 @@ __global__ void __launch_bounds__(256) group_quant_subwarp_kernel(const T* __res
     m = group_max(m, lanes);
     const float scale = fmaxf(__fdiv_rn(m, kInt8Max), eps);
     if (live) {
-      reinterpret_cast<uint2*>(q)[v] = quant8(a, make_divisor(scale));
+      reinterpret_cast<uint2*>(q)[v] = quant8(a, make_divisor(scale), vec_amin(a));
       if ((v & (lanes - 1)) == 0) scales[v / lanes] = scale;
     }
   }
@@ -113,23 +130,32 @@ __global__ void __launch_bounds__(1024) group_quant_rowblock_kernel(const T* __r
   const int64_t g = blockIdx.x;
   const T* xg = x + g * group_vecs * 8;
   Vec8<T> a[VPT];
-  float m = 0.0f;
+  float m = 0.0f, mn = __int_as_float(0x7f800000);
 #pragma unroll
   for (int j = 0; j < VPT; ++j) {
     const int64_t v = threadIdx.x + (int64_t)j * blockDim.x;
     if (v < group_vecs) {
       a[j].load_stream(xg + v * 8);
       m = fmaxf(m, vec_amax(a[j]));
+      mn = fminf(mn, vec_amin(a[j]));
     }
   }
   m = block_reduce<true>(m, scratch);
   const float scale = fmaxf(__fdiv_rn(m, kInt8Max), eps);
   const Divisor d = make_divisor(scale);
   uint2* qg = reinterpret_cast<uint2*>(q + g * group_vecs * 8);
+  if (mn >= d.thresh) {
 #pragma unroll
-  for (int j = 0; j < VPT; ++j) {
-    const int64_t v = threadIdx.x + (int64_t)j * blockDim.x;
-    if (v < group_vecs) qg[v] = quant8(a[j], d);
+    for (int j = 0; j < VPT; ++j) {
+      const int64_t v = threadIdx.x + (int64_t)j * blockDim.x;
+      if (v < group_vecs) qg[v] = quant8<false>(a[j], d);
+    }
+  } else {
+#pragma unroll
+    for (int j = 0; j < VPT; ++j) {
+      const int64_t v = threadIdx.x + (int64_t)j * blockDim.x;
+      if (v < group_vecs) qg[v] = quant8<true>(a[j], d);
+    }
   }
   if (threadIdx.x == 0) scales[g] = scale;
 }

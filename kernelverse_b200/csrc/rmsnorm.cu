@@ -182,8 +182,33 @@ __device__ __forceinline__ void issue_row(const T* x, const T* res, int64_t row,
   bulk_g2s(stage + row_bytes, res + row * (int64_t)nvec * 8, row_bytes, bar, pol);
 }
 
+// Codes of one thread's VPT vectors of a row (y already in s), packed 8 per 64-bit store.
+template <int VPT, int MODE, bool kChecked>
+__device__ __forceinline__ void store_codes(const float (&s)[VPT][8], const Divisor& dv, uint2* crow, int tid,
+                                            int stride, int nvec) {
+#pragma unroll
+  for (int j = 0; j < VPT; ++j) {
+    const int v = tid + j * stride;
+    if (v < nvec) {
+      uint32_t lo, hi;
+      if (MODE == kQuantE4m3) {
+        lo = quant_e4m3x2<kChecked>(s[j][0], s[j][1], dv) | ((uint32_t)quant_e4m3x2<kChecked>(s[j][2], s[j][3], dv) << 16);
+        hi = quant_e4m3x2<kChecked>(s[j][4], s[j][5], dv) | ((uint32_t)quant_e4m3x2<kChecked>(s[j][6], s[j][7], dv) << 16);
+      } else {
+        lo = hi = 0;
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          lo |= (uint32_t)(uint8_t)quant_int8<kChecked>(s[j][e], dv) << (8 * e);
+          hi |= (uint32_t)(uint8_t)quant_int8<kChecked>(s[j][4 + e], dv) << (8 * e);
+        }
+      }
+      __stcs(crow + v, make_uint2(lo, hi));
+    }
+  }
+}
+
 template <typename T, int VPT, int MODE>
-__global__ void __launch_bounds__(256) add_rmsnorm_pipe_kernel(const T* __restrict__ x, const T* __restrict__ res,
+__global__ void __launch_bounds__(512) add_rmsnorm_pipe_kernel(const T* __restrict__ x, const T* __restrict__ res,
                                                                const T* __restrict__ w, int64_t rows, int nvec,
                                                                float hidden_f, float eps, T* __restrict__ out,
                                                                uint8_t* __restrict__ codes, float* __restrict__ scales) {
@@ -193,6 +218,7 @@ __global__ void __launch_bounds__(256) add_rmsnorm_pipe_kernel(const T* __restri
   const uint32_t row_bytes = (uint32_t)nvec * 8u * (uint32_t)sizeof(T);
   const int64_t G = gridDim.x;
   const int tid = threadIdx.x;
+  const int nthr = blockDim.x;
 
   if (tid == 0) {
 #pragma unroll
@@ -208,10 +234,10 @@ __global__ void __launch_bounds__(256) add_rmsnorm_pipe_kernel(const T* __restri
       if (row < rows) issue_row(x, res, row, nvec, smem + s * 2 * row_bytes, row_bytes, &full[s], pol);
     }
   }
-  Vec8<T> wv[VPT];
+  Vec8<T> wv[VPT];   // this thread's weight slice, loaded once
 #pragma unroll
   for (int j = 0; j < VPT; ++j) {
-    const int v = tid + j * blockDim.x;
+    const int v = tid + j * nthr;
     if (v < nvec) wv[j].load(w + (int64_t)v * 8);
   }
 
@@ -225,23 +251,26 @@ __global__ void __launch_bounds__(256) add_rmsnorm_pipe_kernel(const T* __restri
       failed = true;
       break;
     }
-    const T* sx = reinterpret_cast<const T*>(smem + st * 2 * row_bytes);
-    const T* sr = reinterpret_cast<const T*>(smem + st * 2 * row_bytes + row_bytes);
+    const uint4* sx = reinterpret_cast<const uint4*>(smem + st * 2 * row_bytes);
+    const uint4* sr = reinterpret_cast<const uint4*>(smem + st * 2 * row_bytes + row_bytes);
     float s[VPT][8];
     float ss = 0.0f;
 #pragma unroll
     for (int j = 0; j < VPT; ++j) {
-      const int v = tid + j * blockDim.x;
+      const int v = tid + j * nthr;
       if (v < nvec) {
         Vec8<T> a, b;
 #pragma unroll
         for (int i = 0; i < Vec8<T>::kWords; ++i) {
-          a.w[i] = reinterpret_cast<const uint4*>(sx + v * 8)[i];
-          b.w[i] = reinterpret_cast<const uint4*>(sr + v * 8)[i];
+          a.w[i] = sx[v * Vec8<T>::kWords + i];
+          b.w[i] = sr[v * Vec8<T>::kWords + i];
         }
+        float fb[8];
+        a.unpack(s[j]);
+        b.unpack(fb);
 #pragma unroll
         for (int e = 0; e < 8; ++e) {
-          s[j][e] = a.get(e) + b.get(e);
+          s[j][e] += fb[e];
           ss = fmaf(s[j][e], s[j][e], ss);
         }
       } else {
@@ -255,35 +284,41 @@ __global__ void __launch_bounds__(256) add_rmsnorm_pipe_kernel(const T* __restri
       if (next < rows) issue_row(x, res, next, nvec, smem + st * 2 * row_bytes, row_bytes, &full[st], pol);
     }
     const float rinv = 1.0f / sqrtf(__fdiv_rn(ss, hidden_f) + eps);
+    T* orow = out ? out + row * (int64_t)nvec * 8 : nullptr;
 
     if (MODE == kOutY) {
 #pragma unroll
       for (int j = 0; j < VPT; ++j) {
-        const int v = tid + j * blockDim.x;
+        const int v = tid + j * nthr;
         if (v < nvec) {
-          Vec8<T> o;
+          float wf[8], yf[8];
+          wv[j].unpack(wf);
 #pragma unroll
-          for (int e = 0; e < 8; ++e) o.set(e, __fmul_rn(__fmul_rn(s[j][e], rinv), wv[j].get(e)));
-          o.store(out + row * (int64_t)nvec * 8 + (int64_t)v * 8);
+          for (int e = 0; e < 8; ++e) yf[e] = __fmul_rn(__fmul_rn(s[j][e], rinv), wf[e]);
+          Vec8<T> o;
+          o.pack(yf);
+          o.store(orow + (int64_t)v * 8);
         }
       }
       continue;
     }
-    float amax = 0.0f;
+    float amax = 0.0f, amin = __int_as_float(0x7f800000);
 #pragma unroll
     for (int j = 0; j < VPT; ++j) {
-      const int v = tid + j * blockDim.x;
+      const int v = tid + j * nthr;
       if (v < nvec) {
-        if (out) {
+        if (orow) {
           Vec8<T> o;
-#pragma unroll
-          for (int e = 0; e < 8; ++e) o.set(e, s[j][e]);
-          o.store(out + row * (int64_t)nvec * 8 + (int64_t)v * 8);
+          o.pack(s[j]);
+          o.store(orow + (int64_t)v * 8);
         }
+        float wf[8];
+        wv[j].unpack(wf);
 #pragma unroll
         for (int e = 0; e < 8; ++e) {
-          s[j][e] = __fmul_rn(__fmul_rn(s[j][e], rinv), wv[j].get(e));
+          s[j][e] = __fmul_rn(__fmul_rn(s[j][e], rinv), wf[e]);
           amax = fmaxf(amax, fabsf(s[j][e]));
+          amin = fminf(amin, fabsf(s[j][e]));
         }
       }
     }
@@ -292,25 +327,12 @@ __global__ void __launch_bounds__(256) add_rmsnorm_pipe_kernel(const T* __restri
     const float scale = fmaxf(__fdiv_rn(amax, qmax), kMinScalingFactor);
     const Divisor dv = make_divisor(scale);
     uint2* crow = reinterpret_cast<uint2*>(codes + row * (int64_t)nvec * 8);
-#pragma unroll
-    for (int j = 0; j < VPT; ++j) {
-      const int v = tid + j * blockDim.x;
-      if (v < nvec) {
-        uint32_t lo, hi;
-        if (MODE == kQuantE4m3) {
-          lo = quant_e4m3x2(s[j][0], s[j][1], dv) | ((uint32_t)quant_e4m3x2(s[j][2], s[j][3], dv) << 16);
-          hi = quant_e4m3x2(s[j][4], s[j][5], dv) | ((uint32_t)quant_e4m3x2(s[j][6], s[j][7], dv) << 16);
-        } else {
-          lo = hi = 0;
-#pragma unroll
-          for (int e = 0; e < 4; ++e) {
-            lo |= (uint32_t)(uint8_t)quant_int8(s[j][e], dv) << (8 * e);
-            hi |= (uint32_t)(uint8_t)quant_int8(s[j][4 + e], dv) << (8 * e);
-          }
-        }
-        __stcs(crow + v, make_uint2(lo, hi));
-      }
-    }
+    // One check per thread and row instead of one per element: the FMA-corrected
+    // division is valid for every value this thread holds when the smallest one is.
+    if (amin >= dv.thresh)
+      store_codes<VPT, MODE, false>(s, dv, crow, tid, nthr, nvec);
+    else
+      store_codes<VPT, MODE, true>(s, dv, crow, tid, nthr, nvec);
     if (tid == 0) scales[row] = scale;
   }
   if (failed && tid == 0) {
@@ -331,26 +353,28 @@ struct PipeConfig {
 template <typename T, int VPT, int MODE>
 int launch_pipe(const T* x, const T* r, const T* w, int64_t rows, int64_t nvec, float eps, T* out, uint8_t* codes,
                 float* scales, cudaStream_t st) {
+  const int threads = (int)std::min<int64_t>(512, ((nvec + VPT - 1) / VPT + 31) / 32 * 32);
   const size_t smem = (size_t)kStages * 2 * nvec * 8 * sizeof(T);
-  static int cached_dev = -1, cached_blocks = 0;
+  static int cached_dev = -1, cached_blocks = 0, cached_threads = 0;
   static size_t cached_smem = 0;
   int dev = 0;
   cudaGetDevice(&dev);
   auto kern = add_rmsnorm_pipe_kernel<T, VPT, MODE>;
-  if (dev != cached_dev || smem != cached_smem) {
+  if (dev != cached_dev || smem != cached_smem || threads != cached_threads) {
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     if (e != cudaSuccess) return set_error(KVB_E_LAUNCH, "add_rmsnorm: smem attribute: %s", cudaGetErrorString(e));
     int nb = 0;
-    e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&nb, kern, 256, smem);
+    e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&nb, kern, threads, smem);
     if (e != cudaSuccess || nb < 1) return set_error(KVB_E_LAUNCH, "add_rmsnorm: occupancy query failed");
     cached_dev = dev;
     cached_smem = smem;
+    cached_threads = threads;
     cached_blocks = nb;
   }
   int sms = 0;
   cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
   const int64_t grid = std::min<int64_t>(rows, (int64_t)cached_blocks * sms);
-  kern<<<(unsigned)grid, 256, smem, st>>>(x, r, w, rows, (int)nvec, (float)(nvec * 8), eps, out, codes, scales);
+  kern<<<(unsigned)grid, threads, smem, st>>>(x, r, w, rows, (int)nvec, (float)(nvec * 8), eps, out, codes, scales);
   return check_launch("add_rmsnorm_pipe_kernel");
 }
 
@@ -382,10 +406,9 @@ int launch(const void* xv, const void* rv, const void* wv, int64_t rows, int64_t
   const int64_t row_bytes = hidden * (int64_t)sizeof(T);
   if (vec && hidden / 8 >= 256 && row_bytes <= 24 * 1024) {
     const int64_t nvec = hidden / 8;
-    if (nvec <= 256) return launch_pipe<T, 1, MODE>(x, r, w, rows, nvec, eps, out, codes, scales, st);
-    if (nvec <= 512) return launch_pipe<T, 2, MODE>(x, r, w, rows, nvec, eps, out, codes, scales, st);
-    if (nvec <= 1024) return launch_pipe<T, 4, MODE>(x, r, w, rows, nvec, eps, out, codes, scales, st);
-    return launch_pipe<T, 6, MODE>(x, r, w, rows, nvec, eps, out, codes, scales, st);
+    if (nvec <= 512) return launch_pipe<T, 1, MODE>(x, r, w, rows, nvec, eps, out, codes, scales, st);
+    if (nvec <= 1024) return launch_pipe<T, 2, MODE>(x, r, w, rows, nvec, eps, out, codes, scales, st);
+    return launch_pipe<T, 3, MODE>(x, r, w, rows, nvec, eps, out, codes, scales, st);
   }
   if (vec) {
     const int64_t nvec = hidden / 8;
