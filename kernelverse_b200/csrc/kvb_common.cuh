@@ -156,6 +156,26 @@ __device__ __forceinline__ float block_reduce(float v, float* scratch) {
   return r;
 }
 
+// Warp max of non-negative floats with the sm_100a redux instruction (one instruction).
+__device__ __forceinline__ float warp_max_redux(float v) {
+  float r;
+  asm volatile("redux.sync.max.f32 %0, %1, 0xffffffff;" : "=f"(r) : "f"(v));
+  return r;
+}
+
+// Block reduction with a single barrier.  `buf` (>= 32 floats) must differ from the
+// buffer of the previous reduction of the block: that reduction's barrier then already
+// guarantees its buffer has been read, so consecutive reductions alternate two buffers.
+template <bool kMax>
+__device__ __forceinline__ float block_reduce_1bar(float v, float* buf) {
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nwarps = (blockDim.x + 31) >> 5;
+  v = kMax ? warp_max_redux(v) : warp_sum(v);
+  if (lane == 0) buf[warp] = v;
+  __syncthreads();
+  float r = lane < nwarps ? buf[lane] : 0.0f;
+  return kMax ? warp_max_redux(r) : warp_sum(r);
+}
+
 // ------------------------------------------------------------------ quantisation primitives
 // Correctly rounded a / b from a precomputed y = RN(1/b), by Markstein's method
 // (P. Markstein, "IA-64 and Elementary Functions", 2000, Thm. 8.10): with y the

@@ -214,7 +214,7 @@ __global__ void __launch_bounds__(512) add_rmsnorm_pipe_kernel(const T* __restri
                                                                uint8_t* __restrict__ codes, float* __restrict__ scales) {
   extern __shared__ __align__(128) uint8_t smem[];
   __shared__ uint64_t full[kStages];
-  __shared__ float scratch[32];
+  __shared__ float red_sum[32], red_max[32];   // alternating buffers of the two reductions
   const uint32_t row_bytes = (uint32_t)nvec * 8u * (uint32_t)sizeof(T);
   const int64_t G = gridDim.x;
   const int tid = threadIdx.x;
@@ -234,11 +234,18 @@ __global__ void __launch_bounds__(512) add_rmsnorm_pipe_kernel(const T* __restri
       if (row < rows) issue_row(x, res, row, nvec, smem + s * 2 * row_bytes, row_bytes, &full[s], pol);
     }
   }
-  Vec8<T> wv[VPT];   // this thread's weight slice, loaded once
+  float wf[VPT][8];   // this thread's weight slice as float32, loaded once per CTA
 #pragma unroll
   for (int j = 0; j < VPT; ++j) {
     const int v = tid + j * nthr;
-    if (v < nvec) wv[j].load(w + (int64_t)v * 8);
+    Vec8<T> t;
+    if (v < nvec) {
+      t.load(w + (int64_t)v * 8);
+      t.unpack(wf[j]);
+    } else {
+#pragma unroll
+      for (int e = 0; e < 8; ++e) wf[j][e] = 0.0f;
+    }
   }
 
   int k = 0;
@@ -278,7 +285,7 @@ __global__ void __launch_bounds__(512) add_rmsnorm_pipe_kernel(const T* __restri
         for (int e = 0; e < 8; ++e) s[j][e] = 0.0f;
       }
     }
-    ss = block_reduce<false>(ss, scratch);     // after this every thread has finished reading stage st
+    ss = block_reduce_1bar<false>(ss, red_sum);   // after this every thread has finished reading stage st
     if (tid == 0) {
       const int64_t next = row + kStages * G;
       if (next < rows) issue_row(x, res, next, nvec, smem + st * 2 * row_bytes, row_bytes, &full[st], pol);
@@ -291,10 +298,9 @@ __global__ void __launch_bounds__(512) add_rmsnorm_pipe_kernel(const T* __restri
       for (int j = 0; j < VPT; ++j) {
         const int v = tid + j * nthr;
         if (v < nvec) {
-          float wf[8], yf[8];
-          wv[j].unpack(wf);
+          float yf[8];
 #pragma unroll
-          for (int e = 0; e < 8; ++e) yf[e] = __fmul_rn(__fmul_rn(s[j][e], rinv), wf[e]);
+          for (int e = 0; e < 8; ++e) yf[e] = __fmul_rn(__fmul_rn(s[j][e], rinv), wf[j][e]);
           Vec8<T> o;
           o.pack(yf);
           o.store(orow + (int64_t)v * 8);
@@ -312,17 +318,15 @@ __global__ void __launch_bounds__(512) add_rmsnorm_pipe_kernel(const T* __restri
           o.pack(s[j]);
           o.store(orow + (int64_t)v * 8);
         }
-        float wf[8];
-        wv[j].unpack(wf);
 #pragma unroll
         for (int e = 0; e < 8; ++e) {
-          s[j][e] = __fmul_rn(__fmul_rn(s[j][e], rinv), wf[e]);
+          s[j][e] = __fmul_rn(__fmul_rn(s[j][e], rinv), wf[j][e]);
           amax = fmaxf(amax, fabsf(s[j][e]));
           amin = fminf(amin, fabsf(s[j][e]));
         }
       }
     }
-    amax = block_reduce<true>(amax, scratch);
+    amax = block_reduce_1bar<true>(amax, red_max);
     const float qmax = MODE == kQuantE4m3 ? kE4m3Max : kInt8Max;
     const float scale = fmaxf(__fdiv_rn(amax, qmax), kMinScalingFactor);
     const Divisor dv = make_divisor(scale);
