@@ -124,6 +124,69 @@ KVB_API int kvb_add_rmsnorm_quant(const void* x, const void* residual, const voi
                           int64_t rows, int64_t hidden, float eps, void* residual_out,
                           void* codes, int code_dtype, float* scales, void* stream);
 
+/* ---------------------------------------------------------------- paged KV-cache writes */
+
+/*
+ * Replaces operators/kv_cache/paged_kv_cache_update/paged_kv_cache_update.py:21-31:
+ * kv_cache_out = copy of kv_cache_in (skipped when kv_cache_in is NULL or equal to
+ * kv_cache_out), then for every token i with slot_mapping[i] >= 0, flat slot
+ * slot_mapping[i] of kv_cache_out ([num_slots, slot_elems], num_slots = blocks * block_size)
+ * receives to_cache[i] ([num_tokens, slot_elems]).  All of `dtype`; slot_mapping is
+ * KVB_I32 or KVB_I64.  Slots >= num_slots are skipped and flagged in kvb_device_status.
+ */
+KVB_API int kvb_paged_kv_cache_update(const void* to_cache, const void* kv_cache_in, void* kv_cache_out,
+                                      const void* slot_mapping, int index_dtype, int dtype, int64_t num_tokens,
+                                      int64_t num_slots, int64_t slot_elems, void* stream);
+
+/*
+ * FP8 paged KV write (BASELINE fourth config; slot placement as paged_kv_cache_update.py:27-30):
+ * cache[slot_mapping[i], h, :] = e4m3(clamp(x_new[i, h, :] / head_scales[h], +-448)).
+ * x_new [num_tokens, num_heads, head_dim] (x_dtype); cache [num_slots, num_heads, head_dim]
+ * e4m3 codes; negative slots are skipped.
+ */
+KVB_API int kvb_paged_fp8_kv_write(const void* x_new, int x_dtype, void* cache, const void* slot_mapping,
+                                   int index_dtype, const float* head_scales, int64_t num_tokens, int64_t num_slots,
+                                   int num_heads, int head_dim, void* stream);
+
+/* ---------------------------------------------------------------- paged decode attention */
+
+/* Bytes of workspace kvb_paged_attention needs (float32 split-KV partials). */
+KVB_API size_t kvb_paged_attention_workspace_size(int batch, int num_q_heads, int head_dim, int max_partitions);
+
+/*
+ * GQA decode attention over a paged KV cache, split over partitions of the sequence.
+ * Replaces operators/attention/paged_attention_v1/paged_attention_v1.py:27-92 and, with the
+ * v2 outputs, operators/attention/paged_attention_v2/paged_attention_v2.py:28-175.
+ *
+ * query [B, Hq, D] (q_dtype); key_cache / value_cache [num_blocks, block_size, Hkv, D] of
+ * cache_dtype (KVB_E4M3 with per-KV-head float32 k_scale / v_scale [Hkv], or KVB_F16 /
+ * KVB_BF16 with NULL scales): token t of sequence b is row t % block_size of block
+ * block_table[b * bt_stride + t / block_size] -- the memory order in which the reference
+ * gathers and reshapes its cache (paged_attention_v1.py:64-69).  block_table == NULL means
+ * block b holds all of sequence b (dense [B, L, Hkv, D] caches,
+ * operators/attention/batched_decode_attention/batched_decode_attention.py:30-52).
+ * seq_lens [B] (KVB_I32 / KVB_I64); max_seq_len >= every seq_len (sizes the grid).
+ * out[b, h] = softmax(K q * sm_scale) V with q-head h reading KV head h / (Hq / Hkv).
+ *
+ * k_new / v_new [B, Hkv, D] (new_dtype, optional, e4m3 caches only): each sequence's newest
+ * token (position seq_len - 1) is first quantised (e4m3(clamp(x / scale[h]))) and written
+ * to its slot, and the attention uses the written codes.
+ * partition_size: tokens per split-KV partition (multiple of 16; 0 = 256).
+ * exp_sums, max_logits [B, Hq, max_partitions] and tmp_out [B, Hq, max_partitions, D]
+ * (out_dtype, optional, all or none): the v2 partition outputs; then out uses the v2
+ * normalisation (global_sum + 1e-6) and max_partitions must equal
+ * ceil(max_seq_len / partition_size).
+ * D in {64, 128}; block_size divides 16 or is a multiple of 16; Hkv * ceil(group / 8) <= 16.
+ */
+KVB_API int kvb_paged_attention(const void* query, int q_dtype, const void* key_cache, const void* value_cache,
+                                int cache_dtype, const float* k_scale, const float* v_scale, const void* seq_lens,
+                                int seq_lens_dtype, const int32_t* block_table, int64_t bt_stride, int batch,
+                                int num_q_heads, int num_kv_heads, int head_dim, int block_size, int64_t num_blocks,
+                                int64_t max_seq_len, float sm_scale, const void* k_new, const void* v_new,
+                                int new_dtype, int partition_size, void* out, int out_dtype, void* exp_sums,
+                                void* max_logits, void* tmp_out, int max_partitions, void* workspace,
+                                size_t workspace_bytes, void* stream);
+
 #ifdef __cplusplus
 }  /* extern "C" */
 #endif

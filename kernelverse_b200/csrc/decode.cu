@@ -1,0 +1,695 @@
+// Paged GQA decode attention (split-KV) over an e4m3, fp16 or bf16 KV cache, with an
+// optional fused write of each sequence's newest token into an e4m3 cache.
+//
+// Cache layout: [num_blocks, block_size, Hkv, D] -- the memory order the reference's
+// paged_attention_v1/v2 read (their reshape(-1, Hkv, D) of a gathered block) and
+// paged_kv_cache_update writes.  A 16-token chunk of one sequence is therefore 16 rows of
+// Hkv*D elements, contiguous inside a block (16 KB for e4m3, Hkv=8, D=128).
+//
+// One CTA = one (sequence, partition of `part` tokens).  A producer warp streams 16-token
+// chunks of K and V (all heads) into a `kStages`-deep shared-memory ring with 1-D bulk
+// copies (cp.async.bulk, mbarrier completion); consumer warps each own one KV head and up
+// to 8 query heads of its GQA group:
+//   S^T[16 tok x 8 heads] = K[16 x D] . Q^T[D x 8]     (mma.sync m16n8k16, f32 accumulate)
+//   online softmax in the log2 domain (scale folded with log2(e) and the e4m3 K scale)
+//   O^T[D x 8] += V^T[D x 16 tok] . P^T[16 tok x 8]     (mma.sync m16n8k16)
+// e4m3 codes become f16 pairs in registers (cvt.rn.f16x2.e4m3x2).  Because a dot product
+// and the sum over tokens do not depend on the order of their terms, the head dimension is
+// permuted so every thread reads one contiguous run of a K row (D/4 elements) and of a V
+// row (D/8 elements); Q and the output use the same permutations.  Partials (max, sum,
+// unnormalised output per partition) go to a float32 workspace and a merge kernel
+// combines them (paged_attention_v2.py:163-173); when asked, the v2 partition outputs
+// (exp_sums, max_logits, tmp_out = weighted / (exp_sum + 1e-6)) are written as well.
+#include <cmath>
+
+#include "kvb_common.cuh"
+#include "kvb_async.cuh"
+
+namespace kvb {
+namespace {
+
+constexpr int kChunk = 16;
+constexpr int kStagesMax = 4;
+constexpr float kLog2e = 1.4426950408889634f;
+constexpr float kLn2 = 0.6931471805599453f;
+constexpr unsigned int kStatusBadIndex = 2u;   // a block-table entry outside [0, num_blocks)
+
+template <typename KT> struct CacheTraits;
+template <> struct CacheTraits<uint8_t> { static constexpr int kBytes = 1; static constexpr bool kBf16 = false; };
+template <> struct CacheTraits<__half> { static constexpr int kBytes = 2; static constexpr bool kBf16 = false; };
+template <> struct CacheTraits<__nv_bfloat16> { static constexpr int kBytes = 2; static constexpr bool kBf16 = true; };
+
+__device__ __forceinline__ void mma16816(float (&d)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1, bool bf16) {
+  if (bf16) {
+    asm volatile(
+        "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+        "{%0,%1,%2,%3};"
+        : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+        : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+  } else {
+    asm volatile(
+        "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+        "{%0,%1,%2,%3};"
+        : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+        : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+  }
+}
+
+__device__ __forceinline__ uint32_t e4m3x2_to_f16x2(uint32_t lo16) {
+  uint32_t r;
+  const uint16_t v = (uint16_t)lo16;
+  asm("cvt.rn.f16x2.e4m3x2 %0, %1;" : "=r"(r) : "h"(v));
+  return r;
+}
+
+__device__ __forceinline__ uint32_t prmt(uint32_t a, uint32_t b, uint32_t sel) {
+  uint32_t r;
+  asm("prmt.b32 %0, %1, %2, %3;" : "=r"(r) : "r"(a), "r"(b), "r"(sel));
+  return r;
+}
+
+__device__ __forceinline__ uint32_t pack2(float lo, float hi, bool bf16) {
+  if (bf16) {
+    __nv_bfloat162 h = __floats2bfloat162_rn(lo, hi);
+    return *reinterpret_cast<uint32_t*>(&h);
+  }
+  __half2 h = __floats2half2_rn(lo, hi);
+  return *reinterpret_cast<uint32_t*>(&h);
+}
+
+template <typename T>
+__device__ __forceinline__ float load_f(const T* p, int64_t i) { return Elem<T>::to_f(p[i]); }
+
+__device__ __forceinline__ float ex2(float x) { return exp2f(x); }
+
+struct DecodeArgs {
+  const void* q;            // [B, Hq, D] (q_dtype)
+  const void* k_cache;      // [num_blocks, bs, Hkv, D]
+  const void* v_cache;
+  const float* k_scale;     // [Hkv] (e4m3 caches) or null
+  const float* v_scale;
+  const void* seq_lens;     // [B] int32 or int64
+  const int32_t* block_table;  // [B, bt_stride] or null (block b holds all of sequence b)
+  int64_t bt_stride;
+  int64_t num_blocks;
+  const void* k_new;        // [B, Hkv, D] (new_dtype) or null: fused write of token seq_len-1
+  const void* v_new;
+  float* m_part;            // [B, Hq, P]   (log2-domain max)
+  float* l_part;            // [B, Hq, P]
+  float* o_part;            // [B, Hq, P, D] (unnormalised)
+  void* exp_sums;           // optional v2 outputs [B, Hq, P] / [B, Hq, P, D] (out dtype)
+  void* max_logits;
+  void* tmp_out;
+  float sm_scale;
+  int batch, hq, hkv, group, bs, part, pmax, tiles_per_kv, stages;
+  int q_dtype, new_dtype, sl64, v2_dtype;
+};
+
+__device__ __forceinline__ int64_t seq_len_of(const DecodeArgs& a, int b) {
+  return a.sl64 ? reinterpret_cast<const int64_t*>(a.seq_lens)[b] : (int64_t)reinterpret_cast<const int32_t*>(a.seq_lens)[b];
+}
+
+__device__ __forceinline__ float load_any(const void* p, int dt, int64_t i) {
+  if (dt == KVB_BF16) return load_f(reinterpret_cast<const __nv_bfloat16*>(p), i);
+  if (dt == KVB_F16) return load_f(reinterpret_cast<const __half*>(p), i);
+  return reinterpret_cast<const float*>(p)[i];
+}
+__device__ __forceinline__ void store_any(void* p, int dt, int64_t i, float v) {
+  if (dt == KVB_BF16) reinterpret_cast<__nv_bfloat16*>(p)[i] = __float2bfloat16_rn(v);
+  else if (dt == KVB_F16) reinterpret_cast<__half*>(p)[i] = __float2half_rn(v);
+  else reinterpret_cast<float*>(p)[i] = v;
+}
+
+// Physical row (block * bs + offset) of token t of sequence b; -1 if the table entry is invalid.
+__device__ __forceinline__ int64_t token_row(const DecodeArgs& a, int b, int64_t t) {
+  const int64_t blk = t / a.bs;
+  const int64_t phys = a.block_table ? (int64_t)a.block_table[(int64_t)b * a.bt_stride + blk] : (int64_t)b;
+  if (phys < 0 || phys >= a.num_blocks) return -1;
+  return phys * a.bs + (t - blk * a.bs);
+}
+
+template <typename KT, int D, int MAXT>
+__global__ void __launch_bounds__(MAXT) paged_decode_kernel(const __grid_constant__ DecodeArgs a) {
+  using TR = CacheTraits<KT>;
+  constexpr int EB = TR::kBytes;
+  constexpr bool BF = TR::kBf16;
+  constexpr int KSPAN = D / 4 * EB;     // bytes of a K row one thread reads
+  constexpr int VSPAN = D / 8 * EB;     // bytes of a V row one thread reads
+  constexpr int KW = KSPAN / 4, VW = VSPAN / 4;   // ... in 32-bit words
+  constexpr int SLABS = D / 16;         // mma k-slabs of QK = m-tiles of PV
+
+  extern __shared__ __align__(128) uint8_t smem[];
+  __shared__ uint64_t full[kStagesMax], empty[kStagesMax];
+
+  const int p = blockIdx.x, b = blockIdx.y;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int ncons = a.hkv * a.tiles_per_kv;          // consumer warps; warp ncons is the producer
+  const int64_t L = seq_len_of(a, b);
+  const int64_t t_begin = (int64_t)p * a.part;
+  const int64_t t_end = (L < t_begin + a.part ? L : t_begin + a.part);
+  const int D_ = D;
+
+  if (t_begin >= L) {
+    // Partition past this sequence's end: v2 outputs hold exp_sum 0, max -inf, tmp_out 0.
+    if (a.exp_sums) {
+      for (int i = threadIdx.x; i < a.hq; i += blockDim.x) {
+        const int64_t o = ((int64_t)b * a.hq + i) * a.pmax + p;
+        store_any(a.exp_sums, a.v2_dtype, o, 0.0f);
+        store_any(a.max_logits, a.v2_dtype, o, -INFINITY);
+      }
+      for (int i = threadIdx.x; i < a.hq * D_; i += blockDim.x) {
+        const int h = i / D_, d = i % D_;
+        store_any(a.tmp_out, a.v2_dtype, (((int64_t)b * a.hq + h) * a.pmax + p) * D_ + d, 0.0f);
+      }
+    }
+    return;
+  }
+  const int nchunks = (int)((t_end - t_begin + kChunk - 1) / kChunk);
+  const uint32_t row_bytes = (uint32_t)(a.hkv * D * EB);
+  const uint32_t chunk_bytes = kChunk * row_bytes;
+  const int S = a.stages;
+  auto kstage = [&](int s) { return smem + (size_t)s * 2 * chunk_bytes; };
+  auto vstage = [&](int s) { return smem + (size_t)s * 2 * chunk_bytes + chunk_bytes; };
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < S; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], ncons);
+    }
+    fence_mbar_init();
+  }
+  __syncthreads();
+
+  // ------------------------------------------------------------------ producer warp
+  if (warp == ncons) {
+    if (lane == 0) {
+      const uint64_t pol = policy_evict_first();
+      const uint8_t* kc = reinterpret_cast<const uint8_t*>(a.k_cache);
+      const uint8_t* vc = reinterpret_cast<const uint8_t*>(a.v_cache);
+      const int pieces = a.bs >= kChunk ? 1 : kChunk / a.bs;      // bs divides 16 or 16 divides bs
+      const int rows_per_piece = a.bs >= kChunk ? kChunk : a.bs;
+      for (int i = 0; i < nchunks; ++i) {
+        const int s = i % S;
+        if (i >= S && !mbar_wait_bounded(&empty[s], (uint32_t)((i / S) - 1) & 1u)) break;
+        const int64_t t0 = t_begin + (int64_t)i * kChunk;
+        // Count the bytes first (pieces wholly past the end of the sequence are not copied).
+        uint32_t bytes = 0;
+        for (int pc = 0; pc < pieces; ++pc)
+          if (t0 + (int64_t)pc * rows_per_piece < L) bytes += 2u * rows_per_piece * row_bytes;
+        mbar_arrive_expect_tx(&full[s], bytes);
+        for (int pc = 0; pc < pieces; ++pc) {
+          const int64_t t = t0 + (int64_t)pc * rows_per_piece;
+          if (t >= L) continue;
+          const int64_t row = token_row(a, b, t);
+          const uint32_t nb = rows_per_piece * row_bytes;
+          uint8_t* kd = kstage(s) + (size_t)pc * nb;
+          uint8_t* vd = vstage(s) + (size_t)pc * nb;
+          if (row < 0) {   // invalid block index: record it and complete the transaction without a copy
+            atomicOr(&g_tu_status, kStatusBadIndex);
+            asm volatile("mbarrier.complete_tx.relaxed.cta.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(&full[s])),
+                         "r"(2 * nb) : "memory");
+            continue;
+          }
+          bulk_g2s(kd, kc + row * row_bytes, nb, &full[s], pol);
+          bulk_g2s(vd, vc + row * row_bytes, nb, &full[s], pol);
+        }
+      }
+      // Wait (bounded) until the consumers are done with every stage before the CTA exits.
+      for (int i = max(0, nchunks - S); i < nchunks; ++i) mbar_wait_bounded(&empty[i % S], (uint32_t)(i / S) & 1u);
+    }
+    return;
+  }
+  if (warp > ncons) return;
+
+  // ------------------------------------------------------------------ consumer warps
+  const int g = lane >> 2, c = lane & 3;
+  const int kvh = warp / a.tiles_per_kv, nt = warp % a.tiles_per_kv;
+  const int qn = nt * 8 + g;                         // this lane's query head within the group (B operand col)
+  const bool qvalid = qn < a.group;
+  const int qhead = kvh * a.group + qn;
+  // Q as the B operand of QK, permuted: slab j, regs (b0, b1) = dims (D/4)c + 4j + {0,1 | 2,3}.
+  uint32_t qf[SLABS][2];
+#pragma unroll
+  for (int j = 0; j < SLABS; ++j) {
+    float q4[4];
+#pragma unroll
+    for (int e = 0; e < 4; ++e)
+      q4[e] = qvalid ? load_any(a.q, a.q_dtype, ((int64_t)b * a.hq + qhead) * D + (D / 4) * c + 4 * j + e) : 0.0f;
+    qf[j][0] = pack2(q4[0], q4[1], BF);
+    qf[j][1] = pack2(q4[2], q4[3], BF);
+  }
+  const float ksc = a.k_scale ? a.k_scale[kvh] : 1.0f;
+  const float vsc = a.v_scale ? a.v_scale[kvh] : 1.0f;
+  const float qk_scale = a.sm_scale * kLog2e * ksc;
+
+  float o[SLABS][4];
+#pragma unroll
+  for (int t = 0; t < SLABS; ++t) o[t][0] = o[t][1] = o[t][2] = o[t][3] = 0.0f;
+  float m0 = -INFINITY, m1 = -INFINITY, l0 = 0.0f, l1 = 0.0f;   // heads 2c, 2c+1 (log2 domain)
+  const int64_t new_tok = a.k_new ? L - 1 : -1;
+
+  bool failed = false;
+  for (int i = 0; i < nchunks; ++i) {
+    const int s = i % S;
+    if (!mbar_wait_bounded(&full[s], (uint32_t)(i / S) & 1u)) {
+      failed = true;
+      break;
+    }
+    const int64_t t0 = t_begin + (int64_t)i * kChunk;
+    uint8_t* ks = kstage(s);
+    uint8_t* vs = vstage(s);
+    if (new_tok >= t0 && new_tok < t0 + kChunk) {
+      // Fused KV write: quantise this head's new K/V, patch the staged row and write the slot.
+      if constexpr (EB == 1) {
+        const int r = (int)(new_tok - t0);
+        const int64_t row = token_row(a, b, new_tok);
+        for (int d = lane * 2; d < D; d += 64) {
+          const int64_t src = ((int64_t)b * a.hkv + kvh) * D + d;
+          const uint16_t kc2 = quant_e4m3x2(load_any(a.k_new, a.new_dtype, src), load_any(a.k_new, a.new_dtype, src + 1),
+                                            make_divisor(ksc));
+          const uint16_t vc2 = quant_e4m3x2(load_any(a.v_new, a.new_dtype, src), load_any(a.v_new, a.new_dtype, src + 1),
+                                            make_divisor(vsc));
+          const size_t off = (size_t)r * row_bytes + (size_t)kvh * D + d;
+          *reinterpret_cast<uint16_t*>(ks + off) = kc2;
+          *reinterpret_cast<uint16_t*>(vs + off) = vc2;
+          if (nt == 0 && row >= 0) {
+            *reinterpret_cast<uint16_t*>(reinterpret_cast<uint8_t*>(const_cast<void*>(a.k_cache)) + row * row_bytes +
+                                         (int64_t)kvh * D + d) = kc2;
+            *reinterpret_cast<uint16_t*>(reinterpret_cast<uint8_t*>(const_cast<void*>(a.v_cache)) + row * row_bytes +
+                                         (int64_t)kvh * D + d) = vc2;
+          }
+        }
+        __syncwarp();
+      }
+    }
+    // ---- S^T = K . Q^T for tokens g and g+8
+    const int nvalid = (int)(t_end - t0 < kChunk ? t_end - t0 : kChunk);
+    uint32_t kw0[KW], kw1[KW];
+    {
+      const uint8_t* r0 = ks + (size_t)g * row_bytes + (size_t)kvh * D * EB + c * KSPAN;
+      const uint8_t* r1 = r0 + 8 * (size_t)row_bytes;
+      if constexpr (KW == 8) {
+        // Two 16-byte halves per row: lanes of odd g load them in the opposite order, so the
+        // eight lanes of a quarter-warp hit eight different bank groups; selects undo the swap.
+        const int sw = (g & 1) * 16;
+        const uint4 a0 = *reinterpret_cast<const uint4*>(r0 + sw), a1 = *reinterpret_cast<const uint4*>(r0 + 16 - sw);
+        const uint4 b0 = *reinterpret_cast<const uint4*>(r1 + sw), b1 = *reinterpret_cast<const uint4*>(r1 + 16 - sw);
+        const bool odd = g & 1;
+        const uint4 lo0 = odd ? a1 : a0, hi0 = odd ? a0 : a1, lo1 = odd ? b1 : b0, hi1 = odd ? b0 : b1;
+        kw0[0] = lo0.x; kw0[1] = lo0.y; kw0[2] = lo0.z; kw0[3] = lo0.w;
+        kw0[4] = hi0.x; kw0[5] = hi0.y; kw0[6] = hi0.z; kw0[7] = hi0.w;
+        kw1[0] = lo1.x; kw1[1] = lo1.y; kw1[2] = lo1.z; kw1[3] = lo1.w;
+        kw1[4] = hi1.x; kw1[5] = hi1.y; kw1[6] = hi1.z; kw1[7] = hi1.w;
+      } else {
+#pragma unroll
+        for (int u = 0; u < KW / 4; ++u) {
+          const uint4 x0 = *reinterpret_cast<const uint4*>(r0 + 16 * u);
+          const uint4 x1 = *reinterpret_cast<const uint4*>(r1 + 16 * u);
+          kw0[4 * u] = x0.x; kw0[4 * u + 1] = x0.y; kw0[4 * u + 2] = x0.z; kw0[4 * u + 3] = x0.w;
+          kw1[4 * u] = x1.x; kw1[4 * u + 1] = x1.y; kw1[4 * u + 2] = x1.z; kw1[4 * u + 3] = x1.w;
+        }
+      }
+    }
+    float sacc[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+#pragma unroll
+    for (int j = 0; j < SLABS; ++j) {
+      uint32_t af[4];
+      if constexpr (EB == 1) {
+        af[0] = e4m3x2_to_f16x2(kw0[j] & 0xffffu);
+        af[1] = e4m3x2_to_f16x2(kw1[j] & 0xffffu);
+        af[2] = e4m3x2_to_f16x2(kw0[j] >> 16);
+        af[3] = e4m3x2_to_f16x2(kw1[j] >> 16);
+      } else {
+        af[0] = kw0[2 * j];
+        af[1] = kw1[2 * j];
+        af[2] = kw0[2 * j + 1];
+        af[3] = kw1[2 * j + 1];
+      }
+      mma16816(sacc, af, qf[j][0], qf[j][1], BF);
+    }
+    // ---- online softmax; sacc = {tok g: head 2c, 2c+1; tok g+8: head 2c, 2c+1}
+    float sv[4];
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      const int tok = g + (e >= 2 ? 8 : 0);
+      sv[e] = tok < nvalid ? sacc[e] * qk_scale : -INFINITY;
+    }
+    float mx0 = fmaxf(sv[0], sv[2]), mx1 = fmaxf(sv[1], sv[3]);
+#pragma unroll
+    for (int off = 4; off < 32; off <<= 1) {
+      mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, off));
+      mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, off));
+    }
+    const float mn0 = fmaxf(m0, mx0), mn1 = fmaxf(m1, mx1);
+    const float mu0 = mn0 == -INFINITY ? 0.0f : mn0, mu1 = mn1 == -INFINITY ? 0.0f : mn1;
+    const float al0 = ex2(m0 - mu0), al1 = ex2(m1 - mu1);
+    const float p0 = ex2(sv[0] - mu0), p1 = ex2(sv[1] - mu1), p2 = ex2(sv[2] - mu0), p3 = ex2(sv[3] - mu1);
+    l0 = l0 * al0 + (p0 + p2);
+    l1 = l1 * al1 + (p1 + p3);
+    m0 = mn0;
+    m1 = mn1;
+#pragma unroll
+    for (int t = 0; t < SLABS; ++t) {
+      o[t][0] *= al0;
+      o[t][2] *= al0;
+      o[t][1] *= al1;
+      o[t][3] *= al1;
+    }
+    // ---- P^T as the B operand: lane (g, c) needs head g, tokens {2c, 2c+1 | 2c+8, 2c+9}
+    uint32_t pb0, pb1;
+    {
+      const uint32_t pe = pack2(p0, p2, BF);     // head 2c:   tokens g, g+8
+      const uint32_t po = pack2(p1, p3, BF);     // head 2c+1: tokens g, g+8
+      const int srcA = 8 * c + (g >> 1), srcB = srcA + 4;
+      const uint32_t aE = __shfl_sync(0xffffffffu, pe, srcA), aO = __shfl_sync(0xffffffffu, po, srcA);
+      const uint32_t bE = __shfl_sync(0xffffffffu, pe, srcB), bO = __shfl_sync(0xffffffffu, po, srcB);
+      const uint32_t A = (g & 1) ? aO : aE, B = (g & 1) ? bO : bE;
+      pb0 = qvalid ? prmt(A, B, 0x5410) : 0u;
+      pb1 = qvalid ? prmt(A, B, 0x7632) : 0u;
+    }
+    // ---- O^T += V^T . P^T; this lane reads V rows 2c, 2c+1, 2c+8, 2c+9 at dims [(D/8)g, +D/8)
+    uint32_t vw[4][VW];
+    {
+      const int toks[4] = {2 * c, 2 * c + 1, 2 * c + 8, 2 * c + 9};
+#pragma unroll
+      for (int rr = 0; rr < 4; ++rr) {
+        const uint8_t* src = vs + (size_t)toks[rr] * row_bytes + (size_t)kvh * D * EB + g * VSPAN;
+        const bool ok = toks[rr] < nvalid;
+#pragma unroll
+        for (int u = 0; u < VW / 4; ++u) {
+          uint4 x = *reinterpret_cast<const uint4*>(src + 16 * u);
+          if (!ok) x = make_uint4(0, 0, 0, 0);
+          vw[rr][4 * u] = x.x; vw[rr][4 * u + 1] = x.y; vw[rr][4 * u + 2] = x.z; vw[rr][4 * u + 3] = x.w;
+        }
+        if constexpr (VW % 4 != 0) {     // 8-byte spans (e4m3, D = 64)
+          uint2 x = *reinterpret_cast<const uint2*>(src);
+          if (!ok) x = make_uint2(0, 0);
+          vw[rr][0] = x.x;
+          vw[rr][1] = x.y;
+        }
+      }
+    }
+#pragma unroll
+    for (int t = 0; t < SLABS; ++t) {
+      uint32_t af[4];
+      if constexpr (EB == 1) {
+        const uint32_t sel = (t & 1) ? 0x7362u : 0x5140u;
+        const uint32_t x01 = prmt(vw[0][t >> 1], vw[1][t >> 1], sel);
+        const uint32_t x89 = prmt(vw[2][t >> 1], vw[3][t >> 1], sel);
+        af[0] = e4m3x2_to_f16x2(x01 & 0xffffu);
+        af[1] = e4m3x2_to_f16x2(x01 >> 16);
+        af[2] = e4m3x2_to_f16x2(x89 & 0xffffu);
+        af[3] = e4m3x2_to_f16x2(x89 >> 16);
+      } else {
+        af[0] = prmt(vw[0][t], vw[1][t], 0x5410u);
+        af[1] = prmt(vw[0][t], vw[1][t], 0x7632u);
+        af[2] = prmt(vw[2][t], vw[3][t], 0x5410u);
+        af[3] = prmt(vw[2][t], vw[3][t], 0x7632u);
+      }
+      mma16816(o[t], af, pb0, pb1, BF);
+    }
+    // release the stage (shared-memory writes of the fused path are ordered before the next bulk copy)
+    if (EB == 1 && new_tok >= t0 && new_tok < t0 + kChunk) asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+    __syncwarp();
+    if (lane == 0) mbar_arrive(&empty[s]);
+  }
+  if (failed) return;
+
+  // ---- reduce the row sums over the 8 lanes that share c, write the partials
+#pragma unroll
+  for (int off = 4; off < 32; off <<= 1) {
+    l0 += __shfl_xor_sync(0xffffffffu, l0, off);
+    l1 += __shfl_xor_sync(0xffffffffu, l1, off);
+  }
+#pragma unroll
+  for (int e = 0; e < 2; ++e) {
+    const int hn = nt * 8 + 2 * c + e;
+    if (hn >= a.group) continue;
+    const int h = kvh * a.group + hn;
+    const float m = e ? m1 : m0, l = e ? l1 : l0;
+    const int64_t pi = ((int64_t)b * a.hq + h) * a.pmax + p;
+    if (g == 0) {
+      a.m_part[pi] = m;
+      a.l_part[pi] = l;
+    }
+    float* op = a.o_part + pi * D;
+    const float sv_scale = vsc;   // V codes were used unscaled: apply the per-head V scale here
+#pragma unroll
+    for (int t = 0; t < SLABS; t += 2) {
+      const int d = (D / 8) * g + 2 * t;
+      float4 v4 = make_float4(o[t][e] * sv_scale, o[t][2 + e] * sv_scale, o[t + 1][e] * sv_scale,
+                              o[t + 1][2 + e] * sv_scale);
+      *reinterpret_cast<float4*>(op + d) = v4;
+    }
+    if (a.exp_sums) {
+      if (g == 0) {
+        store_any(a.exp_sums, a.v2_dtype, pi, l);
+        store_any(a.max_logits, a.v2_dtype, pi, m * kLn2);
+      }
+      const float inv = 1.0f / (l + 1e-6f);
+#pragma unroll
+      for (int t = 0; t < SLABS; ++t) {
+        const int d = (D / 8) * g + 2 * t;
+        store_any(a.tmp_out, a.v2_dtype, pi * D + d, o[t][e] * sv_scale * inv);
+        store_any(a.tmp_out, a.v2_dtype, pi * D + d + 1, o[t][2 + e] * sv_scale * inv);
+      }
+    }
+  }
+}
+
+// float32 caches: exact float32 arithmetic on CUDA cores (the reference's float32 tolerance,
+// rtol = atol = 5e-4, is tighter than f16/tf32 tensor-core inputs allow).  One CTA = one
+// (query head, sequence, partition); logits live in shared memory; the output loop runs one
+// thread per head dimension so V rows are read coalesced.
+__global__ void __launch_bounds__(128) paged_decode_f32_kernel(const __grid_constant__ DecodeArgs a, int D) {
+  extern __shared__ __align__(16) float fsm[];   // q [D] | logits [part] | rows [part] (int64)
+  __shared__ float red[32];
+  const int p = blockIdx.x, b = blockIdx.y, h = blockIdx.z;
+  const int kvh = h / a.group;
+  const int64_t L = seq_len_of(a, b);
+  const int64_t t_begin = (int64_t)p * a.part;
+  const int64_t pi = ((int64_t)b * a.hq + h) * a.pmax + p;
+  if (t_begin >= L) {
+    if (a.exp_sums) {
+      if (threadIdx.x == 0) {
+        store_any(a.exp_sums, a.v2_dtype, pi, 0.0f);
+        store_any(a.max_logits, a.v2_dtype, pi, -INFINITY);
+      }
+      for (int d = threadIdx.x; d < D; d += blockDim.x) store_any(a.tmp_out, a.v2_dtype, pi * D + d, 0.0f);
+    }
+    return;
+  }
+  const int64_t t_end = L < t_begin + a.part ? L : t_begin + a.part;
+  const int n = (int)(t_end - t_begin);
+  float* qs = fsm;
+  float* lg = fsm + D;
+  int64_t* rows = reinterpret_cast<int64_t*>(fsm + D + a.part);
+  for (int d = threadIdx.x; d < D; d += blockDim.x) qs[d] = load_any(a.q, a.q_dtype, ((int64_t)b * a.hq + h) * D + d);
+  __syncthreads();
+  const float* kc = reinterpret_cast<const float*>(a.k_cache);
+  const float* vc = reinterpret_cast<const float*>(a.v_cache);
+  const int64_t rowe = (int64_t)a.hkv * D;   // elements per token row
+  float mx = -INFINITY;
+  for (int i = threadIdx.x; i < n; i += blockDim.x) {
+    const int64_t row = token_row(a, b, t_begin + i);
+    rows[i] = row;
+    float acc = 0.0f;
+    if (row >= 0) {
+      const float4* kr = reinterpret_cast<const float4*>(kc + row * rowe + (int64_t)kvh * D);
+      for (int d4 = 0; d4 < D / 4; ++d4) {
+        const float4 kv = kr[d4];
+        acc = fmaf(kv.x, qs[4 * d4], acc);
+        acc = fmaf(kv.y, qs[4 * d4 + 1], acc);
+        acc = fmaf(kv.z, qs[4 * d4 + 2], acc);
+        acc = fmaf(kv.w, qs[4 * d4 + 3], acc);
+      }
+    } else {
+      atomicOr(&g_tu_status, kStatusBadIndex);
+    }
+    const float v = acc * a.sm_scale;
+    lg[i] = v;
+    mx = fmaxf(mx, v);
+  }
+  // block max of possibly negative logits (block_reduce<true> assumes non-negative values)
+  float lmax = warp_max(mx);
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = lmax;
+  __syncthreads();
+  lmax = red[0];
+  for (int w = 1; w < (int)(blockDim.x >> 5); ++w) lmax = fmaxf(lmax, red[w]);
+  float ls = 0.0f;
+  for (int i = threadIdx.x; i < n; i += blockDim.x) {
+    const float e = expf(lg[i] - lmax);
+    lg[i] = e;
+    ls += e;
+  }
+  ls = block_reduce<false>(ls, red);
+  __syncthreads();
+  for (int d = threadIdx.x; d < D; d += blockDim.x) {
+    float acc = 0.0f;
+    for (int i = 0; i < n; ++i) {
+      const int64_t row = rows[i];
+      if (row >= 0) acc = fmaf(lg[i], vc[row * rowe + (int64_t)kvh * D + d], acc);
+    }
+    a.o_part[pi * D + d] = acc;
+    if (a.tmp_out) store_any(a.tmp_out, a.v2_dtype, pi * D + d, acc / (ls + 1e-6f));
+  }
+  if (threadIdx.x == 0) {
+    a.m_part[pi] = lmax * kLog2e;
+    a.l_part[pi] = ls;
+    if (a.exp_sums) {
+      store_any(a.exp_sums, a.v2_dtype, pi, ls);
+      store_any(a.max_logits, a.v2_dtype, pi, lmax);
+    }
+  }
+}
+
+// out[b, h, :] = sum_p 2^(m_p - M) o_p / (sum_p 2^(m_p - M) l_p + eps)   (paged_attention_v2.py:163-173)
+__global__ void __launch_bounds__(128) decode_merge_kernel(const float* __restrict__ m_part, const float* __restrict__ l_part,
+                                                           const float* __restrict__ o_part, const void* seq_lens, int sl64,
+                                                           int hq, int D, int part, int pmax, float eps, void* out,
+                                                           int out_dtype) {
+  const int bh = blockIdx.x, b = bh / hq;
+  const int64_t L = sl64 ? reinterpret_cast<const int64_t*>(seq_lens)[b] : (int64_t)reinterpret_cast<const int32_t*>(seq_lens)[b];
+  const int64_t npl = (L + part - 1) / part;
+  const int np = (int)(npl < pmax ? npl : pmax);
+  float M = -INFINITY;
+  for (int p = 0; p < np; ++p) M = fmaxf(M, m_part[(int64_t)bh * pmax + p]);
+  const float Mu = M == -INFINITY ? 0.0f : M;
+  float Ls = 0.0f;
+  for (int p = 0; p < np; ++p) Ls += l_part[(int64_t)bh * pmax + p] * exp2f(m_part[(int64_t)bh * pmax + p] - Mu);
+  const float inv = np > 0 ? 1.0f / (Ls + eps) : 0.0f;
+  for (int d = threadIdx.x; d < D; d += blockDim.x) {
+    float acc = 0.0f;
+    for (int p = 0; p < np; ++p)
+      acc += o_part[((int64_t)bh * pmax + p) * D + d] * exp2f(m_part[(int64_t)bh * pmax + p] - Mu);
+    store_any(out, out_dtype, (int64_t)bh * D + d, acc * inv);
+  }
+}
+
+int sm_count_dev() {
+  int dev = 0, n = 0;
+  cudaGetDevice(&dev);
+  cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
+  return n > 0 ? n : 148;
+}
+
+template <typename KT, int D, int MAXT>
+int launch_decode_t(DecodeArgs& a, size_t smem, cudaStream_t st) {
+  auto kern = paged_decode_kernel<KT, D, MAXT>;
+  static int attr_set_dev = -1;
+  static size_t attr_smem = 0;
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (attr_set_dev != dev || smem > attr_smem) {
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    if (e != cudaSuccess) return set_error(KVB_E_LAUNCH, "paged_attention: smem attribute: %s", cudaGetErrorString(e));
+    attr_set_dev = dev;
+    attr_smem = smem;
+  }
+  const int threads = (a.hkv * a.tiles_per_kv + 1) * 32;
+  dim3 grid(a.pmax, a.batch);
+  kern<<<grid, threads, smem, st>>>(a);
+  return check_launch("paged_decode_kernel");
+}
+
+// Up to 8 consumer warps (+1 producer) get a 288-thread register budget; more use 544.
+template <typename KT, int D>
+int launch_decode(DecodeArgs& a, size_t smem, cudaStream_t st) {
+  if (a.hkv * a.tiles_per_kv <= 8) return launch_decode_t<KT, D, 288>(a, smem, st);
+  return launch_decode_t<KT, D, 544>(a, smem, st);
+}
+
+}  // namespace
+}  // namespace kvb
+
+using namespace kvb;
+
+extern "C" size_t kvb_paged_attention_workspace_size(int batch, int num_q_heads, int head_dim, int max_partitions) {
+  const size_t n = (size_t)batch * num_q_heads * max_partitions;
+  return (n * (size_t)(head_dim + 2)) * sizeof(float) + 256;
+}
+
+extern "C" int kvb_paged_attention(const void* query, int q_dtype, const void* key_cache, const void* value_cache,
+                                   int cache_dtype, const float* k_scale, const float* v_scale, const void* seq_lens,
+                                   int seq_lens_dtype, const int32_t* block_table, int64_t bt_stride, int batch,
+                                   int num_q_heads, int num_kv_heads, int head_dim, int block_size, int64_t num_blocks,
+                                   int64_t max_seq_len, float sm_scale, const void* k_new, const void* v_new,
+                                   int new_dtype, int partition_size, void* out, int out_dtype, void* exp_sums,
+                                   void* max_logits, void* tmp_out, int max_partitions, void* workspace,
+                                   size_t workspace_bytes, void* stream) {
+  if (batch < 0 || num_q_heads <= 0 || num_kv_heads <= 0 || head_dim <= 0 || block_size <= 0 || max_seq_len < 0)
+    return set_error(KVB_E_ARG, "paged_attention: bad sizes");
+  if (batch == 0) return KVB_OK;
+  if (!query || !key_cache || !value_cache || !seq_lens || !out || !workspace)
+    return set_error(KVB_E_ARG, "paged_attention: null pointer");
+  if (num_q_heads % num_kv_heads) return set_error(KVB_E_SHAPE, "paged_attention: num_q_heads %% num_kv_heads != 0");
+  if (head_dim != 64 && head_dim != 128) return set_error(KVB_E_SHAPE, "paged_attention: head_dim must be 64 or 128");
+  if (!(block_size % kChunk == 0 || kChunk % block_size == 0))
+    return set_error(KVB_E_SHAPE, "paged_attention: block_size must divide 16 or be a multiple of 16");
+  if (!block_table && (int64_t)block_size < max_seq_len)
+    return set_error(KVB_E_SHAPE, "paged_attention: without a block table a block must hold a whole sequence");
+  if (seq_lens_dtype != KVB_I32 && seq_lens_dtype != KVB_I64) return set_error(KVB_E_DTYPE, "paged_attention: seq_lens dtype");
+  if (!is_float_dtype(q_dtype) || !is_float_dtype(out_dtype)) return set_error(KVB_E_DTYPE, "paged_attention: q/out dtype");
+  if (cache_dtype == KVB_E4M3 && (!k_scale || !v_scale))
+    return set_error(KVB_E_ARG, "paged_attention: e4m3 caches need k_scale and v_scale");
+  if ((k_new || v_new) && (!k_new || !v_new || cache_dtype != KVB_E4M3 || !is_float_dtype(new_dtype)))
+    return set_error(KVB_E_ARG, "paged_attention: the fused write needs k_new, v_new and an e4m3 cache");
+  const int group = num_q_heads / num_kv_heads;
+  const int tiles = (group + 7) / 8;
+  if (num_kv_heads * tiles > 16) return set_error(KVB_E_SHAPE, "paged_attention: more than 16 (kv head, 8-query) tiles");
+  int part = partition_size > 0 ? partition_size : 256;
+  if (part % kChunk) return set_error(KVB_E_SHAPE, "paged_attention: partition_size must be a multiple of 16");
+  int pmax = (int)((max_seq_len + part - 1) / part);
+  if (pmax < 1) pmax = 1;
+  if (exp_sums || max_logits || tmp_out) {
+    if (!exp_sums || !max_logits || !tmp_out) return set_error(KVB_E_ARG, "paged_attention: v2 outputs come together");
+    if (max_partitions != pmax)
+      return set_error(KVB_E_SHAPE, "paged_attention: max_partitions (%d) != ceil(max_seq_len / partition_size) (%d)",
+                       max_partitions, pmax);
+  }
+  const int esize = cache_dtype == KVB_E4M3 ? 1 : dtype_size(cache_dtype);
+  if (esize != 1 && esize != 2 && cache_dtype != KVB_F32)
+    return set_error(KVB_E_DTYPE, "paged_attention: cache dtype %d unsupported", cache_dtype);
+  const size_t need = kvb_paged_attention_workspace_size(batch, num_q_heads, head_dim, pmax);
+  if (workspace_bytes < need) return set_error(KVB_E_WORKSPACE, "paged_attention: workspace %zu < %zu", workspace_bytes, need);
+  const int64_t row_bytes = (int64_t)num_kv_heads * head_dim * esize;
+  if (row_bytes % 16) return set_error(KVB_E_ALIGN, "paged_attention: a token row must be a multiple of 16 bytes");
+  if (!aligned16(key_cache) || !aligned16(value_cache)) return set_error(KVB_E_ALIGN, "paged_attention: caches must be 16-byte aligned");
+  const size_t stage_bytes = (size_t)2 * kChunk * row_bytes;
+  int stages = (int)std::min<size_t>(kStagesMax, (200 * 1024) / stage_bytes);
+  if (stages > 3 && stage_bytes * 3 >= 96 * 1024) stages = 3;
+  if (cache_dtype != KVB_F32 && stages < 2)
+    return set_error(KVB_E_SHAPE, "paged_attention: a 16-token chunk (%zu B) does not fit twice in shared memory", stage_bytes);
+
+  DecodeArgs a;
+  a.q = query; a.k_cache = key_cache; a.v_cache = value_cache; a.k_scale = k_scale; a.v_scale = v_scale;
+  a.seq_lens = seq_lens; a.block_table = block_table; a.bt_stride = bt_stride; a.num_blocks = num_blocks;
+  a.k_new = k_new; a.v_new = v_new;
+  const size_t n = (size_t)batch * num_q_heads * pmax;
+  float* ws = reinterpret_cast<float*>((reinterpret_cast<uintptr_t>(workspace) + 255) & ~uintptr_t(255));
+  a.o_part = ws; a.m_part = ws + n * head_dim; a.l_part = a.m_part + n;   // o_part first: float4-aligned rows
+  a.exp_sums = exp_sums; a.max_logits = max_logits; a.tmp_out = tmp_out;
+  a.sm_scale = sm_scale;
+  a.batch = batch; a.hq = num_q_heads; a.hkv = num_kv_heads; a.group = group; a.bs = block_size; a.part = part;
+  a.pmax = pmax; a.tiles_per_kv = tiles; a.stages = stages;
+  a.q_dtype = q_dtype; a.new_dtype = new_dtype; a.sl64 = seq_lens_dtype == KVB_I64; a.v2_dtype = out_dtype;
+  const size_t smem = stage_bytes * stages;
+  cudaStream_t st = as_stream(stream);
+  int rc;
+  if (cache_dtype == KVB_E4M3) rc = head_dim == 128 ? launch_decode<uint8_t, 128>(a, smem, st) : launch_decode<uint8_t, 64>(a, smem, st);
+  else if (cache_dtype == KVB_F16) rc = head_dim == 128 ? launch_decode<__half, 128>(a, smem, st) : launch_decode<__half, 64>(a, smem, st);
+  else if (cache_dtype == KVB_BF16)
+    rc = head_dim == 128 ? launch_decode<__nv_bfloat16, 128>(a, smem, st) : launch_decode<__nv_bfloat16, 64>(a, smem, st);
+  else {
+    const size_t fsmem = (size_t)(head_dim + part) * sizeof(float) + (size_t)part * sizeof(int64_t);
+    if (fsmem > 48 * 1024) return set_error(KVB_E_SHAPE, "paged_attention: float32 partitions are limited to 4000 tokens");
+    dim3 grid(pmax, batch, num_q_heads);
+    paged_decode_f32_kernel<<<grid, 128, fsmem, st>>>(a, head_dim);
+    rc = check_launch("paged_decode_f32_kernel");
+  }
+  if (rc) return rc;
+  const float eps = exp_sums ? 1e-6f : 0.0f;
+  decode_merge_kernel<<<batch * num_q_heads, 128, 0, st>>>(a.m_part, a.l_part, a.o_part, seq_lens, a.sl64, num_q_heads,
+                                                           head_dim, part, pmax, eps, out, out_dtype);
+  return check_launch("decode_merge_kernel");
+}

@@ -137,3 +137,129 @@ def add_rmsnorm_quant(x: torch.Tensor, residual: torch.Tensor, weight: torch.Ten
     call("kvb_add_rmsnorm_quant", _ptr(x), _ptr(residual), _ptr(weight), kvb_dtype(x.dtype), rows, h, float(eps),
          _ptr(r_out), _ptr(codes), kvb_dtype(quant_dtype), _ptr(scales), _stream(dev))
     return r_out, codes, scales
+
+
+# --------------------------------------------------------------------------- paged KV cache
+def _index_dtype(t: torch.Tensor) -> int:
+    if t.dtype not in (torch.int32, torch.int64):
+        raise TypeError("slot/sequence indices must be int32 or int64")
+    return kvb_dtype(t.dtype)
+
+
+def paged_kv_cache_update(to_cache: torch.Tensor, kv_cache: torch.Tensor, slot_mapping: torch.Tensor) -> torch.Tensor:
+    """operators/kv_cache/paged_kv_cache_update/paged_kv_cache_update.py:21-31 (returns a new cache)."""
+    dev = _cuda(to_cache, kv_cache, slot_mapping)
+    kv_cache, slot_mapping = kv_cache.contiguous(), slot_mapping.contiguous()
+    to_cache = to_cache.to(kv_cache.dtype).contiguous()
+    out = torch.empty_like(kv_cache)
+    nb, bs = kv_cache.shape[0], kv_cache.shape[1]
+    slot_elems = kv_cache.numel() // max(nb * bs, 1)
+    call("kvb_paged_kv_cache_update", _ptr(to_cache), _ptr(kv_cache), _ptr(out), _ptr(slot_mapping),
+         _index_dtype(slot_mapping), kvb_dtype(kv_cache.dtype), slot_mapping.numel(), nb * bs, slot_elems, _stream(dev))
+    return out
+
+
+def paged_fp8_kv_write(x_new: torch.Tensor, cache: torch.Tensor, slot_mapping: torch.Tensor,
+                       head_scales: torch.Tensor) -> torch.Tensor:
+    """Quantise x_new [T, Hkv, D] into the e4m3 cache [num_blocks, block_size, Hkv, D] in place."""
+    dev = _cuda(x_new, cache, slot_mapping, head_scales)
+    x_new, slot_mapping = x_new.contiguous(), slot_mapping.contiguous()
+    head_scales = head_scales.to(torch.float32).contiguous()
+    t, h, d = x_new.shape
+    nslots = cache.shape[0] * cache.shape[1]
+    call("kvb_paged_fp8_kv_write", _ptr(x_new), kvb_dtype(x_new.dtype), _ptr(cache), _ptr(slot_mapping),
+         _index_dtype(slot_mapping), _ptr(head_scales), t, nslots, h, d, _stream(dev))
+    return cache
+
+
+# --------------------------------------------------------------------------- decode attention
+def _cache_kvb_dtype(t: torch.Tensor) -> int:
+    if t.dtype in (torch.uint8, torch.float8_e4m3fn):
+        return _lib.E4M3
+    return kvb_dtype(t.dtype)
+
+
+def _paged_attention(query, key_cache, value_cache, seq_lens, block_table, *, num_kv_heads, block_size, num_blocks,
+                     max_seq_len, scale, k_scale=None, v_scale=None, k_new=None, v_new=None, partition_size=0,
+                     out_dtype=None, v2=False):
+    dev = _cuda(query, key_cache, value_cache, seq_lens, block_table, k_scale, v_scale, k_new, v_new)
+    query = query.contiguous()
+    b, hq, d = query.shape
+    out_dtype = out_dtype or query.dtype
+    out = torch.empty((b, hq, d), dtype=out_dtype, device=dev)
+    part = partition_size if partition_size else 256
+    pmax = max(1, -(-int(max_seq_len) // part))
+    es = ml = tmp = None
+    if v2:
+        es = torch.empty((b, hq, pmax), dtype=out_dtype, device=dev)
+        ml = torch.empty((b, hq, pmax), dtype=out_dtype, device=dev)
+        tmp = torch.empty((b, hq, pmax, d), dtype=out_dtype, device=dev)
+    ws_bytes = _lib.lib().kvb_paged_attention_workspace_size(b, hq, d, pmax)
+    ws = workspace(dev, ws_bytes)
+    bt_ptr, bt_stride = None, 0
+    if block_table is not None:
+        block_table = block_table.to(torch.int32).contiguous()
+        bt_ptr, bt_stride = block_table.data_ptr(), block_table.shape[1]
+    seq_lens = seq_lens.contiguous()
+    if k_scale is not None:
+        k_scale = k_scale.to(torch.float32).contiguous()
+        v_scale = v_scale.to(torch.float32).contiguous()
+    if k_new is not None:
+        k_new, v_new = k_new.contiguous(), v_new.contiguous()
+    call("kvb_paged_attention", _ptr(query), kvb_dtype(query.dtype), _ptr(key_cache.contiguous()),
+         _ptr(value_cache.contiguous()), _cache_kvb_dtype(key_cache), _ptr(k_scale), _ptr(v_scale), _ptr(seq_lens),
+         _index_dtype(seq_lens), bt_ptr, bt_stride, b, hq, num_kv_heads, d, block_size, num_blocks, int(max_seq_len),
+         float(scale), _ptr(k_new), _ptr(v_new), kvb_dtype(k_new.dtype) if k_new is not None else 0, part, _ptr(out),
+         kvb_dtype(out_dtype), _ptr(es), _ptr(ml), _ptr(tmp), pmax, _ptr(ws), ws.numel(), _stream(dev))
+    return (out, es, ml, tmp) if v2 else out
+
+
+def paged_attention_v1(query, key_cache, value_cache, seq_lens, block_table, scale: Optional[float] = None,
+                       output_dtype: Optional[torch.dtype] = None):
+    """operators/attention/paged_attention_v1/paged_attention_v1.py:27-92.
+
+    ``key_cache`` / ``value_cache`` are the reference's ``[total_blocks, Hkv, block_size, D]``
+    tensors, whose memory the reference reads as ``[total_blocks, block_size, Hkv, D]``
+    (reshape of a gathered block, ``:64-69``); the kernel reads the same memory the same way.
+    """
+    nb, hkv, bs, d = key_cache.shape
+    scale = d ** -0.5 if scale is None else scale
+    return _paged_attention(query, key_cache, value_cache, seq_lens, block_table, num_kv_heads=hkv, block_size=bs,
+                            num_blocks=nb, max_seq_len=block_table.shape[1] * bs, scale=scale, out_dtype=output_dtype)
+
+
+def paged_attention_v2(query, key_cache, value_cache, seq_lens, block_table, partition_size: int,
+                       scale: Optional[float] = None, output_dtype: Optional[torch.dtype] = None):
+    """operators/attention/paged_attention_v2/paged_attention_v2.py:28-175 -> (out, exp_sums, max_logits, tmp_out)."""
+    nb, hkv, bs, d = key_cache.shape
+    scale = d ** -0.5 if scale is None else scale
+    # the partition outputs are sized by the longest sequence, as the reference's .item() does (:42-43)
+    max_len = int(seq_lens.detach().to("cpu", non_blocking=False).max()) if seq_lens.numel() else 0
+    return _paged_attention(query, key_cache, value_cache, seq_lens, block_table, num_kv_heads=hkv, block_size=bs,
+                            num_blocks=nb, max_seq_len=max_len, scale=scale, partition_size=partition_size,
+                            out_dtype=output_dtype, v2=True)
+
+
+def batched_decode_attention(q, k_cache, v_cache, seq_lens, scale: Optional[float] = None,
+                             output_dtype: Optional[torch.dtype] = None):
+    """operators/attention/batched_decode_attention/batched_decode_attention.py:30-52 (dense [B, L, Hkv, D])."""
+    b, lmax, hkv, d = k_cache.shape
+    scale = d ** -0.5 if scale is None else scale
+    return _paged_attention(q, k_cache, v_cache, seq_lens, None, num_kv_heads=hkv, block_size=lmax, num_blocks=b,
+                            max_seq_len=lmax, scale=scale, out_dtype=output_dtype)
+
+
+def paged_fp8_decode(query, k_cache, v_cache, k_scale, v_scale, seq_lens, block_table, scale: Optional[float] = None,
+                     k_new=None, v_new=None, max_seq_len: Optional[int] = None, partition_size: int = 0):
+    """FP8 paged decode (BASELINE fourth config): caches [num_blocks, block_size, Hkv, D] of e4m3 codes.
+
+    With ``k_new`` / ``v_new`` [B, Hkv, D], each sequence's token ``seq_len - 1`` is first
+    quantised into its slot (``block_table[b][(L-1)//bs]*bs + (L-1)%bs``) and attended to.
+    """
+    nb, bs, hkv, d = k_cache.shape
+    scale = d ** -0.5 if scale is None else scale
+    if max_seq_len is None:
+        max_seq_len = block_table.shape[1] * bs
+    return _paged_attention(query, k_cache, v_cache, seq_lens, block_table, num_kv_heads=hkv, block_size=bs,
+                            num_blocks=nb, max_seq_len=max_seq_len, scale=scale, k_scale=k_scale, v_scale=v_scale,
+                            k_new=k_new, v_new=v_new, partition_size=partition_size, out_dtype=query.dtype)
