@@ -82,6 +82,24 @@ __device__ __forceinline__ float load_f(const T* p, int64_t i) { return Elem<T>:
 
 __device__ __forceinline__ float ex2(float x) { return exp2f(x); }
 
+// NW consecutive 32-bit words from shared memory with the widest aligned accesses.
+template <int NW>
+__device__ __forceinline__ void load_words(const uint8_t* p, uint32_t (&w)[NW]) {
+  if constexpr (NW % 4 == 0) {
+#pragma unroll
+    for (int u = 0; u < NW / 4; ++u) {
+      const uint4 x = reinterpret_cast<const uint4*>(p)[u];
+      w[4 * u] = x.x; w[4 * u + 1] = x.y; w[4 * u + 2] = x.z; w[4 * u + 3] = x.w;
+    }
+  } else if constexpr (NW == 2) {
+    const uint2 x = *reinterpret_cast<const uint2*>(p);
+    w[0] = x.x; w[1] = x.y;
+  } else {
+    static_assert(NW == 1, "unsupported span");
+    w[0] = *reinterpret_cast<const uint32_t*>(p);
+  }
+}
+
 struct DecodeArgs {
   const void* q;            // [B, Hq, D] (q_dtype)
   const void* k_cache;      // [num_blocks, bs, Hkv, D]
@@ -301,13 +319,8 @@ __global__ void __launch_bounds__(MAXT) paged_decode_kernel(const __grid_constan
         kw1[0] = lo1.x; kw1[1] = lo1.y; kw1[2] = lo1.z; kw1[3] = lo1.w;
         kw1[4] = hi1.x; kw1[5] = hi1.y; kw1[6] = hi1.z; kw1[7] = hi1.w;
       } else {
-#pragma unroll
-        for (int u = 0; u < KW / 4; ++u) {
-          const uint4 x0 = *reinterpret_cast<const uint4*>(r0 + 16 * u);
-          const uint4 x1 = *reinterpret_cast<const uint4*>(r1 + 16 * u);
-          kw0[4 * u] = x0.x; kw0[4 * u + 1] = x0.y; kw0[4 * u + 2] = x0.z; kw0[4 * u + 3] = x0.w;
-          kw1[4 * u] = x1.x; kw1[4 * u + 1] = x1.y; kw1[4 * u + 2] = x1.z; kw1[4 * u + 3] = x1.w;
-        }
+        load_words<KW>(r0, kw0);
+        load_words<KW>(r1, kw1);
       }
     }
     float sacc[4] = {0.0f, 0.0f, 0.0f, 0.0f};
@@ -374,18 +387,10 @@ __global__ void __launch_bounds__(MAXT) paged_decode_kernel(const __grid_constan
 #pragma unroll
       for (int rr = 0; rr < 4; ++rr) {
         const uint8_t* src = vs + (size_t)toks[rr] * row_bytes + (size_t)kvh * D * EB + g * VSPAN;
-        const bool ok = toks[rr] < nvalid;
+        load_words<VW>(src, vw[rr]);
+        if (toks[rr] >= nvalid) {      // rows past the sequence end hold stale bytes: zero them
 #pragma unroll
-        for (int u = 0; u < VW / 4; ++u) {
-          uint4 x = *reinterpret_cast<const uint4*>(src + 16 * u);
-          if (!ok) x = make_uint4(0, 0, 0, 0);
-          vw[rr][4 * u] = x.x; vw[rr][4 * u + 1] = x.y; vw[rr][4 * u + 2] = x.z; vw[rr][4 * u + 3] = x.w;
-        }
-        if constexpr (VW % 4 != 0) {     // 8-byte spans (e4m3, D = 64)
-          uint2 x = *reinterpret_cast<const uint2*>(src);
-          if (!ok) x = make_uint2(0, 0);
-          vw[rr][0] = x.x;
-          vw[rr][1] = x.y;
+          for (int u = 0; u < VW; ++u) vw[rr][u] = 0u;
         }
       }
     }
@@ -599,6 +604,13 @@ int launch_decode(DecodeArgs& a, size_t smem, cudaStream_t st) {
   return launch_decode_t<KT, D, 544>(a, smem, st);
 }
 
+template <typename KT>
+int launch_decode_d(DecodeArgs& a, int head_dim, size_t smem, cudaStream_t st) {
+  if (head_dim == 128) return launch_decode<KT, 128>(a, smem, st);
+  if (head_dim == 64) return launch_decode<KT, 64>(a, smem, st);
+  return launch_decode<KT, 32>(a, smem, st);
+}
+
 }  // namespace
 }  // namespace kvb
 
@@ -623,7 +635,10 @@ extern "C" int kvb_paged_attention(const void* query, int q_dtype, const void* k
   if (!query || !key_cache || !value_cache || !seq_lens || !out || !workspace)
     return set_error(KVB_E_ARG, "paged_attention: null pointer");
   if (num_q_heads % num_kv_heads) return set_error(KVB_E_SHAPE, "paged_attention: num_q_heads %% num_kv_heads != 0");
-  if (head_dim != 64 && head_dim != 128) return set_error(KVB_E_SHAPE, "paged_attention: head_dim must be 64 or 128");
+  if (cache_dtype == KVB_F32 ? (head_dim % 4 != 0 || head_dim > 1024)
+                             : (head_dim != 32 && head_dim != 64 && head_dim != 128))
+    return set_error(KVB_E_SHAPE, "paged_attention: head_dim %d unsupported (32/64/128; float32 caches: multiples of 4)",
+                     head_dim);
   if (!(block_size % kChunk == 0 || kChunk % block_size == 0))
     return set_error(KVB_E_SHAPE, "paged_attention: block_size must divide 16 or be a multiple of 16");
   if (!block_table && (int64_t)block_size < max_seq_len)
@@ -676,10 +691,9 @@ extern "C" int kvb_paged_attention(const void* query, int q_dtype, const void* k
   const size_t smem = stage_bytes * stages;
   cudaStream_t st = as_stream(stream);
   int rc;
-  if (cache_dtype == KVB_E4M3) rc = head_dim == 128 ? launch_decode<uint8_t, 128>(a, smem, st) : launch_decode<uint8_t, 64>(a, smem, st);
-  else if (cache_dtype == KVB_F16) rc = head_dim == 128 ? launch_decode<__half, 128>(a, smem, st) : launch_decode<__half, 64>(a, smem, st);
-  else if (cache_dtype == KVB_BF16)
-    rc = head_dim == 128 ? launch_decode<__nv_bfloat16, 128>(a, smem, st) : launch_decode<__nv_bfloat16, 64>(a, smem, st);
+  if (cache_dtype == KVB_E4M3) rc = launch_decode_d<uint8_t>(a, head_dim, smem, st);
+  else if (cache_dtype == KVB_F16) rc = launch_decode_d<__half>(a, head_dim, smem, st);
+  else if (cache_dtype == KVB_BF16) rc = launch_decode_d<__nv_bfloat16>(a, head_dim, smem, st);
   else {
     const size_t fsmem = (size_t)(head_dim + part) * sizeof(float) + (size_t)part * sizeof(int64_t);
     if (fsmem > 48 * 1024) return set_error(KVB_E_SHAPE, "paged_attention: float32 partitions are limited to 4000 tokens");
