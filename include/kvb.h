@@ -176,7 +176,7 @@ KVB_API size_t kvb_paged_attention_workspace_size(int batch, int num_q_heads, in
  * (out_dtype, optional, all or none): the v2 partition outputs; then out uses the v2
  * normalisation (global_sum + 1e-6) and max_partitions must equal
  * ceil(max_seq_len / partition_size).
- * D in {64, 128}; block_size divides 16 or is a multiple of 16; Hkv * ceil(group / 8) <= 16.
+ * D in {32, 64, 128} (float32 caches: any multiple of 4); any block_size; Hkv * ceil(group / 8) <= 16.
  */
 KVB_API int kvb_paged_attention(const void* query, int q_dtype, const void* key_cache, const void* value_cache,
                                 int cache_dtype, const float* k_scale, const float* v_scale, const void* seq_lens,

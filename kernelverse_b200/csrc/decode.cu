@@ -204,32 +204,33 @@ __global__ void __launch_bounds__(MAXT) paged_decode_kernel(const __grid_constan
       const uint64_t pol = policy_evict_first();
       const uint8_t* kc = reinterpret_cast<const uint8_t*>(a.k_cache);
       const uint8_t* vc = reinterpret_cast<const uint8_t*>(a.v_cache);
-      const int pieces = a.bs >= kChunk ? 1 : kChunk / a.bs;      // bs divides 16 or 16 divides bs
-      const int rows_per_piece = a.bs >= kChunk ? kChunk : a.bs;
       for (int i = 0; i < nchunks; ++i) {
         const int s = i % S;
         if (i >= S && !mbar_wait_bounded(&empty[s], (uint32_t)((i / S) - 1) & 1u)) break;
         const int64_t t0 = t_begin + (int64_t)i * kChunk;
-        // Count the bytes first (pieces wholly past the end of the sequence are not copied).
+        const int64_t t1 = t_end < t0 + kChunk ? t_end : t0 + kChunk;   // rows past the end are not copied
+        // The chunk is copied as runs of rows that stay inside one block (any block size).
         uint32_t bytes = 0;
-        for (int pc = 0; pc < pieces; ++pc)
-          if (t0 + (int64_t)pc * rows_per_piece < L) bytes += 2u * rows_per_piece * row_bytes;
+        for (int64_t t = t0; t < t1;) {
+          const int64_t n = min(t1 - t, (int64_t)a.bs - t % a.bs);
+          bytes += 2u * (uint32_t)n * row_bytes;
+          t += n;
+        }
         mbar_arrive_expect_tx(&full[s], bytes);
-        for (int pc = 0; pc < pieces; ++pc) {
-          const int64_t t = t0 + (int64_t)pc * rows_per_piece;
-          if (t >= L) continue;
+        for (int64_t t = t0; t < t1;) {
+          const int64_t n = min(t1 - t, (int64_t)a.bs - t % a.bs);
           const int64_t row = token_row(a, b, t);
-          const uint32_t nb = rows_per_piece * row_bytes;
-          uint8_t* kd = kstage(s) + (size_t)pc * nb;
-          uint8_t* vd = vstage(s) + (size_t)pc * nb;
+          const uint32_t nb = (uint32_t)n * row_bytes;
+          const size_t doff = (size_t)(t - t0) * row_bytes;
           if (row < 0) {   // invalid block index: record it and complete the transaction without a copy
             atomicOr(&g_tu_status, kStatusBadIndex);
             asm volatile("mbarrier.complete_tx.relaxed.cta.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(&full[s])),
                          "r"(2 * nb) : "memory");
-            continue;
+          } else {
+            bulk_g2s(kstage(s) + doff, kc + row * row_bytes, nb, &full[s], pol);
+            bulk_g2s(vstage(s) + doff, vc + row * row_bytes, nb, &full[s], pol);
           }
-          bulk_g2s(kd, kc + row * row_bytes, nb, &full[s], pol);
-          bulk_g2s(vd, vc + row * row_bytes, nb, &full[s], pol);
+          t += n;
         }
       }
       // Wait (bounded) until the consumers are done with every stage before the CTA exits.
@@ -639,8 +640,6 @@ extern "C" int kvb_paged_attention(const void* query, int q_dtype, const void* k
                              : (head_dim != 32 && head_dim != 64 && head_dim != 128))
     return set_error(KVB_E_SHAPE, "paged_attention: head_dim %d unsupported (32/64/128; float32 caches: multiples of 4)",
                      head_dim);
-  if (!(block_size % kChunk == 0 || kChunk % block_size == 0))
-    return set_error(KVB_E_SHAPE, "paged_attention: block_size must divide 16 or be a multiple of 16");
   if (!block_table && (int64_t)block_size < max_seq_len)
     return set_error(KVB_E_SHAPE, "paged_attention: without a block table a block must hold a whole sequence");
   if (seq_lens_dtype != KVB_I32 && seq_lens_dtype != KVB_I64) return set_error(KVB_E_DTYPE, "paged_attention: seq_lens dtype");
