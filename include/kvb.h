@@ -187,6 +187,33 @@ KVB_API int kvb_paged_attention(const void* query, int q_dtype, const void* key_
                                 void* max_logits, void* tmp_out, int max_partitions, void* workspace,
                                 size_t workspace_bytes, void* stream);
 
+/*
+ * Allocation-free variant of kvb_paged_attention (no counterpart in the reference).
+ * Some callers cannot allocate device memory: a plugin that its host framework hands only
+ * input and output buffers, or a serving loop that must not call cudaMalloc (which can
+ * synchronise the device) on its hot path.  This entry point takes the same arguments as
+ * kvb_paged_attention minus the workspace and keeps its split-KV partials in a static
+ * device array of KVB_PAGED_ATTENTION_NOALLOC_SCRATCH_BYTES (16 MiB), which every GPU that
+ * loads the library holds until the process exits.  It allocates and frees nothing.
+ *   - Calls needing more scratch than that (batch * num_q_heads * ceil(max_seq_len /
+ *     partition_size) * (head_dim + 2) * 4 + 256 bytes) fail with KVB_E_WORKSPACE; a larger
+ *     partition_size shrinks the need.
+ *   - The first call on a device looks up the array's device address (cudaGetSymbolAddress)
+ *     with that device current; make that first call before any stream capture.
+ *   - All calls on a device share the array and it keeps the last call's contents; calls
+ *     whose work overlaps on the GPU (different streams or host threads) race on it.
+ */
+#define KVB_PAGED_ATTENTION_NOALLOC_SCRATCH_BYTES (16u * 1024u * 1024u)
+KVB_API int kvb_paged_attention_noalloc(const void* query, int q_dtype, const void* key_cache,
+                                        const void* value_cache, int cache_dtype, const float* k_scale,
+                                        const float* v_scale, const void* seq_lens, int seq_lens_dtype,
+                                        const int32_t* block_table, int64_t bt_stride, int batch, int num_q_heads,
+                                        int num_kv_heads, int head_dim, int block_size, int64_t num_blocks,
+                                        int64_t max_seq_len, float sm_scale, const void* k_new, const void* v_new,
+                                        int new_dtype, int partition_size, void* out, int out_dtype,
+                                        void* exp_sums, void* max_logits, void* tmp_out, int max_partitions,
+                                        void* stream);
+
 #ifdef __cplusplus
 }  /* extern "C" */
 #endif

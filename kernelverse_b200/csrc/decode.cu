@@ -706,3 +706,74 @@ extern "C" int kvb_paged_attention(const void* query, int q_dtype, const void* k
                                                            head_dim, part, pmax, eps, out, out_dtype);
   return check_launch("decode_merge_kernel");
 }
+
+// ---------------------------------------------------------------------------------------------
+// Allocation-free variant of kvb_paged_attention.
+//
+// Its split-KV partials live in this file-scope device array instead of a caller-provided
+// workspace.  Every GPU that loads this library's decode module holds the array until the
+// process exits, and all calls on a device share it: calls whose work overlaps on the GPU
+// (other streams, other host threads) race on it.  Nothing in it needs to start at zero --
+// the decode kernel writes every partial the merge kernel reads -- and it keeps whatever
+// the last call left there.
+#include <mutex>
+
+namespace kvb {
+namespace {
+static __device__ __align__(256) unsigned char g_noalloc_scratch[KVB_PAGED_ATTENTION_NOALLOC_SCRATCH_BYTES];
+
+constexpr int kMaxDevices = 64;
+std::mutex g_noalloc_mutex;
+void* g_noalloc_ptr[kMaxDevices] = {};
+
+// Device address of g_noalloc_scratch on the current device, looked up once per device
+// (the host-side symbol is only a stand-in and must never be passed to a kernel).
+int noalloc_scratch(void** out) {
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return set_error(KVB_E_LAUNCH, "paged_attention_noalloc: cudaGetDevice: %s", cudaGetErrorString(e));
+  if (dev < 0 || dev >= kMaxDevices) return set_error(KVB_E_DEVICE, "paged_attention_noalloc: device %d out of range", dev);
+  std::lock_guard<std::mutex> g(g_noalloc_mutex);
+  if (!g_noalloc_ptr[dev]) {
+    void* p = nullptr;
+    e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
+    if (e != cudaSuccess || !p)
+      return set_error(KVB_E_LAUNCH, "paged_attention_noalloc: cudaGetSymbolAddress: %s", cudaGetErrorString(e));
+    g_noalloc_ptr[dev] = p;
+  }
+  *out = g_noalloc_ptr[dev];
+  return KVB_OK;
+}
+}  // namespace
+}  // namespace kvb
+
+extern "C" int kvb_paged_attention_noalloc(const void* query, int q_dtype, const void* key_cache,
+                                           const void* value_cache, int cache_dtype, const float* k_scale,
+                                           const float* v_scale, const void* seq_lens, int seq_lens_dtype,
+                                           const int32_t* block_table, int64_t bt_stride, int batch, int num_q_heads,
+                                           int num_kv_heads, int head_dim, int block_size, int64_t num_blocks,
+                                           int64_t max_seq_len, float sm_scale, const void* k_new, const void* v_new,
+                                           int new_dtype, int partition_size, void* out, int out_dtype,
+                                           void* exp_sums, void* max_logits, void* tmp_out, int max_partitions,
+                                           void* stream) {
+  if (batch < 0 || num_q_heads <= 0 || head_dim <= 0 || max_seq_len < 0)
+    return set_error(KVB_E_ARG, "paged_attention_noalloc: bad sizes");
+  const int part = partition_size > 0 ? partition_size : 256;
+  int64_t pmax = (max_seq_len + part - 1) / part;
+  if (pmax < 1) pmax = 1;
+  const size_t need = kvb_paged_attention_workspace_size(batch, num_q_heads, head_dim, (int)pmax);
+  if (need > (size_t)KVB_PAGED_ATTENTION_NOALLOC_SCRATCH_BYTES)
+    return set_error(KVB_E_WORKSPACE,
+                     "paged_attention_noalloc: this call needs %zu bytes of scratch but the static scratch holds %u "
+                     "(batch * num_q_heads * ceil(max_seq_len / partition_size) * (head_dim + 2) * 4 + 256 bytes); "
+                     "use a larger partition_size or kvb_paged_attention with a caller workspace",
+                     need, (unsigned)KVB_PAGED_ATTENTION_NOALLOC_SCRATCH_BYTES);
+  void* ws = nullptr;
+  const int rc = noalloc_scratch(&ws);
+  if (rc) return rc;
+  return kvb_paged_attention(query, q_dtype, key_cache, value_cache, cache_dtype, k_scale, v_scale, seq_lens,
+                             seq_lens_dtype, block_table, bt_stride, batch, num_q_heads, num_kv_heads, head_dim,
+                             block_size, num_blocks, max_seq_len, sm_scale, k_new, v_new, new_dtype, partition_size, out,
+                             out_dtype, exp_sums, max_logits, tmp_out, max_partitions, ws,
+                             (size_t)KVB_PAGED_ATTENTION_NOALLOC_SCRATCH_BYTES, stream);
+}
