@@ -201,6 +201,44 @@ def time_region(torch, fn, steps: int, dist, world: int):
     return ms, t_wall0, t_wall1
 
 
+def make_c4_inputs(torch, dev, seed: int, batch: int = 64, hq: int = 32, hkv: int = 8, d: int = 128, bs: int = 16):
+    """BASELINE fourth config: ctx ~ U[512, 8192], seeded permuted block table, e4m3 caches."""
+    g = torch.Generator(device="cpu").manual_seed(seed)
+    lens = torch.randint(512, 8193, (batch,), generator=g, dtype=torch.int32)
+    nblk = ((lens + bs - 1) // bs)
+    total = int(nblk.sum())
+    maxb = int(nblk.max())
+    perm = torch.randperm(total, generator=g, dtype=torch.int64).to(torch.int32)
+    bt = torch.zeros((batch, maxb), dtype=torch.int32)
+    pos = 0
+    for b in range(batch):
+        n = int(nblk[b])
+        bt[b, :n] = perm[pos:pos + n]
+        pos += n
+    gd = torch.Generator(device=dev).manual_seed(seed)
+    k_scale = (torch.rand((hkv,), generator=gd, device=dev) * 0.01 + 0.005)
+    v_scale = (torch.rand((hkv,), generator=gd, device=dev) * 0.01 + 0.005)
+    kc = (torch.randn((total, bs, hkv, d), generator=gd, device=dev) / k_scale[None, None, :, None]).clamp(-448, 448).to(
+        torch.float8_e4m3fn)
+    vc = (torch.randn((total, bs, hkv, d), generator=gd, device=dev) / v_scale[None, None, :, None]).clamp(-448, 448).to(
+        torch.float8_e4m3fn)
+    q = torch.randn((batch, hq, d), generator=gd, device=dev).to(torch.bfloat16)
+    k_new = torch.randn((batch, hkv, d), generator=gd, device=dev).to(torch.bfloat16)
+    v_new = torch.randn((batch, hkv, d), generator=gd, device=dev).to(torch.bfloat16)
+    return dict(q=q, kc=kc, vc=vc, ks=k_scale, vs=v_scale, lens=lens.to(dev), bt=bt.to(dev), k_new=k_new, v_new=v_new,
+                sum_ctx=int(lens.sum()), sum_blocks=total, max_len=maxb * bs)
+
+
+def c4_bytes(c, hq=32, hkv=8, d=128) -> int:
+    b = c["q"].shape[0]
+    return (c["sum_ctx"] * 2 * hkv * d          # K + V e4m3 read
+            + c["sum_blocks"] * 4               # block-table entries
+            + 2 * b * hq * d * 2                # q read, out written (bf16)
+            + 2 * b * hkv * d * 2               # new K/V read (bf16)
+            + 2 * b * hkv * d                   # new K/V codes written
+            + b * 4 + 2 * hkv * 4)              # seq_lens, scales
+
+
 def secondary_benchmarks(torch, ops, hbm_peak):
     """Other hot-path kernels at their BASELINE configs (1 GPU)."""
     out = []
@@ -239,6 +277,28 @@ def secondary_benchmarks(torch, ops, hbm_peak):
                 "bytes_per_call": nbytes, "achieved_gbs_cold_l2": round(nbytes / us / 1e3, 1),
                 "frac_cold_l2": round(nbytes / us / 1e3 / hbm_peak, 4)})
     del flush
+    # fourth config: paged FP8 KV write + GQA decode (one step = write the new token + attend)
+    c = make_c4_inputs(torch, dev, 11)
+    step = lambda: ops.paged_fp8_decode(c["q"], c["kc"], c["vc"], c["ks"], c["vs"], c["lens"], c["bt"],  # noqa: E731
+                                        k_new=c["k_new"], v_new=c["v_new"], max_seq_len=c["max_len"])
+    for _ in range(5):
+        step()
+    torch.cuda.synchronize()
+    n = 50
+    s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    s.record(stream)
+    for _ in range(n):
+        step()
+    e.record(stream)
+    torch.cuda.synchronize()
+    us = s.elapsed_time(e) / n * 1e3
+    nbytes = c4_bytes(c)
+    flops = 4 * 128 * 32 * c["sum_ctx"]
+    out.append({"workload": "paged FP8 KV write + GQA decode, B=64, 32/8 heads, D=128, bs=16, ctx~U[512,8192] "
+                            "(BASELINE config 4)", "kernel": "paged_decode_kernel<e4m3,128> + decode_merge_kernel",
+                "sum_ctx": c["sum_ctx"], "us_per_call": round(us, 2), "bytes_per_call": nbytes,
+                "achieved_gbs": round(nbytes / us / 1e3, 1), "frac": round(nbytes / us / 1e3 / hbm_peak, 4),
+                "tflops": round(flops / us / 1e6, 2), "l2": "KV cache larger than L2"})
     return out
 
 
@@ -252,6 +312,8 @@ def main():
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--profile-only", action="store_true",
                     help="run W warm-up + K steps of the headline kernel and exit (for ncu captures)")
+    ap.add_argument("--profile-workload", choices=["c2", "c4"], default="c2",
+                    help="workload that --profile-only runs")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
@@ -295,6 +357,14 @@ def main():
     from kernelverse_b200 import ops
 
     dev = torch.device("cuda", local)
+    if args.profile_only and args.profile_workload == "c4":
+        c = make_c4_inputs(torch, dev, 11)
+        step4 = lambda: ops.paged_fp8_decode(c["q"], c["kc"], c["vc"], c["ks"], c["vs"], c["lens"],  # noqa: E731
+                                             c["bt"], k_new=c["k_new"], v_new=c["v_new"], max_seq_len=c["max_len"])
+        for _ in range(args.warmup + args.steps):
+            step4()
+        torch.cuda.synchronize()
+        return
     x, r, w = make_c2_inputs(torch, dev, seed=1000 + rank)
     step = lambda: ops.add_rmsnorm_quant(x, r, w, EPS)   # noqa: E731
 

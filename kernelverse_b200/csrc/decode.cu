@@ -80,7 +80,12 @@ __device__ __forceinline__ uint32_t pack2(float lo, float hi, bool bf16) {
 template <typename T>
 __device__ __forceinline__ float load_f(const T* p, int64_t i) { return Elem<T>::to_f(p[i]); }
 
-__device__ __forceinline__ float ex2(float x) { return exp2f(x); }
+// 2^x with the hardware approximation (MUFU.EX2, relative error ~2^-22; ex2(-inf) = +0).
+__device__ __forceinline__ float ex2(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
 
 // NW consecutive 32-bit words from shared memory with the widest aligned accesses.
 template <int NW>
@@ -147,7 +152,7 @@ __device__ __forceinline__ int64_t token_row(const DecodeArgs& a, int b, int64_t
 }
 
 template <typename KT, int D, int MAXT>
-__global__ void __launch_bounds__(MAXT) paged_decode_kernel(const __grid_constant__ DecodeArgs a) {
+__global__ void __launch_bounds__(MAXT, MAXT <= 288 ? 2 : 1) paged_decode_kernel(const __grid_constant__ DecodeArgs a) {
   using TR = CacheTraits<KT>;
   constexpr int EB = TR::kBytes;
   constexpr bool BF = TR::kBf16;
@@ -362,12 +367,14 @@ __global__ void __launch_bounds__(MAXT) paged_decode_kernel(const __grid_constan
     l1 = l1 * al1 + (p1 + p3);
     m0 = mn0;
     m1 = mn1;
+    if (__any_sync(0xffffffffu, al0 != 1.0f || al1 != 1.0f)) {   // skipped once the running maxima settle
 #pragma unroll
-    for (int t = 0; t < SLABS; ++t) {
-      o[t][0] *= al0;
-      o[t][2] *= al0;
-      o[t][1] *= al1;
-      o[t][3] *= al1;
+      for (int t = 0; t < SLABS; ++t) {
+        o[t][0] *= al0;
+        o[t][2] *= al0;
+        o[t][1] *= al1;
+        o[t][3] *= al1;
+      }
     }
     // ---- P^T as the B operand: lane (g, c) needs head g, tokens {2c, 2c+1 | 2c+8, 2c+9}
     uint32_t pb0, pb1;
