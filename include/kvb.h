@@ -124,6 +124,31 @@ KVB_API int kvb_add_rmsnorm_quant(const void* x, const void* residual, const voi
                           int64_t rows, int64_t hidden, float eps, void* residual_out,
                           void* codes, int code_dtype, float* scales, void* stream);
 
+/* ---------------------------------------------------------------- W8A8 int8 GEMM */
+
+/* Bytes of workspace kvb_w8a8_scaled_mm needs (0-sized needs still take a 256-byte block). */
+KVB_API size_t kvb_w8a8_workspace_size(int64_t M, int64_t N, int64_t K, int b_layout, int has_azp);
+
+/*
+ * W8A8 GEMM on tcgen05 tensor cores (int32 accumulation in TMEM).
+ * Replaces operators/gemm/int8_scaled_mm_azp/int8_scaled_mm_azp.py:61-85 (whose float
+ * dequantise-then-matmul is computed exactly in integers here) and implements the BASELINE
+ * third config:
+ *   acc[m, n] = sum_k a[m, k] * B(n, k)                 (exact int32)
+ *   acc      -= azp[n] * sum_k a[m, k]                  (when azp != NULL; azp holds integers)
+ *   out[m, n] = ((float(acc) * a_scales[m]) * b_scales[n] + azp_adj[n]) + bias[n]
+ *             (each term only when its pointer is non-NULL; one float32 rounding per step)
+ * out_dtype KVB_BF16 / KVB_F16 / KVB_F32, or KVB_I32 for the raw accumulator (scales unused).
+ * a [M, K] int8 row-major.  b_layout 0: b [N, K] (K contiguous); 1: b [K, N] (the reference's
+ * layout, transposed into the workspace first).  out [M, ldo] row-major.  K % 16 == 0;
+ * a (and b for layout 0) 16-byte aligned.  Workspace: kvb_w8a8_workspace_size() bytes when
+ * b_layout == 1 or azp != NULL, else may be NULL.
+ */
+KVB_API int kvb_w8a8_scaled_mm(const int8_t* a, const int8_t* b, int b_layout, const float* a_scales,
+                               const float* b_scales, const void* bias, int bias_dtype, const float* azp,
+                               const float* azp_adj, int64_t M, int64_t N, int64_t K, void* out, int out_dtype,
+                               int64_t ldo, void* workspace, size_t workspace_bytes, void* stream);
+
 /* ---------------------------------------------------------------- paged KV-cache writes */
 
 /*

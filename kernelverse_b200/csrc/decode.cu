@@ -579,12 +579,6 @@ __global__ void __launch_bounds__(128) decode_merge_kernel(const float* __restri
   }
 }
 
-int sm_count_dev() {
-  int dev = 0, n = 0;
-  cudaGetDevice(&dev);
-  cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
-  return n > 0 ? n : 148;
-}
 
 template <typename KT, int D, int MAXT>
 int launch_decode_t(DecodeArgs& a, size_t smem, cudaStream_t st) {

@@ -1,0 +1,486 @@
+// W8A8 int8 GEMM on the 5th-generation tensor cores: out = f(A[M,K] . B[N,K]^T).
+//
+//   acc[m, n]  = sum_k A[m, k] * B[n, k]                      (exact int32, tcgen05.mma kind::i8, TMEM)
+//   acc'[m, n] = acc[m, n] - azp[n] * rowsum(A[m, :])         (optional zero-point correction, exact)
+//   out[m, n]  = ((float(acc') * sa[m]) * sb[n] + azp_adj[n]) + bias[n]   (each step one float32 rounding)
+//
+// or the raw int32 accumulator.  This is the reference's int8_scaled_mm_azp
+// (operators/gemm/int8_scaled_mm_azp/int8_scaled_mm_azp.py:61-85, with its dequantise-then-float
+// matmul replaced by the exact integer form) and the BASELINE third config (azp off, bias on).
+//
+// Structure: a persistent kernel, one CTA per SM, 128 x BN output tiles (BN = 256 or 128).
+//   warp 0: TMA producer -- A [128 x 128 B] and B [BN x 128 B] K-major boxes with 128-byte
+//           swizzle into a kStages-deep shared-memory ring (mbarrier complete_tx);
+//   warp 1: allocates 2 x BN TMEM columns (double-buffered accumulator) and one lane issues
+//           4 x tcgen05.mma (M=128, N=BN, K=32) per stage, committing the stage back to the
+//           producer and each finished tile to the epilogue;
+//   warps 2-5: epilogue -- tcgen05.ld 32 columns at a time from their TMEM lane quarter,
+//           scale / bias / convert, store; then release the accumulator buffer.
+// Every mbarrier wait is bounded (kvb_async.cuh); on a timeout the roles drain and the CTA
+// frees its TMEM before exiting.
+#include <cuda.h>
+#include <cudaTypedefs.h>
+
+#include <mutex>
+
+#include "kvb_common.cuh"
+#include "kvb_async.cuh"
+
+namespace kvb {
+namespace {
+
+constexpr int kBM = 128;
+constexpr int kBK = 128;          // bytes of K per stage = one 128-byte swizzle row
+constexpr int kUmmaK = 32;        // K of one kind::i8 MMA
+constexpr int kThreads = 192;     // 6 warps
+
+struct GemmArgs {
+  int M, N, K;
+  const float* sa;       // [M]
+  const float* sb;       // [N]
+  const void* bias;      // [N] or null
+  int bias_dtype;
+  const float* azp;      // [N] or null (integer-valued)
+  const int32_t* rowsum; // [M] (when azp)
+  const float* azp_adj;  // [N] or null
+  void* out;
+  int64_t ldo;
+  int out_dtype;         // KVB_BF16 / KVB_F16 / KVB_F32 / KVB_I32
+  int n_blocks, m_blocks, tiles;
+};
+
+// ---------------------------------------------------------------- tcgen05 / TMA wrappers
+__device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, int x, int y, uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];"
+      ::"r"(smem_u32(dst)), "l"(map), "r"(x), "r"(y), "r"(smem_u32(bar))
+      : "memory");
+}
+
+__device__ __forceinline__ void tmem_alloc(uint32_t* dst_smem, uint32_t ncols) {
+  asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(dst_smem)),
+               "r"(ncols)
+               : "memory");
+  asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void tmem_dealloc(uint32_t taddr, uint32_t ncols) {
+  asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols) : "memory");
+}
+__device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
+
+// Shared-memory matrix descriptor: K-major operand, 128-byte swizzle, 8-row atoms of 1024 B.
+__device__ __forceinline__ uint64_t smem_desc_k128(const void* p) {
+  const uint32_t a = smem_u32(p);
+  uint64_t d = 0;
+  d |= (uint64_t)((a >> 4) & 0x3FFFu);          // start address
+  d |= (uint64_t)1u << 16;                       // leading byte offset: 16 B (unused for swizzled K-major)
+  d |= (uint64_t)(1024u >> 4) << 32;             // stride byte offset: 1024 B between 8-row groups
+  d |= (uint64_t)1u << 46;                       // descriptor version (sm_100)
+  d |= (uint64_t)2u << 61;                       // layout: SWIZZLE_128B
+  return d;
+}
+
+// Instruction descriptor of tcgen05.mma kind::i8: s32 accumulate, signed A and B, K-major both.
+__host__ __device__ constexpr uint32_t idesc_i8(int m, int n) {
+  return (2u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(n >> 3) << 17) | ((uint32_t)(m >> 4) << 24);
+}
+
+__device__ __forceinline__ void mma_i8(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc, uint32_t idesc, uint32_t accum) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::i8 [%0], %1, %2, %3, {%5, %6, %7, %8}, p;\n\t}"
+      ::"r"(tmem_d), "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accum), "r"(0), "r"(0), "r"(0), "r"(0)
+      : "memory");
+}
+
+__device__ __forceinline__ void mma_commit(uint64_t* bar) {
+  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar))
+               : "memory");
+}
+
+// 32 lanes x 32 consecutive 32-bit columns: this thread gets its lane's 32 columns.
+__device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&r)[32]) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
+      "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]), "=r"(r[8]),
+        "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]), "=r"(r[16]),
+        "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]), "=r"(r[24]),
+        "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+      : "r"(taddr));
+  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+}
+
+// Tile order: M fastest inside a group of 8 N blocks, so the CTAs running at the same time
+// share B tiles in L2 and A (which fits in L2) is re-read from L2.
+__device__ __forceinline__ void tile_coords(const GemmArgs& g, int t, int& mb, int& nb) {
+  constexpr int kGroup = 8;
+  const int per_group = kGroup * g.m_blocks;
+  const int grp = t / per_group;
+  const int first_n = grp * kGroup;
+  const int gn = min(kGroup, g.n_blocks - first_n);
+  const int r = t - grp * per_group;
+  mb = r / gn;
+  nb = first_n + r % gn;
+}
+
+__device__ __forceinline__ float load_bias(const void* p, int dt, int n) {
+  if (dt == KVB_BF16) return __bfloat162float(reinterpret_cast<const __nv_bfloat16*>(p)[n]);
+  if (dt == KVB_F16) return __half2float(reinterpret_cast<const __half*>(p)[n]);
+  return reinterpret_cast<const float*>(p)[n];
+}
+
+template <int BN, int STAGES>
+__global__ void __launch_bounds__(kThreads, 1) w8a8_gemm_kernel(const __grid_constant__ CUtensorMap tmap_a,
+                                                                 const __grid_constant__ CUtensorMap tmap_b,
+                                                                 const __grid_constant__ GemmArgs g) {
+  constexpr uint32_t kABytes = kBM * kBK;
+  constexpr uint32_t kBBytes = BN * kBK;
+  constexpr uint32_t kStageBytes = kABytes + kBBytes;
+  constexpr uint32_t kTmemCols = 2 * BN;      // 512 or 256: a power of two >= 32
+  constexpr uint32_t kIdesc = idesc_i8(kBM, BN);
+
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  __shared__ uint64_t full[STAGES], empty[STAGES], tmem_full[2], tmem_empty[2], mma_done;
+  __shared__ uint32_t tmem_base_s;
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int KB = (g.K + kBK - 1) / kBK;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    for (int j = 0; j < 2; ++j) {
+      mbar_init(&tmem_full[j], 1);
+      mbar_init(&tmem_empty[j], 4);
+    }
+    mbar_init(&mma_done, 1);
+    fence_mbar_init();
+    asm volatile("prefetch.tensormap [%0];" ::"l"(&tmap_a) : "memory");
+    asm volatile("prefetch.tensormap [%0];" ::"l"(&tmap_b) : "memory");
+  }
+  if (warp == 1) tmem_alloc(&tmem_base_s, kTmemCols);
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = tmem_base_s;
+
+  if (warp == 0) {
+    // ------------------------------------------------------------ TMA producer
+    if (lane == 0) {
+      uint32_t it = 0;
+      bool ok = true;
+      for (int t = blockIdx.x; t < g.tiles && ok; t += gridDim.x) {
+        int mb, nb;
+        tile_coords(g, t, mb, nb);
+        for (int kb = 0; kb < KB; ++kb, ++it) {
+          const int s = it % STAGES;
+          const uint32_t use = it / STAGES;
+          if (use > 0 && !mbar_wait_bounded(&empty[s], (use - 1) & 1u)) {
+            ok = false;
+            break;
+          }
+          uint8_t* sa_ = smem + s * kStageBytes;
+          mbar_arrive_expect_tx(&full[s], kStageBytes);
+          tma_load_2d(sa_, &tmap_a, kb * kBK, mb * kBM, &full[s]);
+          tma_load_2d(sa_ + kABytes, &tmap_b, kb * kBK, nb * BN, &full[s]);
+        }
+      }
+      // drain: every stage issued must have been consumed before this CTA exits
+      for (uint32_t i = it > STAGES ? it - STAGES : 0; i < it; ++i)
+        mbar_wait_bounded(&empty[i % STAGES], (i / STAGES) & 1u);
+    }
+  } else if (warp == 1) {
+    // ------------------------------------------------------------ MMA issuer
+    if (lane == 0) {
+      uint32_t it = 0, local = 0;
+      bool ok = true;
+      for (int t = blockIdx.x; t < g.tiles && ok; t += gridDim.x, ++local) {
+        const uint32_t ab = local & 1u, v = local >> 1;
+        if (v > 0 && !mbar_wait_bounded(&tmem_empty[ab], (v - 1) & 1u)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        const uint32_t d_tmem = tmem_base + ab * BN;
+        for (int kb = 0; kb < KB; ++kb, ++it) {
+          const int s = it % STAGES;
+          if (!mbar_wait_bounded(&full[s], (it / STAGES) & 1u)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint8_t* a_s = smem + s * kStageBytes;
+          const uint8_t* b_s = a_s + kABytes;
+#pragma unroll
+          for (int kk = 0; kk < kBK / kUmmaK; ++kk)
+            mma_i8(d_tmem, smem_desc_k128(a_s + kk * kUmmaK), smem_desc_k128(b_s + kk * kUmmaK), kIdesc,
+                   (kb | kk) != 0);
+          mma_commit(&empty[s]);      // stage s is free once these MMAs have read it
+        }
+        if (!ok) break;
+        mma_commit(&tmem_full[ab]);   // accumulator ab is final once every MMA above completes
+      }
+      // every MMA this thread issued has completed before TMEM may be freed
+      mma_commit(&mma_done);
+      mbar_wait_bounded(&mma_done, 0);
+    }
+  } else {
+    // ------------------------------------------------------------ epilogue (warps 2..5)
+    const int q = warp & 3;                 // TMEM lane quarter this warp may access
+    uint32_t local = 0;
+    for (int t = blockIdx.x; t < g.tiles; t += gridDim.x, ++local) {
+      const uint32_t ab = local & 1u, v = local >> 1;
+      if (!mbar_wait_bounded(&tmem_full[ab], v & 1u)) break;
+      tc_fence_after();
+      int mb, nb;
+      tile_coords(g, t, mb, nb);
+      const int m = mb * kBM + q * 32 + lane;
+      const bool mrow = m < g.M;
+      const float sa = mrow ? g.sa[m] : 0.0f;
+      const int32_t rs = (g.azp && mrow) ? g.rowsum[m] : 0;
+#pragma unroll 1
+      for (int c0 = 0; c0 < BN; c0 += 32) {
+        uint32_t r[32];
+        __syncwarp();                       // tcgen05.ld is .sync.aligned: reconverge first
+        tmem_ld32(tmem_base + ((uint32_t)(q * 32) << 16) + ab * BN + c0, r);
+        const int n0 = nb * BN + c0;
+        if (!mrow || n0 >= g.N) continue;
+        const int ncols = min(32, g.N - n0);
+        if (g.out_dtype == KVB_I32) {
+          int32_t* o = reinterpret_cast<int32_t*>(g.out) + (int64_t)m * g.ldo + n0;
+          if (ncols == 32 && (((uintptr_t)o) & 15) == 0) {
+#pragma unroll
+            for (int j = 0; j < 32; j += 4) *reinterpret_cast<uint4*>(o + j) = make_uint4(r[j], r[j + 1], r[j + 2], r[j + 3]);
+          } else {
+#pragma unroll
+            for (int j = 0; j < 32; ++j)
+              if (j < ncols) o[j] = (int32_t)r[j];
+          }
+          continue;
+        }
+        float f[32];
+#pragma unroll
+        for (int j = 0; j < 32; ++j) {
+          const int n = n0 + j < g.N ? n0 + j : g.N - 1;
+          int32_t acc = (int32_t)r[j];
+          if (g.azp) acc -= (int32_t)g.azp[n] * rs;
+          float y = __fmul_rn(__fmul_rn((float)acc, sa), g.sb[n]);
+          if (g.azp_adj) y = __fadd_rn(y, g.azp_adj[n]);
+          if (g.bias) y = __fadd_rn(y, load_bias(g.bias, g.bias_dtype, n));
+          f[j] = y;
+        }
+        if (g.out_dtype == KVB_BF16 || g.out_dtype == KVB_F16) {
+          uint32_t pk[16];
+#pragma unroll
+          for (int j = 0; j < 16; ++j) {
+            if (g.out_dtype == KVB_BF16) {
+              __nv_bfloat162 h = __floats2bfloat162_rn(f[2 * j], f[2 * j + 1]);
+              pk[j] = *reinterpret_cast<uint32_t*>(&h);
+            } else {
+              __half2 h = __floats2half2_rn(f[2 * j], f[2 * j + 1]);
+              pk[j] = *reinterpret_cast<uint32_t*>(&h);
+            }
+          }
+          uint16_t* o = reinterpret_cast<uint16_t*>(g.out) + (int64_t)m * g.ldo + n0;
+          if (ncols == 32 && (((uintptr_t)o) & 15) == 0) {
+#pragma unroll
+            for (int j = 0; j < 16; j += 4) *reinterpret_cast<uint4*>(o + 2 * j) = make_uint4(pk[j], pk[j + 1], pk[j + 2], pk[j + 3]);
+          } else {
+#pragma unroll
+            for (int j = 0; j < 32; ++j)
+              if (j < ncols) o[j] = (uint16_t)(pk[j >> 1] >> ((j & 1) * 16));
+          }
+        } else {
+          float* o = reinterpret_cast<float*>(g.out) + (int64_t)m * g.ldo + n0;
+          if (ncols == 32 && (((uintptr_t)o) & 15) == 0) {
+#pragma unroll
+            for (int j = 0; j < 32; j += 4) *reinterpret_cast<float4*>(o + j) = make_float4(f[j], f[j + 1], f[j + 2], f[j + 3]);
+          } else {
+#pragma unroll
+            for (int j = 0; j < 32; ++j)
+              if (j < ncols) o[j] = f[j];
+          }
+        }
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&tmem_empty[ab]);
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    __syncwarp();
+    tc_fence_after();
+    tmem_dealloc(tmem_base, kTmemCols);
+  }
+}
+
+// rowsum[m] = sum_k A[m, k] (int32), for the zero-point correction.
+__global__ void __launch_bounds__(256) rowsum_i8_kernel(const int8_t* __restrict__ a, int M, int K, int32_t* __restrict__ out) {
+  const int warps = blockDim.x >> 5, lane = threadIdx.x & 31;
+  for (int m = blockIdx.x * warps + (threadIdx.x >> 5); m < M; m += gridDim.x * warps) {
+    const int8_t* row = a + (int64_t)m * K;
+    int s = 0;
+    for (int k = lane * 4; k + 3 < K; k += 128) {
+      const int w = *reinterpret_cast<const int*>(row + k);
+      s = __dp4a(w, 0x01010101, s);
+    }
+    for (int k = (K & ~3) + lane; k < K; k += 32) s += row[k];
+    for (int o = 16; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
+    if (lane == 0) out[m] = s;
+  }
+}
+
+// B [K, N] (N contiguous) -> Bt [N, K] (K contiguous), 32x32 tiles through shared memory.
+__global__ void __launch_bounds__(256) transpose_i8_kernel(const int8_t* __restrict__ b, int K, int N, int8_t* __restrict__ bt) {
+  __shared__ int8_t tile[32][33];
+  const int k0 = blockIdx.y * 32, n0 = blockIdx.x * 32;
+  for (int i = threadIdx.y; i < 32; i += blockDim.y) {
+    const int k = k0 + i, n = n0 + threadIdx.x;
+    if (k < K && n < N) tile[i][threadIdx.x] = b[(int64_t)k * N + n];
+  }
+  __syncthreads();
+  for (int i = threadIdx.y; i < 32; i += blockDim.y) {
+    const int n = n0 + i, k = k0 + threadIdx.x;
+    if (k < K && n < N) bt[(int64_t)n * K + k] = tile[threadIdx.x][i];
+  }
+}
+
+// ---------------------------------------------------------------- host side
+PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    cudaDriverEntryPointQueryResult q;
+    void* p = nullptr;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+  });
+  return fn;
+}
+
+// 2-D int8 K-major map: rows x K, box [box_rows x 128 B], 128-byte swizzle, zero fill out of bounds.
+int make_map(CUtensorMap* map, const void* base, int rows, int K, int box_rows) {
+  auto fn = encode_fn();
+  if (!fn) return set_error(KVB_E_LAUNCH, "w8a8_scaled_mm: cuTensorMapEncodeTiled unavailable");
+  cuuint64_t dims[2] = {(cuuint64_t)K, (cuuint64_t)rows};
+  cuuint64_t strides[1] = {(cuuint64_t)K};
+  cuuint32_t box[2] = {(cuuint32_t)kBK, (cuuint32_t)box_rows};
+  cuuint32_t estr[2] = {1, 1};
+  CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void*>(base), dims, strides, box, estr,
+                  CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                  CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return set_error(KVB_E_LAUNCH, "w8a8_scaled_mm: cuTensorMapEncodeTiled failed (%d)", (int)r);
+  return KVB_OK;
+}
+
+int num_sms() {
+  int dev = 0, n = 0;
+  cudaGetDevice(&dev);
+  cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
+  return n > 0 ? n : 148;
+}
+
+template <int BN, int STAGES>
+int launch_gemm(const int8_t* a, const int8_t* b_nk, GemmArgs& g, cudaStream_t st) {
+  CUtensorMap ma, mb;
+  int rc = make_map(&ma, a, g.M, g.K, kBM);
+  if (rc) return rc;
+  rc = make_map(&mb, b_nk, g.N, g.K, BN);
+  if (rc) return rc;
+  g.m_blocks = (g.M + kBM - 1) / kBM;
+  g.n_blocks = (g.N + BN - 1) / BN;
+  g.tiles = g.m_blocks * g.n_blocks;
+  const size_t smem = (size_t)STAGES * (kBM * kBK + BN * kBK) + 1024;
+  auto kern = w8a8_gemm_kernel<BN, STAGES>;
+  static int set_dev = -1;
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (set_dev != dev) {
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    if (e != cudaSuccess) return set_error(KVB_E_LAUNCH, "w8a8_scaled_mm: smem attribute: %s", cudaGetErrorString(e));
+    set_dev = dev;
+  }
+  const int grid = std::min(g.tiles, num_sms());
+  kern<<<grid, kThreads, smem, st>>>(ma, mb, g);
+  return check_launch("w8a8_gemm_kernel");
+}
+
+bool is_sm100() {
+  static int cached = -1;
+  if (cached < 0) {
+    int dev = 0, major = 0;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, dev);
+    cached = major == 10;
+  }
+  return cached == 1;
+}
+
+}  // namespace
+}  // namespace kvb
+
+using namespace kvb;
+
+extern "C" size_t kvb_w8a8_workspace_size(int64_t M, int64_t N, int64_t K, int b_layout, int has_azp) {
+  size_t n = 256;
+  if (b_layout == 1) n += (size_t)N * K + 256;      // transposed B
+  if (has_azp) n += (size_t)M * 4 + 256;            // row sums of A
+  return n;
+}
+
+extern "C" int kvb_w8a8_scaled_mm(const int8_t* a, const int8_t* b, int b_layout, const float* a_scales,
+                                  const float* b_scales, const void* bias, int bias_dtype, const float* azp,
+                                  const float* azp_adj, int64_t M, int64_t N, int64_t K, void* out, int out_dtype,
+                                  int64_t ldo, void* workspace, size_t workspace_bytes, void* stream) {
+  if (M < 0 || N < 0 || K < 0) return set_error(KVB_E_ARG, "w8a8_scaled_mm: negative size");
+  if (M == 0 || N == 0) return KVB_OK;
+  if (!a || !b || !out) return set_error(KVB_E_ARG, "w8a8_scaled_mm: null pointer");
+  if (out_dtype != KVB_I32 && (!a_scales || !b_scales)) return set_error(KVB_E_ARG, "w8a8_scaled_mm: scales required");
+  if (out_dtype != KVB_BF16 && out_dtype != KVB_F16 && out_dtype != KVB_F32 && out_dtype != KVB_I32)
+    return set_error(KVB_E_DTYPE, "w8a8_scaled_mm: out dtype %d", out_dtype);
+  if (bias && bias_dtype != KVB_BF16 && bias_dtype != KVB_F16 && bias_dtype != KVB_F32)
+    return set_error(KVB_E_DTYPE, "w8a8_scaled_mm: bias dtype %d", bias_dtype);
+  if (b_layout != 0 && b_layout != 1) return set_error(KVB_E_ARG, "w8a8_scaled_mm: b_layout must be 0 ([N,K]) or 1 ([K,N])");
+  if (K % 16 != 0 || K == 0) return set_error(KVB_E_SHAPE, "w8a8_scaled_mm: K must be a positive multiple of 16");
+  if (M > 0x7fffffff || N > 0x7fffffff || K > 0x7fffffff) return set_error(KVB_E_SHAPE, "w8a8_scaled_mm: size too large");
+  if (ldo < N) return set_error(KVB_E_SHAPE, "w8a8_scaled_mm: ldo < N");
+  if (!aligned16(a) || (b_layout == 0 && !aligned16(b))) return set_error(KVB_E_ALIGN, "w8a8_scaled_mm: A/B must be 16-byte aligned");
+  if (!is_sm100()) return set_error(KVB_E_DEVICE, "w8a8_scaled_mm: needs an sm_100 device");
+  const size_t need = kvb_w8a8_workspace_size(M, N, K, b_layout, azp != nullptr);
+  if ((b_layout == 1 || azp) && (!workspace || workspace_bytes < need))
+    return set_error(KVB_E_WORKSPACE, "w8a8_scaled_mm: workspace %zu < %zu", workspace_bytes, need);
+  cudaStream_t st = as_stream(stream);
+  uint8_t* ws = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(workspace) + 255) & ~uintptr_t(255));
+  const int8_t* b_nk = b;
+  if (b_layout == 1) {
+    int8_t* bt = reinterpret_cast<int8_t*>(ws);
+    ws += ((size_t)N * K + 255) & ~size_t(255);
+    dim3 grid((unsigned)((N + 31) / 32), (unsigned)((K + 31) / 32));
+    transpose_i8_kernel<<<grid, dim3(32, 8), 0, st>>>(b, (int)K, (int)N, bt);
+    int rc = check_launch("transpose_i8_kernel");
+    if (rc) return rc;
+    b_nk = bt;
+  }
+  GemmArgs g{};
+  g.M = (int)M; g.N = (int)N; g.K = (int)K;
+  g.sa = a_scales; g.sb = b_scales; g.bias = bias; g.bias_dtype = bias_dtype;
+  g.azp = azp; g.azp_adj = azp_adj; g.out = out; g.ldo = ldo; g.out_dtype = out_dtype;
+  if (azp) {
+    int32_t* rs = reinterpret_cast<int32_t*>(ws);
+    rowsum_i8_kernel<<<(unsigned)std::min<int64_t>((M + 7) / 8, 148 * 16), 256, 0, st>>>(a, (int)M, (int)K, rs);
+    int rc = check_launch("rowsum_i8_kernel");
+    if (rc) return rc;
+    g.rowsum = rs;
+  }
+  if (M <= 256) return launch_gemm<128, 6>(a, b_nk, g, st);
+  return launch_gemm<256, 4>(a, b_nk, g, st);
+}

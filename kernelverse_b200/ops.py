@@ -263,3 +263,44 @@ def paged_fp8_decode(query, k_cache, v_cache, k_scale, v_scale, seq_lens, block_
     return _paged_attention(query, k_cache, v_cache, seq_lens, block_table, num_kv_heads=hkv, block_size=bs,
                             num_blocks=nb, max_seq_len=max_seq_len, scale=scale, k_scale=k_scale, v_scale=v_scale,
                             k_new=k_new, v_new=v_new, partition_size=partition_size, out_dtype=query.dtype)
+
+
+# --------------------------------------------------------------------------- W8A8 GEMM
+def _gemm(a, b, b_layout, a_scales, b_scales, bias, azp, azp_adj, out_dtype):
+    dev = _cuda(a, b, a_scales, b_scales, bias, azp, azp_adj)
+    a = a.contiguous()
+    b = b.contiguous()
+    m, k = a.shape
+    n = b.shape[0] if b_layout == 0 else b.shape[1]
+    out = torch.empty((m, n), dtype=out_dtype, device=dev)
+    f32 = lambda t: None if t is None else t.to(torch.float32).contiguous()  # noqa: E731
+    a_scales, b_scales, azp, azp_adj = f32(a_scales), f32(b_scales), f32(azp), f32(azp_adj)
+    if bias is not None:
+        bias = bias.contiguous()
+    ws_bytes = _lib.lib().kvb_w8a8_workspace_size(m, n, k, b_layout, int(azp is not None))
+    ws = workspace(dev, ws_bytes)
+    call("kvb_w8a8_scaled_mm", _ptr(a), _ptr(b), b_layout, _ptr(a_scales), _ptr(b_scales), _ptr(bias),
+         kvb_dtype(bias.dtype) if bias is not None else 0, _ptr(azp), _ptr(azp_adj), m, n, k, _ptr(out),
+         kvb_dtype(out_dtype), n, _ptr(ws), ws.numel(), _stream(dev))
+    return out
+
+
+def w8a8_scaled_mm(a: torch.Tensor, b: torch.Tensor, a_scales: torch.Tensor, b_scales: torch.Tensor,
+                   bias: Optional[torch.Tensor] = None, out_dtype: torch.dtype = torch.bfloat16) -> torch.Tensor:
+    """BASELINE third config: out = (acc * a_scales[m]) * b_scales[n] + bias[n], acc = a[M,K] . b[N,K]^T (int32)."""
+    return _gemm(a, b, 0, a_scales, b_scales, bias, None, None, out_dtype)
+
+
+def w8a8_int32_acc(a: torch.Tensor, b: torch.Tensor) -> torch.Tensor:
+    """The exact int32 accumulator a[M,K] . b[N,K]^T of the W8A8 GEMM."""
+    return _gemm(a, b, 0, None, None, None, None, None, torch.int32)
+
+
+def int8_scaled_mm_azp(a, b, a_scales, b_scales, azp_adj, azp, bias, has_azp: bool, has_bias: bool,
+                       output_dtype: torch.dtype):
+    """operators/gemm/int8_scaled_mm_azp/int8_scaled_mm_azp.py:61-85 (b is [K, N]; azp_adj always added)."""
+    m, n = a.shape[0], b.shape[1]
+    if a_scales.numel() != m or b_scales.numel() != n:
+        raise ValueError("a_scales must have M entries and b_scales N entries")
+    return _gemm(a, b, 1, a_scales.reshape(-1), b_scales.reshape(-1), bias.reshape(-1) if has_bias else None,
+                 azp.reshape(-1) if has_azp else None, azp_adj.reshape(-1), output_dtype)

@@ -1,0 +1,122 @@
+"""GPU parity of the tcgen05 W8A8 GEMM against the oracle.
+
+The int32 accumulator and the bf16 epilogue ((acc * sa) * sb + bias, one float32 rounding per
+step) are bit-exact.  The reference drop-in (int8_scaled_mm_azp: b [K, N], zero point,
+azp_adj) is compared with the float64 oracle at the reference's own tolerances
+(config.json: FP32 5e-4, FP16 1e-2, BF16 1.5e-2 / 1e-2).
+"""
+import numpy as np
+import pytest
+import torch
+
+from conftest import golden_names, load_golden
+from gpu_util import TORCH_DT, dev, host, require_gpu, seeded
+from oracle import gemm
+
+pytestmark = pytest.mark.gpu
+
+
+@pytest.fixture(autouse=True)
+def _gpu():
+    require_gpu()
+
+
+def _ops():
+    from kernelverse_b200 import ops
+    return ops
+
+
+def _i8(rng, shape, lo=-127, hi=128):
+    return rng.integers(lo, hi, shape).astype(np.int8)
+
+
+def _scales(rng, n):
+    return (rng.random(n) * 9e-3 + 1e-3).astype(np.float32)
+
+
+@pytest.mark.parametrize("name", golden_names("w8a8"))
+def test_w8a8_golden(name):
+    meta, g = load_golden(name)
+    a, b = dev(g["a"][0]), dev(g["b"][0])
+    acc = _ops().w8a8_int32_acc(a, b)
+    np.testing.assert_array_equal(host(acc), g["acc"][0])
+    out = _ops().w8a8_scaled_mm(a, b, dev(g["sa"][0]), dev(g["sb"][0]), dev(g["bias"][0], torch.bfloat16))
+    np.testing.assert_array_equal(host(out), g["out"][0])
+
+
+@pytest.mark.parametrize("name", golden_names("int8_scaled_mm_azp"))
+def test_int8_scaled_mm_azp_golden(name):
+    meta, g = load_golden(name)
+    ins = [dev(g[k][0]) for k in ("a", "b", "a_scales", "b_scales", "azp_adj", "azp", "bias")]
+    dt = TORCH_DT[meta["output_dtype"]]
+    out = _ops().int8_scaled_mm_azp(*ins, meta["has_azp"], meta["has_bias"], dt)
+    assert out.dtype == dt
+    tol = {"FP32": (5e-4, 5e-4), "FP16": (1e-2, 1e-2), "BF16": (1.5e-2, 1e-2)}[meta["output_dtype"]]
+    np.testing.assert_allclose(host(out), g["out"][0].astype(np.float32), rtol=tol[0], atol=tol[1])
+
+
+@pytest.mark.parametrize("M,N,K", [(1, 64, 16), (16, 256, 128), (129, 300, 48), (200, 128, 8208), (256, 1000, 256),
+                                   (300, 512, 1024), (5, 17, 32), (1024, 2048, 4096)])
+def test_w8a8_shapes_exact(M, N, K):
+    rng = seeded(M * 7 + N + K)
+    a, b = _i8(rng, (M, K)), _i8(rng, (N, K))
+    sa, sb = _scales(rng, M), _scales(rng, N)
+    bias = (0.1 * rng.standard_normal(N)).astype(np.float32)
+    from oracle.numerics import round_bf16
+    bias = round_bf16(bias)
+    at, bt = dev(a), dev(b)
+    acc = _ops().w8a8_int32_acc(at, bt)
+    ref_acc = gemm.w8a8_acc(a, b)
+    np.testing.assert_array_equal(host(acc), ref_acc)
+    out = _ops().w8a8_scaled_mm(at, bt, dev(sa), dev(sb), dev(bias, torch.bfloat16))
+    np.testing.assert_array_equal(host(out), gemm.w8a8_scaled_mm(a, b, sa, sb, bias, "BF16", acc=ref_acc))
+
+
+@pytest.mark.parametrize("M", [16, 256, 4096])
+def test_w8a8_baseline_config_full_size(M):
+    """BASELINE third config: K = 8192, N = 28672; bit-exact oracle rows + full int32 check."""
+    N, K = 28672, 8192
+    rng = seeded(M)
+    a, b = _i8(rng, (M, K)), _i8(rng, (N, K))
+    sa, sb = _scales(rng, M), _scales(rng, N)
+    from oracle.numerics import round_bf16
+    bias = round_bf16((0.1 * rng.standard_normal(N)).astype(np.float32))
+    at, bt = dev(a), dev(b)
+    out = _ops().w8a8_scaled_mm(at, bt, dev(sa), dev(sb), dev(bias, torch.bfloat16))
+    rows = np.unique(np.concatenate([np.arange(min(M, 8)), rng.integers(0, M, 24)]))
+    ref = gemm.w8a8_scaled_mm(a[rows], b, sa[rows], sb, bias, "BF16")
+    np.testing.assert_array_equal(host(out)[rows], ref)
+    # every accumulator, checked against the library int8 GEMM (cuBLASLt via torch._int_mm)
+    acc = _ops().w8a8_int32_acc(at, bt)
+    if M > 16:
+        assert torch.equal(acc, torch._int_mm(at, bt.t()))
+    else:
+        pad = torch.zeros((32, K), dtype=torch.int8, device="cuda")
+        pad[:M] = at
+        assert torch.equal(acc, torch._int_mm(pad, bt.t())[:M])
+
+
+@pytest.mark.parametrize("dt", ["FP32", "FP16", "BF16"])
+@pytest.mark.parametrize("has_azp,has_bias", [(True, True), (False, True), (True, False), (False, False)])
+def test_int8_scaled_mm_azp_kn_layout(dt, has_azp, has_bias):
+    rng = seeded(3)
+    M, N, K = 300, 1000, 2048
+    a = rng.integers(-64, 64, (M, K)).astype(np.int8)
+    b = rng.integers(-64, 64, (K, N)).astype(np.int8)
+    sa = (rng.random(M) * 0.02 + 0.001).astype(np.float32)
+    sb = (rng.random(N) * 0.02 + 0.001).astype(np.float32)
+    adj = (rng.standard_normal(N) * 0.01).astype(np.float32)
+    azp = rng.integers(-8, 8, N).astype(np.float32)
+    bias = (rng.standard_normal(N) * 0.01).astype(np.float32)
+    out = _ops().int8_scaled_mm_azp(dev(a), dev(b), dev(sa), dev(sb), dev(adj), dev(azp), dev(bias), has_azp, has_bias,
+                                    TORCH_DT[dt])
+    ref = gemm.int8_scaled_mm_azp(a, b, sa, sb, adj, azp, bias, has_azp, has_bias, dt)
+    tol = {"FP32": (5e-4, 5e-4), "FP16": (1e-2, 1e-2), "BF16": (1.5e-2, 1e-2)}[dt]
+    np.testing.assert_allclose(host(out), ref, rtol=tol[0], atol=tol[1])
+
+
+def test_w8a8_rejects_bad_k():
+    from kernelverse_b200 import _lib
+    a = torch.zeros((4, 24), dtype=torch.int8, device="cuda")
+    with pytest.raises(_lib.KvbError, match="multiple of 16"):
+        _ops().w8a8_int32_acc(a, a)
