@@ -242,7 +242,7 @@ __global__ void __launch_bounds__(kThreads, 1) w8a8_gemm_kernel(const __grid_con
       tile_coords(g, t, mb, nb);
       const int m = mb * kBM + q * 32 + lane;
       const bool mrow = m < g.M;
-      const float sa = mrow ? g.sa[m] : 0.0f;
+      const float sa = (mrow && g.sa) ? g.sa[m] : 0.0f;   // no scales in int32-accumulator mode
       const int32_t rs = (g.azp && mrow) ? g.rowsum[m] : 0;
 #pragma unroll 1
       for (int c0 = 0; c0 < BN; c0 += 32) {
