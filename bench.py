@@ -239,6 +239,60 @@ def c4_bytes(c, hq=32, hkv=8, d=128) -> int:
             + b * 4 + 2 * hkv * 4)              # seq_lens, scales
 
 
+def make_c3_inputs(torch, dev, seed: int, M: int, N: int = 28672, K: int = 8192):
+    """BASELINE third config: int8 uniform in [-127, 127], scales U(1e-3, 1e-2), bias N(0, 0.1) bf16."""
+    g = torch.Generator(device=dev).manual_seed(seed)
+    a = torch.randint(-127, 128, (M, K), generator=g, device=dev, dtype=torch.int8)
+    b = torch.randint(-127, 128, (N, K), generator=g, device=dev, dtype=torch.int8)
+    sa = torch.rand((M,), generator=g, device=dev) * 9e-3 + 1e-3
+    sb = torch.rand((N,), generator=g, device=dev) * 9e-3 + 1e-3
+    bias = (0.1 * torch.randn((N,), generator=g, device=dev)).to(torch.bfloat16)
+    return a, b, sa, sb, bias
+
+
+def time_fn(torch, fn, iters: int, warm: int = 3) -> float:
+    """Mean microseconds per call of back-to-back launches (CUDA events on the current stream)."""
+    stream = torch.cuda.current_stream()
+    for _ in range(warm):
+        fn()
+    torch.cuda.synchronize()
+    s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    s.record(stream)
+    for _ in range(iters):
+        fn()
+    e.record(stream)
+    torch.cuda.synchronize()
+    return s.elapsed_time(e) / iters * 1e3
+
+
+def gemm_benchmarks(torch, ops, hbm_peak):
+    """BASELINE third config at M = 16, 256, 4096 plus the library int8 GEMM as the measured int8 peak."""
+    dev = torch.device("cuda")
+    res = []
+    N, K = 28672, 8192
+    lib_tops = None
+    for M in (4096, 256, 16):
+        a, b, sa, sb, bias = make_c3_inputs(torch, dev, 21 + M, M)
+        us = time_fn(torch, lambda: ops.w8a8_scaled_mm(a, b, sa, sb, bias), 20 if M == 4096 else 50)
+        ops_ = 2 * M * N * K
+        nbytes = M * K + N * K + M * N * 2 + M * 4 + N * 4 + N * 2
+        entry = {"workload": f"W8A8 GEMM M={M}, N={N}, K={K}, bf16 out (BASELINE config 3)",
+                 "kernel": "w8a8_gemm_kernel<%d>" % (256 if M > 256 else 128), "us_per_call": round(us, 2),
+                 "tops": round(ops_ / us / 1e6, 1), "bytes_per_call": nbytes,
+                 "achieved_gbs": round(nbytes / us / 1e3, 1), "hbm_frac": round(nbytes / us / 1e3 / hbm_peak, 4)}
+        if M == 4096:
+            bt = b.t()
+            lus = time_fn(torch, lambda: torch._int_mm(a, bt), 20)
+            lib_tops = ops_ / lus / 1e6
+            entry["library_int8_tops"] = round(lib_tops, 1)
+            entry["library"] = "torch._int_mm (cuBLASLt int8, int32 out, same shape)"
+            entry["frac_of_library_int8"] = round(entry["tops"] / lib_tops, 4)
+            entry["frac_of_nominal_4500_tops"] = round(entry["tops"] / 4500.0, 4)
+        res.append(entry)
+        del a, b
+    return res
+
+
 def secondary_benchmarks(torch, ops, hbm_peak):
     """Other hot-path kernels at their BASELINE configs (1 GPU)."""
     out = []
@@ -312,7 +366,7 @@ def main():
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--profile-only", action="store_true",
                     help="run W warm-up + K steps of the headline kernel and exit (for ncu captures)")
-    ap.add_argument("--profile-workload", choices=["c2", "c4"], default="c2",
+    ap.add_argument("--profile-workload", choices=["c2", "c4", "c3m16", "c3m256", "c3m4096"], default="c2",
                     help="workload that --profile-only runs")
     args = ap.parse_args()
     if args.warmup < 3:
@@ -363,6 +417,12 @@ def main():
                                              c["bt"], k_new=c["k_new"], v_new=c["v_new"], max_seq_len=c["max_len"])
         for _ in range(args.warmup + args.steps):
             step4()
+        torch.cuda.synchronize()
+        return
+    if args.profile_only and args.profile_workload.startswith("c3m"):
+        a3, b3, sa3, sb3, bias3 = make_c3_inputs(torch, dev, 21, int(args.profile_workload[3:]))
+        for _ in range(args.warmup + args.steps):
+            ops.w8a8_scaled_mm(a3, b3, sa3, sb3, bias3)
         torch.cuda.synchronize()
         return
     x, r, w = make_c2_inputs(torch, dev, seed=1000 + rank)
@@ -422,7 +482,7 @@ def main():
 
     secondary = None
     if world == 1 and not args.no_secondary:
-        secondary = secondary_benchmarks(torch, ops, hbm_peak)
+        secondary = secondary_benchmarks(torch, ops, hbm_peak) + gemm_benchmarks(torch, ops, hbm_peak)
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu:

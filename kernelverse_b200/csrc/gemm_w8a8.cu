@@ -50,11 +50,23 @@ struct GemmArgs {
 };
 
 // ---------------------------------------------------------------- tcgen05 / TMA wrappers
-__device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, int x, int y, uint64_t* bar) {
+__device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, int x, int y, uint64_t* bar,
+                                            uint64_t policy) {
   asm volatile(
-      "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];"
-      ::"r"(smem_u32(dst)), "l"(map), "r"(x), "r"(y), "r"(smem_u32(bar))
+      "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes.L2::cache_hint [%0], [%1, {%2, %3}], "
+      "[%4], %5;"
+      ::"r"(smem_u32(dst)), "l"(map), "r"(x), "r"(y), "r"(smem_u32(bar)), "l"(policy)
       : "memory");
+}
+__device__ __forceinline__ uint64_t policy_evict_last() {
+  uint64_t p;
+  asm volatile("createpolicy.fractional.L2::evict_last.b64 %0, 1.0;" : "=l"(p));
+  return p;
+}
+__device__ __forceinline__ uint64_t policy_evict_normal() {
+  uint64_t p;
+  asm volatile("createpolicy.fractional.L2::evict_normal.b64 %0, 1.0;" : "=l"(p));
+  return p;
 }
 
 __device__ __forceinline__ void tmem_alloc(uint32_t* dst_smem, uint32_t ncols) {
@@ -139,7 +151,9 @@ __global__ void __launch_bounds__(kThreads, 1) w8a8_gemm_kernel(const __grid_con
   constexpr uint32_t kABytes = kBM * kBK;
   constexpr uint32_t kBBytes = BN * kBK;
   constexpr uint32_t kStageBytes = kABytes + kBBytes;
-  constexpr uint32_t kTmemCols = 2 * BN;      // 512 or 256: a power of two >= 32
+  // two accumulator buffers of BN columns; the allocation is a power of two >= 32
+  constexpr uint32_t kTmemCols = 2 * BN <= 32 ? 32 : 2 * BN <= 64 ? 64 : 2 * BN <= 128 ? 128 : 2 * BN <= 256 ? 256 : 512;
+  static_assert(BN % 16 == 0 && BN >= 16 && BN <= 256, "tcgen05 kind::i8 with M=128 needs N % 16 == 0, N <= 256");
   constexpr uint32_t kIdesc = idesc_i8(kBM, BN);
 
   extern __shared__ __align__(1024) uint8_t smem_raw[];
@@ -175,6 +189,9 @@ __global__ void __launch_bounds__(kThreads, 1) w8a8_gemm_kernel(const __grid_con
     if (lane == 0) {
       uint32_t it = 0;
       bool ok = true;
+      // A tiles are re-read by every N block: keep them in L2; B is streamed once when M is small.
+      const uint64_t pol_a = policy_evict_last();
+      const uint64_t pol_b = g.m_blocks <= 2 ? policy_evict_first() : policy_evict_normal();
       for (int t = blockIdx.x; t < g.tiles && ok; t += gridDim.x) {
         int mb, nb;
         tile_coords(g, t, mb, nb);
@@ -187,8 +204,8 @@ __global__ void __launch_bounds__(kThreads, 1) w8a8_gemm_kernel(const __grid_con
           }
           uint8_t* sa_ = smem + s * kStageBytes;
           mbar_arrive_expect_tx(&full[s], kStageBytes);
-          tma_load_2d(sa_, &tmap_a, kb * kBK, mb * kBM, &full[s]);
-          tma_load_2d(sa_ + kABytes, &tmap_b, kb * kBK, nb * BN, &full[s]);
+          tma_load_2d(sa_, &tmap_a, kb * kBK, mb * kBM, &full[s], pol_a);
+          tma_load_2d(sa_ + kABytes, &tmap_b, kb * kBK, nb * BN, &full[s], pol_b);
         }
       }
       // drain: every stage issued must have been consumed before this CTA exits
@@ -251,7 +268,7 @@ __global__ void __launch_bounds__(kThreads, 1) w8a8_gemm_kernel(const __grid_con
         tmem_ld32(tmem_base + ((uint32_t)(q * 32) << 16) + ab * BN + c0, r);
         const int n0 = nb * BN + c0;
         if (!mrow || n0 >= g.N) continue;
-        const int ncols = min(32, g.N - n0);
+        const int ncols = min(min(32, BN - c0), g.N - n0);   // BN need not be a multiple of 32
         if (g.out_dtype == KVB_I32) {
           int32_t* o = reinterpret_cast<int32_t*>(g.out) + (int64_t)m * g.ldo + n0;
           if (ncols == 32 && (((uintptr_t)o) & 15) == 0) {
@@ -481,6 +498,8 @@ extern "C" int kvb_w8a8_scaled_mm(const int8_t* a, const int8_t* b, int b_layout
     if (rc) return rc;
     g.rowsum = rs;
   }
-  if (M <= 256) return launch_gemm<128, 6>(a, b_nk, g, st);
+  // Small M streams B from HBM: 208-column tiles make N = 28672 exactly 138 tiles (one wave on
+  // 148 SMs) and keep ~1.9 waves at two M blocks.  Large M is tensor-bound: 256-column tiles.
+  if (M <= 256) return launch_gemm<208, 5>(a, b_nk, g, st);
   return launch_gemm<256, 4>(a, b_nk, g, st);
 }
