@@ -293,6 +293,97 @@ def gemm_benchmarks(torch, ops, hbm_peak):
     return res
 
 
+def multi_gpu_benchmarks(torch, ops, dist, world: int, rank: int, hbm_peak: float):
+    """N > 1: TP W8A8 GEMM (fused all-gather vs GEMM + NCCL all-gather) and balanced batch-sharded decode.
+
+    BASELINE fifth config: M = 4096, K = 8192, N = 57344 split by columns; decode at batch 512 with
+    the fourth config's head layout and context distribution, sequences balanced by context length.
+    Times are device times (CUDA events), max over ranks.
+    """
+    from kernelverse_b200.sharding import TPW8A8, balance_sequences, column_shard
+    dev = torch.device("cuda", torch.cuda.current_device())
+    res = []
+    M, N, K = 4096, 57344, 8192
+    g = torch.Generator(device=dev).manual_seed(5)
+    a = torch.randint(-127, 128, (M, K), generator=g, device=dev, dtype=torch.int8)
+    sa = torch.rand((M,), generator=g, device=dev) * 9e-3 + 1e-3
+    n0, nw = column_shard(N, world, rank)
+    gr = torch.Generator(device=dev).manual_seed(100 + rank)
+    b = torch.randint(-127, 128, (nw, K), generator=gr, device=dev, dtype=torch.int8)
+    sb = torch.rand((nw,), generator=gr, device=dev) * 9e-3 + 1e-3
+    bias = (0.1 * torch.randn((nw,), generator=gr, device=dev)).to(torch.bfloat16)
+    tp = TPW8A8(dist.group.WORLD, M, b, sb, bias)
+
+    def timed(fn, iters):
+        for _ in range(3):
+            fn()
+        ms, _, _ = time_region(torch, fn, iters, dist, world)
+        return ms / iters * 1e3
+
+    us_fused = timed(lambda: tp(a, sa), 10)
+    gathered = torch.empty((world, M, nw), dtype=torch.bfloat16, device=dev)
+
+    def nccl_step():
+        local = ops.w8a8_scaled_mm(a, b, sa, sb, bias)
+        dist.all_gather_into_tensor(gathered, local)
+    us_nccl = timed(nccl_step, 10)
+    us_gemm = timed(lambda: ops.w8a8_scaled_mm(a, b, sa, sb, bias), 10)
+    ops_total = 2 * M * N * K
+    recv = (world - 1) * M * nw * 2
+    res.append({"workload": f"TP W8A8 GEMM M={M}, N={N} (x{world} column shards of {nw}), K={K}, bf16 out "
+                            "(BASELINE config 5a)",
+                "us_fused_gemm_allgather": round(us_fused, 1), "us_gemm_then_nccl_allgather": round(us_nccl, 1),
+                "us_gemm_only": round(us_gemm, 1), "tops_fused": round(ops_total / us_fused / 1e6, 1),
+                "bytes_received_per_rank": recv,
+                "nvlink_gbs_per_rank_fused": round(recv / us_fused / 1e3, 1),
+                "note": "fused = kvb_w8a8_scaled_mm_allgather (peer stores from the epilogue into symmetric memory)"})
+    del tp, gathered, a, b
+    torch.cuda.empty_cache()
+    # batch-sharded decode, batch 512 balanced by context length
+    gl = torch.Generator(device="cpu").manual_seed(77)
+    lens_all = torch.randint(512, 8193, (512,), generator=gl, dtype=torch.int32)
+    mine = balance_sequences(lens_all.tolist(), world)[rank]
+    c = make_c4_sharded(torch, dev, lens_all[torch.from_numpy(mine)], 300 + rank)
+    step = lambda: ops.paged_fp8_decode(c["q"], c["kc"], c["vc"], c["ks"], c["vs"], c["lens"], c["bt"],  # noqa: E731
+                                        k_new=c["k_new"], v_new=c["v_new"], max_seq_len=c["max_len"])
+    us = timed(step, 10)
+    tot = torch.tensor([float(c4_bytes(c))], device=dev, dtype=torch.float64)
+    dist.all_reduce(tot)
+    res.append({"workload": f"batch-sharded paged FP8 decode, batch 512 over {world} GPUs, balanced by context "
+                            "(BASELINE config 5b)", "us_per_step": round(us, 1),
+                "bytes_all_ranks": int(tot.item()), "achieved_gbs_all_ranks": round(tot.item() / us / 1e3, 1),
+                "frac_of_world_hbm": round(tot.item() / us / 1e3 / (hbm_peak * world), 4)})
+    return res
+
+
+def make_c4_sharded(torch, dev, lens, seed: int, hq: int = 32, hkv: int = 8, d: int = 128, bs: int = 16):
+    """Decode inputs for a given set of context lengths (one rank's share of a larger batch)."""
+    batch = len(lens)
+    g = torch.Generator(device="cpu").manual_seed(seed)
+    nblk = ((lens + bs - 1) // bs)
+    total = int(nblk.sum())
+    maxb = int(nblk.max())
+    perm = torch.randperm(total, generator=g, dtype=torch.int64).to(torch.int32)
+    bt = torch.zeros((batch, maxb), dtype=torch.int32)
+    pos = 0
+    for i in range(batch):
+        n = int(nblk[i])
+        bt[i, :n] = perm[pos:pos + n]
+        pos += n
+    gd = torch.Generator(device=dev).manual_seed(seed)
+    k_scale = torch.rand((hkv,), generator=gd, device=dev) * 0.01 + 0.005
+    v_scale = torch.rand((hkv,), generator=gd, device=dev) * 0.01 + 0.005
+    kc = (torch.randn((total, bs, hkv, d), generator=gd, device=dev) / k_scale[None, None, :, None]).clamp(-448, 448).to(
+        torch.float8_e4m3fn)
+    vc = (torch.randn((total, bs, hkv, d), generator=gd, device=dev) / v_scale[None, None, :, None]).clamp(-448, 448).to(
+        torch.float8_e4m3fn)
+    return dict(q=torch.randn((batch, hq, d), generator=gd, device=dev).to(torch.bfloat16), kc=kc, vc=vc, ks=k_scale,
+                vs=v_scale, lens=lens.to(dev), bt=bt.to(dev),
+                k_new=torch.randn((batch, hkv, d), generator=gd, device=dev).to(torch.bfloat16),
+                v_new=torch.randn((batch, hkv, d), generator=gd, device=dev).to(torch.bfloat16),
+                sum_ctx=int(lens.sum()), sum_blocks=total, max_len=maxb * bs)
+
+
 def secondary_benchmarks(torch, ops, hbm_peak):
     """Other hot-path kernels at their BASELINE configs (1 GPU)."""
     out = []
@@ -483,6 +574,8 @@ def main():
     secondary = None
     if world == 1 and not args.no_secondary:
         secondary = secondary_benchmarks(torch, ops, hbm_peak) + gemm_benchmarks(torch, ops, hbm_peak)
+    elif world > 1 and not args.no_secondary:
+        secondary = multi_gpu_benchmarks(torch, ops, dist, world, rank, hbm_peak)
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu:

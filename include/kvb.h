@@ -149,6 +149,22 @@ KVB_API int kvb_w8a8_scaled_mm(const int8_t* a, const int8_t* b, int b_layout, c
                                const float* azp_adj, int64_t M, int64_t N, int64_t K, void* out, int out_dtype,
                                int64_t ldo, void* workspace, size_t workspace_bytes, void* stream);
 
+/*
+ * Column-sharded tensor-parallel W8A8 GEMM with the all-gather fused into its epilogue
+ * (BASELINE fifth config; no reference counterpart -- the reference has no multi-GPU code).
+ * Rank `rank` of `world` (<= 8) holds b_shard [N_shard, K] (columns rank*N_shard ... of the
+ * full weight), its b_scales_shard / bias_shard, and the replicated a [M, K], a_scales [M].
+ * out_ptrs[r] is rank r's output buffer [M, ldo] (ldo >= world * N_shard), mapped into this
+ * process (e.g. symmetric memory); every finished tile is stored into all `world` buffers at
+ * columns rank*N_shard + n with plain peer stores over NVLink, then fenced at system scope.
+ * The caller must order the kernels of all ranks before reading (e.g. a small collective on
+ * the same stream after the call).  Same epilogue and exactness as kvb_w8a8_scaled_mm.
+ */
+KVB_API int kvb_w8a8_scaled_mm_allgather(const int8_t* a, const int8_t* b_shard, const float* a_scales,
+                                         const float* b_scales_shard, const void* bias_shard, int bias_dtype,
+                                         int64_t M, int64_t N_shard, int64_t K, void* const* out_ptrs, int world,
+                                         int rank, int64_t ldo, int out_dtype, void* stream);
+
 /* ---------------------------------------------------------------- paged KV-cache writes */
 
 /*

@@ -47,7 +47,17 @@ struct GemmArgs {
   int64_t ldo;
   int out_dtype;         // KVB_BF16 / KVB_F16 / KVB_F32 / KVB_I32
   int n_blocks, m_blocks, tiles;
+  // Fused all-gather: every output tile is also stored into these peer buffers (same layout,
+  // columns offset by col_off).  nout == 0 for a plain GEMM.
+  int nout;
+  int64_t col_off;
+  void* outs[8];
 };
+
+template <typename V>
+__device__ __forceinline__ V* dst_ptr(const GemmArgs& g, int d, int64_t m, int64_t n) {
+  return reinterpret_cast<V*>(d < 0 ? g.out : g.outs[d]) + m * g.ldo + g.col_off + n;
+}
 
 // ---------------------------------------------------------------- tcgen05 / TMA wrappers
 __device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, int x, int y, uint64_t* bar,
@@ -270,14 +280,16 @@ __global__ void __launch_bounds__(kThreads, 1) w8a8_gemm_kernel(const __grid_con
         if (!mrow || n0 >= g.N) continue;
         const int ncols = min(min(32, BN - c0), g.N - n0);   // BN need not be a multiple of 32
         if (g.out_dtype == KVB_I32) {
-          int32_t* o = reinterpret_cast<int32_t*>(g.out) + (int64_t)m * g.ldo + n0;
-          if (ncols == 32 && (((uintptr_t)o) & 15) == 0) {
+          for (int d = g.nout ? 0 : -1; d < g.nout; ++d) {
+            int32_t* o = dst_ptr<int32_t>(g, d, m, n0);
+            if (ncols == 32 && (((uintptr_t)o) & 15) == 0) {
 #pragma unroll
-            for (int j = 0; j < 32; j += 4) *reinterpret_cast<uint4*>(o + j) = make_uint4(r[j], r[j + 1], r[j + 2], r[j + 3]);
-          } else {
+              for (int j = 0; j < 32; j += 4) *reinterpret_cast<uint4*>(o + j) = make_uint4(r[j], r[j + 1], r[j + 2], r[j + 3]);
+            } else {
 #pragma unroll
-            for (int j = 0; j < 32; ++j)
-              if (j < ncols) o[j] = (int32_t)r[j];
+              for (int j = 0; j < 32; ++j)
+                if (j < ncols) o[j] = (int32_t)r[j];
+            }
           }
           continue;
         }
@@ -304,24 +316,28 @@ __global__ void __launch_bounds__(kThreads, 1) w8a8_gemm_kernel(const __grid_con
               pk[j] = *reinterpret_cast<uint32_t*>(&h);
             }
           }
-          uint16_t* o = reinterpret_cast<uint16_t*>(g.out) + (int64_t)m * g.ldo + n0;
-          if (ncols == 32 && (((uintptr_t)o) & 15) == 0) {
+          for (int d = g.nout ? 0 : -1; d < g.nout; ++d) {
+            uint16_t* o = dst_ptr<uint16_t>(g, d, m, n0);
+            if (ncols == 32 && (((uintptr_t)o) & 15) == 0) {
 #pragma unroll
-            for (int j = 0; j < 16; j += 4) *reinterpret_cast<uint4*>(o + 2 * j) = make_uint4(pk[j], pk[j + 1], pk[j + 2], pk[j + 3]);
-          } else {
+              for (int j = 0; j < 16; j += 4) *reinterpret_cast<uint4*>(o + 2 * j) = make_uint4(pk[j], pk[j + 1], pk[j + 2], pk[j + 3]);
+            } else {
 #pragma unroll
-            for (int j = 0; j < 32; ++j)
-              if (j < ncols) o[j] = (uint16_t)(pk[j >> 1] >> ((j & 1) * 16));
+              for (int j = 0; j < 32; ++j)
+                if (j < ncols) o[j] = (uint16_t)(pk[j >> 1] >> ((j & 1) * 16));
+            }
           }
         } else {
-          float* o = reinterpret_cast<float*>(g.out) + (int64_t)m * g.ldo + n0;
-          if (ncols == 32 && (((uintptr_t)o) & 15) == 0) {
+          for (int d = g.nout ? 0 : -1; d < g.nout; ++d) {
+            float* o = dst_ptr<float>(g, d, m, n0);
+            if (ncols == 32 && (((uintptr_t)o) & 15) == 0) {
 #pragma unroll
-            for (int j = 0; j < 32; j += 4) *reinterpret_cast<float4*>(o + j) = make_float4(f[j], f[j + 1], f[j + 2], f[j + 3]);
-          } else {
+              for (int j = 0; j < 32; j += 4) *reinterpret_cast<float4*>(o + j) = make_float4(f[j], f[j + 1], f[j + 2], f[j + 3]);
+            } else {
 #pragma unroll
-            for (int j = 0; j < 32; ++j)
-              if (j < ncols) o[j] = f[j];
+              for (int j = 0; j < 32; ++j)
+                if (j < ncols) o[j] = f[j];
+            }
           }
         }
       }
@@ -330,6 +346,7 @@ __global__ void __launch_bounds__(kThreads, 1) w8a8_gemm_kernel(const __grid_con
       if (lane == 0) mbar_arrive(&tmem_empty[ab]);
     }
   }
+  if (g.nout > 1 && warp >= 2) __threadfence_system();   // peer stores visible before the kernel completes
   tc_fence_before();
   __syncthreads();
   if (warp == 1) {
@@ -446,6 +463,36 @@ bool is_sm100() {
 }  // namespace kvb
 
 using namespace kvb;
+
+extern "C" int kvb_w8a8_scaled_mm_allgather(const int8_t* a, const int8_t* b_shard, const float* a_scales,
+                                            const float* b_scales_shard, const void* bias_shard, int bias_dtype,
+                                            int64_t M, int64_t N_shard, int64_t K, void* const* out_ptrs, int world,
+                                            int rank, int64_t ldo, int out_dtype, void* stream) {
+  if (world < 1 || world > 8 || rank < 0 || rank >= world) return set_error(KVB_E_ARG, "w8a8_allgather: world 1..8, 0 <= rank < world");
+  if (!out_ptrs) return set_error(KVB_E_ARG, "w8a8_allgather: null out_ptrs");
+  for (int r = 0; r < world; ++r)
+    if (!out_ptrs[r]) return set_error(KVB_E_ARG, "w8a8_allgather: null output pointer of rank %d", r);
+  if (M < 0 || N_shard < 0 || K <= 0) return set_error(KVB_E_ARG, "w8a8_allgather: bad sizes");
+  if (M == 0 || N_shard == 0) return KVB_OK;
+  if (ldo < (int64_t)world * N_shard) return set_error(KVB_E_SHAPE, "w8a8_allgather: ldo < world * N_shard");
+  if (!a || !b_shard || (out_dtype != KVB_I32 && (!a_scales || !b_scales_shard)))
+    return set_error(KVB_E_ARG, "w8a8_allgather: null pointer");
+  if (out_dtype != KVB_BF16 && out_dtype != KVB_F16 && out_dtype != KVB_F32 && out_dtype != KVB_I32)
+    return set_error(KVB_E_DTYPE, "w8a8_allgather: out dtype %d", out_dtype);
+  if (K % 16 != 0) return set_error(KVB_E_SHAPE, "w8a8_allgather: K must be a multiple of 16");
+  if (!aligned16(a) || !aligned16(b_shard)) return set_error(KVB_E_ALIGN, "w8a8_allgather: A/B must be 16-byte aligned");
+  if (!is_sm100()) return set_error(KVB_E_DEVICE, "w8a8_allgather: needs an sm_100 device");
+  GemmArgs g{};
+  g.M = (int)M; g.N = (int)N_shard; g.K = (int)K;
+  g.sa = a_scales; g.sb = b_scales_shard; g.bias = bias_shard; g.bias_dtype = bias_dtype;
+  g.out = out_ptrs[rank]; g.ldo = ldo; g.out_dtype = out_dtype;
+  g.nout = world;
+  g.col_off = (int64_t)rank * N_shard;
+  for (int d = 0; d < world; ++d) g.outs[d] = out_ptrs[(rank + d) % world];   // own buffer first, then peers in turn
+  cudaStream_t st = as_stream(stream);
+  if (M <= 256) return launch_gemm<208, 5>(a, b_shard, g, st);
+  return launch_gemm<256, 4>(a, b_shard, g, st);
+}
 
 extern "C" size_t kvb_w8a8_workspace_size(int64_t M, int64_t N, int64_t K, int b_layout, int has_azp) {
   size_t n = 256;
