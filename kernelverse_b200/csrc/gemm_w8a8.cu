@@ -21,6 +21,7 @@
 #include <cuda.h>
 #include <cudaTypedefs.h>
 
+#include <cstring>
 #include <mutex>
 
 #include "kvb_common.cuh"
@@ -52,7 +53,21 @@ struct GemmArgs {
   int nout;
   int64_t col_off;
   void* outs[8];
+  int tma_store;         // 1: full 128-byte output chunks go through TMA tensor stores (omaps)
+  int ndest;             // number of valid output maps (destinations) for the TMA-store path
 };
+
+// Output tensor maps, one per destination buffer (own buffer first), for TMA stores of
+// [32 rows x 128 B] chunks with 128-byte swizzle.
+struct OutMaps {
+  CUtensorMap m[8];
+};
+
+__device__ __forceinline__ void tma_store_2d(const CUtensorMap* map, const void* src, int x, int y) {
+  asm volatile("cp.async.bulk.tensor.2d.global.shared::cta.bulk_group [%0, {%1, %2}], [%3];"
+               ::"l"(map), "r"(x), "r"(y), "r"(smem_u32(src))
+               : "memory");
+}
 
 template <typename V>
 __device__ __forceinline__ V* dst_ptr(const GemmArgs& g, int d, int64_t m, int64_t n) {
@@ -154,10 +169,48 @@ __device__ __forceinline__ float load_bias(const void* p, int dt, int n) {
   return reinterpret_cast<const float*>(p)[n];
 }
 
+// Scale / bias / convert 32 accumulator columns starting at global column n0 into output
+// words: 32 words for 32-bit outputs, 16 packed pairs for 16-bit outputs.
+__device__ __forceinline__ void epilogue32(const GemmArgs& g, const uint32_t (&r)[32], int n0, float sa, int32_t rs,
+                                           uint32_t* w) {
+  if (g.out_dtype == KVB_I32) {
+#pragma unroll
+    for (int j = 0; j < 32; ++j) w[j] = r[j];
+    return;
+  }
+  float f[32];
+#pragma unroll
+  for (int j = 0; j < 32; ++j) {
+    const int n = n0 + j < g.N ? n0 + j : g.N - 1;
+    int32_t acc = (int32_t)r[j];
+    if (g.azp) acc -= (int32_t)g.azp[n] * rs;
+    float y = __fmul_rn(__fmul_rn((float)acc, sa), g.sb[n]);
+    if (g.azp_adj) y = __fadd_rn(y, g.azp_adj[n]);
+    if (g.bias) y = __fadd_rn(y, load_bias(g.bias, g.bias_dtype, n));
+    f[j] = y;
+  }
+  if (g.out_dtype == KVB_F32) {
+#pragma unroll
+    for (int j = 0; j < 32; ++j) w[j] = __float_as_uint(f[j]);
+  } else {
+#pragma unroll
+    for (int j = 0; j < 16; ++j) {
+      if (g.out_dtype == KVB_BF16) {
+        __nv_bfloat162 h = __floats2bfloat162_rn(f[2 * j], f[2 * j + 1]);
+        w[j] = *reinterpret_cast<uint32_t*>(&h);
+      } else {
+        __half2 h = __floats2half2_rn(f[2 * j], f[2 * j + 1]);
+        w[j] = *reinterpret_cast<uint32_t*>(&h);
+      }
+    }
+  }
+}
+
 template <int BN, int STAGES>
 __global__ void __launch_bounds__(kThreads, 1) w8a8_gemm_kernel(const __grid_constant__ CUtensorMap tmap_a,
                                                                  const __grid_constant__ CUtensorMap tmap_b,
-                                                                 const __grid_constant__ GemmArgs g) {
+                                                                 const __grid_constant__ GemmArgs g,
+                                                                 const __grid_constant__ OutMaps om) {
   constexpr uint32_t kABytes = kBM * kBK;
   constexpr uint32_t kBBytes = BN * kBK;
   constexpr uint32_t kStageBytes = kABytes + kBBytes;
@@ -259,7 +312,12 @@ __global__ void __launch_bounds__(kThreads, 1) w8a8_gemm_kernel(const __grid_con
     }
   } else {
     // ------------------------------------------------------------ epilogue (warps 2..5)
+    // Each warp owns 32 TMEM lanes (= 32 output rows) and two 4 KB staging buffers.
     const int q = warp & 3;                 // TMEM lane quarter this warp may access
+    const int esize = (g.out_dtype == KVB_I32 || g.out_dtype == KVB_F32) ? 4 : 2;
+    const int CW = 128 / esize;             // columns per 128-byte chunk
+    uint8_t* stage_base = smem + (size_t)STAGES * kStageBytes + (size_t)q * 8192;
+    int sbuf = 0;
     uint32_t local = 0;
     for (int t = blockIdx.x; t < g.tiles; t += gridDim.x, ++local) {
       const uint32_t ab = local & 1u, v = local >> 1;
@@ -272,72 +330,54 @@ __global__ void __launch_bounds__(kThreads, 1) w8a8_gemm_kernel(const __grid_con
       const float sa = (mrow && g.sa) ? g.sa[m] : 0.0f;   // no scales in int32-accumulator mode
       const int32_t rs = (g.azp && mrow) ? g.rowsum[m] : 0;
 #pragma unroll 1
-      for (int c0 = 0; c0 < BN; c0 += 32) {
+      for (int c0 = 0; c0 < BN; c0 += CW) {
+        const int n0 = nb * BN + c0;
+        uint32_t w[32];
         uint32_t r[32];
         __syncwarp();                       // tcgen05.ld is .sync.aligned: reconverge first
         tmem_ld32(tmem_base + ((uint32_t)(q * 32) << 16) + ab * BN + c0, r);
-        const int n0 = nb * BN + c0;
-        if (!mrow || n0 >= g.N) continue;
-        const int ncols = min(min(32, BN - c0), g.N - n0);   // BN need not be a multiple of 32
-        if (g.out_dtype == KVB_I32) {
-          for (int d = g.nout ? 0 : -1; d < g.nout; ++d) {
-            int32_t* o = dst_ptr<int32_t>(g, d, m, n0);
-            if (ncols == 32 && (((uintptr_t)o) & 15) == 0) {
+        epilogue32(g, r, n0, sa, rs, w);
+        if (esize == 2 && c0 + 32 < BN) {
+          __syncwarp();
+          tmem_ld32(tmem_base + ((uint32_t)(q * 32) << 16) + ab * BN + c0 + 32, r);
+          epilogue32(g, r, n0 + 32, sa, rs, w + 16);
+        }
+        if (n0 >= g.N) continue;
+        const bool full_chunk = c0 + CW <= BN && n0 + CW <= g.N;
+        if (g.tma_store && full_chunk) {
+          // Stage the warp's [32 x 128 B] chunk with the 128-byte swizzle, then one TMA store per
+          // destination; rows past M are clipped by the tensor map.
+          uint8_t* buf = stage_base + sbuf * 4096;
+          if (lane == 0) asm volatile("cp.async.bulk.wait_group.read 1;" ::: "memory");   // buf is free again
+          __syncwarp();
 #pragma unroll
-              for (int j = 0; j < 32; j += 4) *reinterpret_cast<uint4*>(o + j) = make_uint4(r[j], r[j + 1], r[j + 2], r[j + 3]);
-            } else {
-#pragma unroll
-              for (int j = 0; j < 32; ++j)
-                if (j < ncols) o[j] = (int32_t)r[j];
-            }
+          for (int j = 0; j < 8; ++j)
+            *reinterpret_cast<uint4*>(buf + lane * 128 + ((j ^ (lane & 7)) << 4)) =
+                make_uint4(w[4 * j], w[4 * j + 1], w[4 * j + 2], w[4 * j + 3]);
+          asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+          __syncwarp();
+          if (lane == 0) {
+            for (int d = 0; d < g.ndest; ++d)
+              tma_store_2d(&om.m[d], buf, (int)(g.col_off + n0), mb * kBM + q * 32);
+            asm volatile("cp.async.bulk.commit_group;" ::: "memory");
           }
+          sbuf ^= 1;
           continue;
         }
-        float f[32];
+        if (!mrow) continue;
+        // Ragged edge: direct stores of the valid columns to every destination.
+        const int ncols = min(min(CW, BN - c0), g.N - n0);
+        for (int d = g.nout ? 0 : -1; d < g.nout; ++d) {
+          if (esize == 4) {
+            uint32_t* o = dst_ptr<uint32_t>(g, d, m, n0);
 #pragma unroll
-        for (int j = 0; j < 32; ++j) {
-          const int n = n0 + j < g.N ? n0 + j : g.N - 1;
-          int32_t acc = (int32_t)r[j];
-          if (g.azp) acc -= (int32_t)g.azp[n] * rs;
-          float y = __fmul_rn(__fmul_rn((float)acc, sa), g.sb[n]);
-          if (g.azp_adj) y = __fadd_rn(y, g.azp_adj[n]);
-          if (g.bias) y = __fadd_rn(y, load_bias(g.bias, g.bias_dtype, n));
-          f[j] = y;
-        }
-        if (g.out_dtype == KVB_BF16 || g.out_dtype == KVB_F16) {
-          uint32_t pk[16];
-#pragma unroll
-          for (int j = 0; j < 16; ++j) {
-            if (g.out_dtype == KVB_BF16) {
-              __nv_bfloat162 h = __floats2bfloat162_rn(f[2 * j], f[2 * j + 1]);
-              pk[j] = *reinterpret_cast<uint32_t*>(&h);
-            } else {
-              __half2 h = __floats2half2_rn(f[2 * j], f[2 * j + 1]);
-              pk[j] = *reinterpret_cast<uint32_t*>(&h);
-            }
-          }
-          for (int d = g.nout ? 0 : -1; d < g.nout; ++d) {
+            for (int j = 0; j < 32; ++j)
+              if (j < ncols) o[j] = w[j];
+          } else {
             uint16_t* o = dst_ptr<uint16_t>(g, d, m, n0);
-            if (ncols == 32 && (((uintptr_t)o) & 15) == 0) {
 #pragma unroll
-              for (int j = 0; j < 16; j += 4) *reinterpret_cast<uint4*>(o + 2 * j) = make_uint4(pk[j], pk[j + 1], pk[j + 2], pk[j + 3]);
-            } else {
-#pragma unroll
-              for (int j = 0; j < 32; ++j)
-                if (j < ncols) o[j] = (uint16_t)(pk[j >> 1] >> ((j & 1) * 16));
-            }
-          }
-        } else {
-          for (int d = g.nout ? 0 : -1; d < g.nout; ++d) {
-            float* o = dst_ptr<float>(g, d, m, n0);
-            if (ncols == 32 && (((uintptr_t)o) & 15) == 0) {
-#pragma unroll
-              for (int j = 0; j < 32; j += 4) *reinterpret_cast<float4*>(o + j) = make_float4(f[j], f[j + 1], f[j + 2], f[j + 3]);
-            } else {
-#pragma unroll
-              for (int j = 0; j < 32; ++j)
-                if (j < ncols) o[j] = f[j];
-            }
+            for (int j = 0; j < 64; ++j)
+              if (j < ncols) o[j] = (uint16_t)(w[j >> 1] >> ((j & 1) * 16));
           }
         }
       }
@@ -345,6 +385,8 @@ __global__ void __launch_bounds__(kThreads, 1) w8a8_gemm_kernel(const __grid_con
       __syncwarp();
       if (lane == 0) mbar_arrive(&tmem_empty[ab]);
     }
+    if (lane == 0) asm volatile("cp.async.bulk.wait_group 0;" ::: "memory");   // every output write has landed
+    __syncwarp();
   }
   if (g.nout > 1 && warp >= 2) __threadfence_system();   // peer stores visible before the kernel completes
   tc_fence_before();
@@ -423,8 +465,38 @@ int num_sms() {
   return n > 0 ? n : 148;
 }
 
+// Output map over a [rows, cols] row-major buffer with leading dimension ldo (elements):
+// box [32 rows x 128 B], 128-byte swizzle (the epilogue's staging layout).
+int make_out_map(CUtensorMap* map, void* base, int out_dtype, int64_t rows, int64_t cols, int64_t ldo) {
+  auto fn = encode_fn();
+  if (!fn) return set_error(KVB_E_LAUNCH, "w8a8_scaled_mm: cuTensorMapEncodeTiled unavailable");
+  const int es = (out_dtype == KVB_I32 || out_dtype == KVB_F32) ? 4 : 2;
+  const CUtensorMapDataType dt = out_dtype == KVB_BF16   ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16
+                                 : out_dtype == KVB_F16  ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16
+                                 : out_dtype == KVB_F32  ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32
+                                                         : CU_TENSOR_MAP_DATA_TYPE_INT32;
+  cuuint64_t dims[2] = {(cuuint64_t)cols, (cuuint64_t)rows};
+  cuuint64_t strides[1] = {(cuuint64_t)(ldo * es)};
+  cuuint32_t box[2] = {(cuuint32_t)(128 / es), 32u};
+  cuuint32_t estr[2] = {1, 1};
+  CUresult r = fn(map, dt, 2, base, dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                  CU_TENSOR_MAP_L2_PROMOTION_NONE, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return set_error(KVB_E_LAUNCH, "w8a8_scaled_mm: output tensor map failed (%d)", (int)r);
+  return KVB_OK;
+}
+
+// TMA stores need 16-byte aligned bases, row pitches and column offsets.
+bool tma_store_ok(const GemmArgs& g, void* const* dests, int ndest, int64_t map_cols) {
+  const int es = (g.out_dtype == KVB_I32 || g.out_dtype == KVB_F32) ? 4 : 2;
+  if ((g.ldo * es) % 16 || (g.col_off * es) % 16 || ndest > 8 || map_cols > g.ldo) return false;
+  for (int d = 0; d < ndest; ++d)
+    if (!aligned16(dests[d])) return false;
+  return true;
+}
+
 template <int BN, int STAGES>
-int launch_gemm(const int8_t* a, const int8_t* b_nk, GemmArgs& g, cudaStream_t st) {
+int launch_gemm(const int8_t* a, const int8_t* b_nk, GemmArgs& g, void* const* dests, int ndest, int64_t map_cols,
+                cudaStream_t st) {
   CUtensorMap ma, mb;
   int rc = make_map(&ma, a, g.M, g.K, kBM);
   if (rc) return rc;
@@ -433,7 +505,16 @@ int launch_gemm(const int8_t* a, const int8_t* b_nk, GemmArgs& g, cudaStream_t s
   g.m_blocks = (g.M + kBM - 1) / kBM;
   g.n_blocks = (g.N + BN - 1) / BN;
   g.tiles = g.m_blocks * g.n_blocks;
-  const size_t smem = (size_t)STAGES * (kBM * kBK + BN * kBK) + 1024;
+  OutMaps om;
+  memset(&om, 0, sizeof(om));
+  g.tma_store = tma_store_ok(g, dests, ndest, map_cols) ? 1 : 0;
+  g.ndest = g.tma_store ? ndest : 0;
+  for (int d = 0; d < g.ndest; ++d) {
+    rc = make_out_map(&om.m[d], dests[d], g.out_dtype, g.M, map_cols, g.ldo);
+    if (rc) return rc;
+  }
+  constexpr size_t kStaging = 4 * 8192;       // 4 epilogue warps x 2 x [32 rows x 128 B]
+  const size_t smem = (size_t)STAGES * (kBM * kBK + BN * kBK) + kStaging + 1024;
   auto kern = w8a8_gemm_kernel<BN, STAGES>;
   static int set_dev = -1;
   int dev = 0;
@@ -444,7 +525,7 @@ int launch_gemm(const int8_t* a, const int8_t* b_nk, GemmArgs& g, cudaStream_t s
     set_dev = dev;
   }
   const int grid = std::min(g.tiles, num_sms());
-  kern<<<grid, kThreads, smem, st>>>(ma, mb, g);
+  kern<<<grid, kThreads, smem, st>>>(ma, mb, g, om);
   return check_launch("w8a8_gemm_kernel");
 }
 
@@ -488,10 +569,11 @@ extern "C" int kvb_w8a8_scaled_mm_allgather(const int8_t* a, const int8_t* b_sha
   g.out = out_ptrs[rank]; g.ldo = ldo; g.out_dtype = out_dtype;
   g.nout = world;
   g.col_off = (int64_t)rank * N_shard;
-  for (int d = 0; d < world; ++d) g.outs[d] = out_ptrs[(rank + d) % world];   // own buffer first, then peers in turn
+  void* dests[8];
+  for (int d = 0; d < world; ++d) dests[d] = g.outs[d] = out_ptrs[(rank + d) % world];   // own buffer first, then peers
   cudaStream_t st = as_stream(stream);
-  if (M <= 256) return launch_gemm<208, 5>(a, b_shard, g, st);
-  return launch_gemm<256, 4>(a, b_shard, g, st);
+  if (M <= 256) return launch_gemm<208, 4>(a, b_shard, g, dests, world, ldo, st);
+  return launch_gemm<256, 4>(a, b_shard, g, dests, world, ldo, st);
 }
 
 extern "C" size_t kvb_w8a8_workspace_size(int64_t M, int64_t N, int64_t K, int b_layout, int has_azp) {
@@ -547,6 +629,7 @@ extern "C" int kvb_w8a8_scaled_mm(const int8_t* a, const int8_t* b, int b_layout
   }
   // Small M streams B from HBM: 208-column tiles make N = 28672 exactly 138 tiles (one wave on
   // 148 SMs) and keep ~1.9 waves at two M blocks.  Large M is tensor-bound: 256-column tiles.
-  if (M <= 256) return launch_gemm<208, 5>(a, b_nk, g, st);
-  return launch_gemm<256, 4>(a, b_nk, g, st);
+  void* dests[1] = {out};
+  if (M <= 256) return launch_gemm<208, 4>(a, b_nk, g, dests, 1, N, st);
+  return launch_gemm<256, 4>(a, b_nk, g, dests, 1, N, st);
 }
