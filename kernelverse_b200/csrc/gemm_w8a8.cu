@@ -206,7 +206,7 @@ __device__ __forceinline__ void epilogue32(const GemmArgs& g, const uint32_t (&r
   }
 }
 
-template <int BN, int STAGES>
+template <int BN, int STAGES, bool kTmaStore>
 __global__ void __launch_bounds__(kThreads, 1) w8a8_gemm_kernel(const __grid_constant__ CUtensorMap tmap_a,
                                                                  const __grid_constant__ CUtensorMap tmap_b,
                                                                  const __grid_constant__ GemmArgs g,
@@ -344,7 +344,7 @@ __global__ void __launch_bounds__(kThreads, 1) w8a8_gemm_kernel(const __grid_con
         }
         if (n0 >= g.N) continue;
         const bool full_chunk = c0 + CW <= BN && n0 + CW <= g.N;
-        if (g.tma_store && full_chunk) {
+        if (kTmaStore && g.tma_store && full_chunk) {
           // Stage the warp's [32 x 128 B] chunk with the 128-byte swizzle, then one TMA store per
           // destination; rows past M are clipped by the tensor map.
           uint8_t* buf = stage_base + sbuf * 4096;
@@ -385,8 +385,10 @@ __global__ void __launch_bounds__(kThreads, 1) w8a8_gemm_kernel(const __grid_con
       __syncwarp();
       if (lane == 0) mbar_arrive(&tmem_empty[ab]);
     }
-    if (lane == 0) asm volatile("cp.async.bulk.wait_group 0;" ::: "memory");   // every output write has landed
-    __syncwarp();
+    if (kTmaStore) {
+      if (lane == 0) asm volatile("cp.async.bulk.wait_group 0;" ::: "memory");   // every output write has landed
+      __syncwarp();
+    }
   }
   if (g.nout > 1 && warp >= 2) __threadfence_system();   // peer stores visible before the kernel completes
   tc_fence_before();
@@ -494,7 +496,7 @@ bool tma_store_ok(const GemmArgs& g, void* const* dests, int ndest, int64_t map_
   return true;
 }
 
-template <int BN, int STAGES>
+template <int BN, int STAGES, bool kTmaStore>
 int launch_gemm(const int8_t* a, const int8_t* b_nk, GemmArgs& g, void* const* dests, int ndest, int64_t map_cols,
                 cudaStream_t st) {
   CUtensorMap ma, mb;
@@ -507,15 +509,15 @@ int launch_gemm(const int8_t* a, const int8_t* b_nk, GemmArgs& g, void* const* d
   g.tiles = g.m_blocks * g.n_blocks;
   OutMaps om;
   memset(&om, 0, sizeof(om));
-  g.tma_store = tma_store_ok(g, dests, ndest, map_cols) ? 1 : 0;
+  g.tma_store = kTmaStore && tma_store_ok(g, dests, ndest, map_cols) ? 1 : 0;
   g.ndest = g.tma_store ? ndest : 0;
   for (int d = 0; d < g.ndest; ++d) {
     rc = make_out_map(&om.m[d], dests[d], g.out_dtype, g.M, map_cols, g.ldo);
     if (rc) return rc;
   }
-  constexpr size_t kStaging = 4 * 8192;       // 4 epilogue warps x 2 x [32 rows x 128 B]
+  constexpr size_t kStaging = kTmaStore ? 4 * 8192 : 0;   // 4 epilogue warps x 2 x [32 rows x 128 B]
   const size_t smem = (size_t)STAGES * (kBM * kBK + BN * kBK) + kStaging + 1024;
-  auto kern = w8a8_gemm_kernel<BN, STAGES>;
+  auto kern = w8a8_gemm_kernel<BN, STAGES, kTmaStore>;
   static int set_dev = -1;
   int dev = 0;
   cudaGetDevice(&dev);
@@ -572,8 +574,9 @@ extern "C" int kvb_w8a8_scaled_mm_allgather(const int8_t* a, const int8_t* b_sha
   void* dests[8];
   for (int d = 0; d < world; ++d) dests[d] = g.outs[d] = out_ptrs[(rank + d) % world];   // own buffer first, then peers
   cudaStream_t st = as_stream(stream);
-  if (M <= 256) return launch_gemm<208, 4>(a, b_shard, g, dests, world, ldo, st);
-  return launch_gemm<256, 4>(a, b_shard, g, dests, world, ldo, st);
+  // Peer destinations: stage output chunks and write them with TMA tensor stores (large NVLink writes).
+  if (M <= 256) return launch_gemm<208, 4, true>(a, b_shard, g, dests, world, ldo, st);
+  return launch_gemm<256, 4, true>(a, b_shard, g, dests, world, ldo, st);
 }
 
 extern "C" size_t kvb_w8a8_workspace_size(int64_t M, int64_t N, int64_t K, int b_layout, int has_azp) {
@@ -630,6 +633,6 @@ extern "C" int kvb_w8a8_scaled_mm(const int8_t* a, const int8_t* b, int b_layout
   // Small M streams B from HBM: 208-column tiles make N = 28672 exactly 138 tiles (one wave on
   // 148 SMs) and keep ~1.9 waves at two M blocks.  Large M is tensor-bound: 256-column tiles.
   void* dests[1] = {out};
-  if (M <= 256) return launch_gemm<208, 4>(a, b_nk, g, dests, 1, N, st);
-  return launch_gemm<256, 4>(a, b_nk, g, dests, 1, N, st);
+  if (M <= 256) return launch_gemm<208, 5, false>(a, b_nk, g, dests, 1, N, st);
+  return launch_gemm<256, 4, false>(a, b_nk, g, dests, 1, N, st);
 }
