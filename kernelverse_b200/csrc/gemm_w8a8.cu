@@ -365,9 +365,18 @@ __global__ void __launch_bounds__(kThreads, 1) w8a8_gemm_kernel(const __grid_con
           continue;
         }
         if (!mrow) continue;
-        // Ragged edge: direct stores of the valid columns to every destination.
+        // Direct stores of the valid columns to every destination: 16-byte vectors for a full,
+        // aligned chunk, element stores at a ragged edge.
         const int ncols = min(min(CW, BN - c0), g.N - n0);
         for (int d = g.nout ? 0 : -1; d < g.nout; ++d) {
+          uint8_t* ob = esize == 4 ? reinterpret_cast<uint8_t*>(dst_ptr<uint32_t>(g, d, m, n0))
+                                   : reinterpret_cast<uint8_t*>(dst_ptr<uint16_t>(g, d, m, n0));
+          if (ncols == CW && (reinterpret_cast<uintptr_t>(ob) & 15) == 0) {
+#pragma unroll
+            for (int j = 0; j < 8; ++j)
+              reinterpret_cast<uint4*>(ob)[j] = make_uint4(w[4 * j], w[4 * j + 1], w[4 * j + 2], w[4 * j + 3]);
+            continue;
+          }
           if (esize == 4) {
             uint32_t* o = dst_ptr<uint32_t>(g, d, m, n0);
 #pragma unroll
