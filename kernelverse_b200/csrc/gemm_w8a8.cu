@@ -132,6 +132,61 @@ __device__ __forceinline__ void mma_i8(uint32_t tmem_d, uint64_t adesc, uint64_t
       : "memory");
 }
 
+// ---- CTA-pair (cta_group::2) variants
+__device__ __forceinline__ uint32_t cluster_ctarank() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+  return r;
+}
+// shared::cluster address of `addr` (a local shared::cta address) in CTA `rank` of the cluster
+__device__ __forceinline__ uint32_t mapa_shared(uint32_t addr, uint32_t rank) {
+  uint32_t r;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(addr), "r"(rank));
+  return r;
+}
+__device__ __forceinline__ void cluster_sync_all() {
+  asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+// TMA load into this CTA's shared memory whose completion is counted on the pair leader's barrier.
+__device__ __forceinline__ void tma_load_2d_pair(void* dst, const CUtensorMap* map, int x, int y, uint32_t bar_cluster,
+                                                 uint64_t policy) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes.L2::cache_hint "
+      "[%0], [%1, {%2, %3}], [%4], %5;"
+      ::"r"(smem_u32(dst)), "l"(map), "r"(x), "r"(y), "r"(bar_cluster), "l"(policy)
+      : "memory");
+}
+// M = 256 MMA over the CTA pair: A rows 0-127 / 128-255 and B rows [0, N/2) / [N/2, N) come from the
+// leader's / the peer's shared memory at the same offsets; D lands in both CTAs' TMEM.
+__device__ __forceinline__ void mma_i8_pair(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
+                                            uint32_t accum) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::2.kind::i8 [%0], %1, %2, %3, {%5, %6, %7, %8, %9, %10, %11, %12}, p;\n\t}"
+      ::"r"(tmem_d), "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accum), "r"(0), "r"(0), "r"(0), "r"(0), "r"(0), "r"(0),
+        "r"(0), "r"(0)
+      : "memory");
+}
+// Completion of this thread's prior MMAs arrives on the barrier at the same offset in both CTAs.
+__device__ __forceinline__ void mma_commit_pair(uint64_t* bar) {
+  asm volatile("tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.multicast::cluster.b64 [%0], %1;"
+               ::"r"(smem_u32(bar)), "h"((uint16_t)3)
+               : "memory");
+}
+__device__ __forceinline__ void mbar_arrive_cluster(uint32_t bar_cluster) {
+  asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(bar_cluster) : "memory");
+}
+__device__ __forceinline__ void tmem_alloc_pair(uint32_t* dst_smem, uint32_t ncols) {
+  asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(dst_smem)),
+               "r"(ncols)
+               : "memory");
+  asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void tmem_dealloc_pair(uint32_t taddr, uint32_t ncols) {
+  asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols) : "memory");
+}
+
 __device__ __forceinline__ void mma_commit(uint64_t* bar) {
   asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar))
                : "memory");
@@ -206,18 +261,23 @@ __device__ __forceinline__ void epilogue32(const GemmArgs& g, const uint32_t (&r
   }
 }
 
-template <int BN, int STAGES, bool kTmaStore>
+// k2Sm: CTA pairs (cluster of 2) compute 256 x BN tiles with cta_group::2 MMAs; each CTA loads
+// its 128 rows of A and BN/2 rows of B, so a k-block moves 32 KB per SM instead of 48 KB.
+template <int BN, int STAGES, bool kTmaStore, bool k2Sm>
 __global__ void __launch_bounds__(kThreads, 1) w8a8_gemm_kernel(const __grid_constant__ CUtensorMap tmap_a,
                                                                  const __grid_constant__ CUtensorMap tmap_b,
                                                                  const __grid_constant__ GemmArgs g,
                                                                  const __grid_constant__ OutMaps om) {
+  constexpr int kTileM = k2Sm ? 2 * kBM : kBM;
+  constexpr int kBRows = k2Sm ? BN / 2 : BN;
   constexpr uint32_t kABytes = kBM * kBK;
-  constexpr uint32_t kBBytes = BN * kBK;
+  constexpr uint32_t kBBytes = kBRows * kBK;
   constexpr uint32_t kStageBytes = kABytes + kBBytes;
+  static_assert(!k2Sm || BN % 32 == 0, "cta_group::2 kind::i8 needs N % 32 == 0");
   // two accumulator buffers of BN columns; the allocation is a power of two >= 32
   constexpr uint32_t kTmemCols = 2 * BN <= 32 ? 32 : 2 * BN <= 64 ? 64 : 2 * BN <= 128 ? 128 : 2 * BN <= 256 ? 256 : 512;
   static_assert(BN % 16 == 0 && BN >= 16 && BN <= 256, "tcgen05 kind::i8 with M=128 needs N % 16 == 0, N <= 256");
-  constexpr uint32_t kIdesc = idesc_i8(kBM, BN);
+  constexpr uint32_t kIdesc = idesc_i8(kTileM, BN);
 
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -226,6 +286,10 @@ __global__ void __launch_bounds__(kThreads, 1) w8a8_gemm_kernel(const __grid_con
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int KB = (g.K + kBK - 1) / kBK;
+  const uint32_t crank = k2Sm ? cluster_ctarank() : 0u;   // 0 = pair leader (issues the MMAs)
+  const bool leader = crank == 0;
+  const int tile0 = k2Sm ? (int)(blockIdx.x >> 1) : (int)blockIdx.x;
+  const int tstride = k2Sm ? (int)(gridDim.x >> 1) : (int)gridDim.x;
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < STAGES; ++s) {
@@ -234,16 +298,23 @@ __global__ void __launch_bounds__(kThreads, 1) w8a8_gemm_kernel(const __grid_con
     }
     for (int j = 0; j < 2; ++j) {
       mbar_init(&tmem_full[j], 1);
-      mbar_init(&tmem_empty[j], 4);
+      mbar_init(&tmem_empty[j], k2Sm ? 8 : 4);   // every epilogue warp of the pair releases the buffer
     }
     mbar_init(&mma_done, 1);
     fence_mbar_init();
     asm volatile("prefetch.tensormap [%0];" ::"l"(&tmap_a) : "memory");
     asm volatile("prefetch.tensormap [%0];" ::"l"(&tmap_b) : "memory");
   }
-  if (warp == 1) tmem_alloc(&tmem_base_s, kTmemCols);
+  if (warp == 1) {
+    if constexpr (k2Sm) tmem_alloc_pair(&tmem_base_s, kTmemCols);
+    else tmem_alloc(&tmem_base_s, kTmemCols);
+  }
   tc_fence_before();
   __syncthreads();
+  if constexpr (k2Sm) {
+    __syncwarp();
+    cluster_sync_all();    // the peer's barriers are initialised before any remote signal
+  }
   tc_fence_after();
   const uint32_t tmem_base = tmem_base_s;
 
@@ -255,9 +326,10 @@ __global__ void __launch_bounds__(kThreads, 1) w8a8_gemm_kernel(const __grid_con
       // A tiles are re-read by every N block: keep them in L2; B is streamed once when M is small.
       const uint64_t pol_a = policy_evict_last();
       const uint64_t pol_b = g.m_blocks <= 2 ? policy_evict_first() : policy_evict_normal();
-      for (int t = blockIdx.x; t < g.tiles && ok; t += gridDim.x) {
+      for (int t = tile0; t < g.tiles && ok; t += tstride) {
         int mb, nb;
         tile_coords(g, t, mb, nb);
+        const int ya = mb * kTileM + (int)crank * kBM, yb = nb * BN + (int)crank * kBRows;
         for (int kb = 0; kb < KB; ++kb, ++it) {
           const int s = it % STAGES;
           const uint32_t use = it / STAGES;
@@ -266,9 +338,17 @@ __global__ void __launch_bounds__(kThreads, 1) w8a8_gemm_kernel(const __grid_con
             break;
           }
           uint8_t* sa_ = smem + s * kStageBytes;
-          mbar_arrive_expect_tx(&full[s], kStageBytes);
-          tma_load_2d(sa_, &tmap_a, kb * kBK, mb * kBM, &full[s], pol_a);
-          tma_load_2d(sa_ + kABytes, &tmap_b, kb * kBK, nb * BN, &full[s], pol_b);
+          if constexpr (k2Sm) {
+            // both CTAs' bytes complete on the leader's full barrier, which expects them all
+            const uint32_t bar = mapa_shared(smem_u32(&full[s]), 0);
+            if (leader) mbar_arrive_expect_tx(&full[s], 2 * kStageBytes);
+            tma_load_2d_pair(sa_, &tmap_a, kb * kBK, ya, bar, pol_a);
+            tma_load_2d_pair(sa_ + kABytes, &tmap_b, kb * kBK, yb, bar, pol_b);
+          } else {
+            mbar_arrive_expect_tx(&full[s], kStageBytes);
+            tma_load_2d(sa_, &tmap_a, kb * kBK, ya, &full[s], pol_a);
+            tma_load_2d(sa_ + kABytes, &tmap_b, kb * kBK, yb, &full[s], pol_b);
+          }
         }
       }
       // drain: every stage issued must have been consumed before this CTA exits
@@ -277,10 +357,10 @@ __global__ void __launch_bounds__(kThreads, 1) w8a8_gemm_kernel(const __grid_con
     }
   } else if (warp == 1) {
     // ------------------------------------------------------------ MMA issuer
-    if (lane == 0) {
+    if (lane == 0 && leader) {
       uint32_t it = 0, local = 0;
       bool ok = true;
-      for (int t = blockIdx.x; t < g.tiles && ok; t += gridDim.x, ++local) {
+      for (int t = tile0; t < g.tiles && ok; t += tstride, ++local) {
         const uint32_t ab = local & 1u, v = local >> 1;
         if (v > 0 && !mbar_wait_bounded(&tmem_empty[ab], (v - 1) & 1u)) {
           ok = false;
@@ -298,17 +378,26 @@ __global__ void __launch_bounds__(kThreads, 1) w8a8_gemm_kernel(const __grid_con
           const uint8_t* a_s = smem + s * kStageBytes;
           const uint8_t* b_s = a_s + kABytes;
 #pragma unroll
-          for (int kk = 0; kk < kBK / kUmmaK; ++kk)
-            mma_i8(d_tmem, smem_desc_k128(a_s + kk * kUmmaK), smem_desc_k128(b_s + kk * kUmmaK), kIdesc,
-                   (kb | kk) != 0);
-          mma_commit(&empty[s]);      // stage s is free once these MMAs have read it
+          for (int kk = 0; kk < kBK / kUmmaK; ++kk) {
+            const uint64_t ad = smem_desc_k128(a_s + kk * kUmmaK), bd = smem_desc_k128(b_s + kk * kUmmaK);
+            if constexpr (k2Sm) mma_i8_pair(d_tmem, ad, bd, kIdesc, (kb | kk) != 0);
+            else mma_i8(d_tmem, ad, bd, kIdesc, (kb | kk) != 0);
+          }
+          // stage s is free (in both CTAs) once these MMAs have read it
+          if constexpr (k2Sm) mma_commit_pair(&empty[s]);
+          else mma_commit(&empty[s]);
         }
         if (!ok) break;
-        mma_commit(&tmem_full[ab]);   // accumulator ab is final once every MMA above completes
+        // accumulator ab is final once every MMA above completes
+        if constexpr (k2Sm) mma_commit_pair(&tmem_full[ab]);
+        else mma_commit(&tmem_full[ab]);
       }
       // every MMA this thread issued has completed before TMEM may be freed
-      mma_commit(&mma_done);
+      if constexpr (k2Sm) mma_commit_pair(&mma_done);
+      else mma_commit(&mma_done);
       mbar_wait_bounded(&mma_done, 0);
+    } else if (k2Sm && lane == 0) {
+      mbar_wait_bounded(&mma_done, 0);   // the leader's MMAs also write this CTA's TMEM
     }
   } else {
     // ------------------------------------------------------------ epilogue (warps 2..5)
@@ -319,13 +408,14 @@ __global__ void __launch_bounds__(kThreads, 1) w8a8_gemm_kernel(const __grid_con
     uint8_t* stage_base = smem + (size_t)STAGES * kStageBytes + (size_t)q * 8192;
     int sbuf = 0;
     uint32_t local = 0;
-    for (int t = blockIdx.x; t < g.tiles; t += gridDim.x, ++local) {
+    for (int t = tile0; t < g.tiles; t += tstride, ++local) {
       const uint32_t ab = local & 1u, v = local >> 1;
       if (!mbar_wait_bounded(&tmem_full[ab], v & 1u)) break;
       tc_fence_after();
       int mb, nb;
       tile_coords(g, t, mb, nb);
-      const int m = mb * kBM + q * 32 + lane;
+      const int row0 = mb * kTileM + (int)crank * kBM + q * 32;   // first output row of this warp
+      const int m = row0 + lane;
       const bool mrow = m < g.M;
       const float sa = (mrow && g.sa) ? g.sa[m] : 0.0f;   // no scales in int32-accumulator mode
       const int32_t rs = (g.azp && mrow) ? g.rowsum[m] : 0;
@@ -358,7 +448,7 @@ __global__ void __launch_bounds__(kThreads, 1) w8a8_gemm_kernel(const __grid_con
           __syncwarp();
           if (lane == 0) {
             for (int d = 0; d < g.ndest; ++d)
-              tma_store_2d(&om.m[d], buf, (int)(g.col_off + n0), mb * kBM + q * 32);
+              tma_store_2d(&om.m[d], buf, (int)(g.col_off + n0), row0);
             asm volatile("cp.async.bulk.commit_group;" ::: "memory");
           }
           sbuf ^= 1;
@@ -392,7 +482,10 @@ __global__ void __launch_bounds__(kThreads, 1) w8a8_gemm_kernel(const __grid_con
       }
       tc_fence_before();
       __syncwarp();
-      if (lane == 0) mbar_arrive(&tmem_empty[ab]);
+      if (lane == 0) {
+        if constexpr (k2Sm) mbar_arrive_cluster(mapa_shared(smem_u32(&tmem_empty[ab]), 0));   // the leader's barrier
+        else mbar_arrive(&tmem_empty[ab]);
+      }
     }
     if (kTmaStore) {
       if (lane == 0) asm volatile("cp.async.bulk.wait_group 0;" ::: "memory");   // every output write has landed
@@ -402,10 +495,15 @@ __global__ void __launch_bounds__(kThreads, 1) w8a8_gemm_kernel(const __grid_con
   if (g.nout > 1 && warp >= 2) __threadfence_system();   // peer stores visible before the kernel completes
   tc_fence_before();
   __syncthreads();
+  if constexpr (k2Sm) {
+    __syncwarp();
+    cluster_sync_all();    // neither CTA leaves while its peer may still signal it
+  }
   if (warp == 1) {
     __syncwarp();
     tc_fence_after();
-    tmem_dealloc(tmem_base, kTmemCols);
+    if constexpr (k2Sm) tmem_dealloc_pair(tmem_base, kTmemCols);
+    else tmem_dealloc(tmem_base, kTmemCols);
   }
 }
 
@@ -505,15 +603,17 @@ bool tma_store_ok(const GemmArgs& g, void* const* dests, int ndest, int64_t map_
   return true;
 }
 
-template <int BN, int STAGES, bool kTmaStore>
+template <int BN, int STAGES, bool kTmaStore, bool k2Sm>
 int launch_gemm(const int8_t* a, const int8_t* b_nk, GemmArgs& g, void* const* dests, int ndest, int64_t map_cols,
                 cudaStream_t st) {
+  constexpr int kTileM = k2Sm ? 2 * kBM : kBM;
+  constexpr int kBRows = k2Sm ? BN / 2 : BN;
   CUtensorMap ma, mb;
   int rc = make_map(&ma, a, g.M, g.K, kBM);
   if (rc) return rc;
-  rc = make_map(&mb, b_nk, g.N, g.K, BN);
+  rc = make_map(&mb, b_nk, g.N, g.K, kBRows);
   if (rc) return rc;
-  g.m_blocks = (g.M + kBM - 1) / kBM;
+  g.m_blocks = (g.M + kTileM - 1) / kTileM;
   g.n_blocks = (g.N + BN - 1) / BN;
   g.tiles = g.m_blocks * g.n_blocks;
   OutMaps om;
@@ -525,8 +625,8 @@ int launch_gemm(const int8_t* a, const int8_t* b_nk, GemmArgs& g, void* const* d
     if (rc) return rc;
   }
   constexpr size_t kStaging = kTmaStore ? 4 * 8192 : 0;   // 4 epilogue warps x 2 x [32 rows x 128 B]
-  const size_t smem = (size_t)STAGES * (kBM * kBK + BN * kBK) + kStaging + 1024;
-  auto kern = w8a8_gemm_kernel<BN, STAGES, kTmaStore>;
+  const size_t smem = (size_t)STAGES * (kBM * kBK + kBRows * kBK) + kStaging + 1024;
+  auto kern = w8a8_gemm_kernel<BN, STAGES, kTmaStore, k2Sm>;
   static int set_dev = -1;
   int dev = 0;
   cudaGetDevice(&dev);
@@ -535,9 +635,28 @@ int launch_gemm(const int8_t* a, const int8_t* b_nk, GemmArgs& g, void* const* d
     if (e != cudaSuccess) return set_error(KVB_E_LAUNCH, "w8a8_scaled_mm: smem attribute: %s", cudaGetErrorString(e));
     set_dev = dev;
   }
-  const int grid = std::min(g.tiles, num_sms());
-  kern<<<grid, kThreads, smem, st>>>(ma, mb, g, om);
-  return check_launch("w8a8_gemm_kernel");
+  if constexpr (k2Sm) {
+    // CTA pairs: a cluster of 2 along x, one pair per two SMs
+    cudaLaunchConfig_t cfg = {};
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = 2;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    cfg.gridDim = dim3(2u * (unsigned)std::min(g.tiles, num_sms() / 2));
+    cfg.blockDim = dim3(kThreads);
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = st;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    cudaError_t e = cudaLaunchKernelEx(&cfg, kern, ma, mb, g, om);
+    if (e != cudaSuccess) return set_error(KVB_E_LAUNCH, "w8a8_gemm_kernel (pairs): %s", cudaGetErrorString(e));
+    return check_launch("w8a8_gemm_kernel");
+  } else {
+    const int grid = std::min(g.tiles, num_sms());
+    kern<<<grid, kThreads, smem, st>>>(ma, mb, g, om);
+    return check_launch("w8a8_gemm_kernel");
+  }
 }
 
 bool is_sm100() {
@@ -584,8 +703,8 @@ extern "C" int kvb_w8a8_scaled_mm_allgather(const int8_t* a, const int8_t* b_sha
   for (int d = 0; d < world; ++d) dests[d] = g.outs[d] = out_ptrs[(rank + d) % world];   // own buffer first, then peers
   cudaStream_t st = as_stream(stream);
   // Peer destinations: stage output chunks and write them with TMA tensor stores (large NVLink writes).
-  if (M <= 256) return launch_gemm<208, 4, true>(a, b_shard, g, dests, world, ldo, st);
-  return launch_gemm<256, 4, true>(a, b_shard, g, dests, world, ldo, st);
+  if (M <= 256) return launch_gemm<208, 4, true, false>(a, b_shard, g, dests, world, ldo, st);
+  return launch_gemm<256, 6, true, true>(a, b_shard, g, dests, world, ldo, st);
 }
 
 extern "C" size_t kvb_w8a8_workspace_size(int64_t M, int64_t N, int64_t K, int b_layout, int has_azp) {
@@ -642,6 +761,6 @@ extern "C" int kvb_w8a8_scaled_mm(const int8_t* a, const int8_t* b, int b_layout
   // Small M streams B from HBM: 208-column tiles make N = 28672 exactly 138 tiles (one wave on
   // 148 SMs) and keep ~1.9 waves at two M blocks.  Large M is tensor-bound: 256-column tiles.
   void* dests[1] = {out};
-  if (M <= 256) return launch_gemm<208, 5, false>(a, b_nk, g, dests, 1, N, st);
-  return launch_gemm<256, 4, false>(a, b_nk, g, dests, 1, N, st);
+  if (M <= 256) return launch_gemm<208, 5, false, false>(a, b_nk, g, dests, 1, N, st);
+  return launch_gemm<256, 6, false, true>(a, b_nk, g, dests, 1, N, st);
 }
