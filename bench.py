@@ -250,19 +250,45 @@ def make_c3_inputs(torch, dev, seed: int, M: int, N: int = 28672, K: int = 8192)
     return a, b, sa, sb, bias
 
 
+def _backlog(torch, calls: int) -> None:
+    """Queue a device spin long enough for the host to enqueue ``calls`` more calls behind it, so
+    events time the device work and not the Python/ctypes cost of issuing each call."""
+    torch.cuda._sleep(int(2e9 * (1e-3 + calls * 50e-6)))
+
+
 def time_fn(torch, fn, iters: int, warm: int = 3) -> float:
-    """Mean microseconds per call of back-to-back launches (CUDA events on the current stream)."""
+    """Mean microseconds per call of back-to-back launches (CUDA events on the current stream,
+    issued behind a device spin so host overhead is not in the figure)."""
     stream = torch.cuda.current_stream()
     for _ in range(warm):
         fn()
     torch.cuda.synchronize()
     s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    _backlog(torch, iters)
     s.record(stream)
     for _ in range(iters):
         fn()
     e.record(stream)
     torch.cuda.synchronize()
     return s.elapsed_time(e) / iters * 1e3
+
+
+def time_cold(torch, fn, iters: int, flush) -> float:
+    """Median microseconds of one call after L2 has been flushed by writing ``flush``
+    (larger than L2), each call bracketed by its own events, all issued behind a device spin."""
+    stream = torch.cuda.current_stream()
+    for _ in range(3):
+        fn()
+    torch.cuda.synchronize()
+    ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(iters)]
+    _backlog(torch, 2 * iters)
+    for s, e in ev:
+        flush.zero_()
+        s.record(stream)
+        fn()
+        e.record(stream)
+    torch.cuda.synchronize()
+    return statistics.median(s.elapsed_time(e) for s, e in ev) * 1e3
 
 
 def gemm_benchmarks(torch, ops, hbm_peak):
@@ -395,30 +421,20 @@ def secondary_benchmarks(torch, ops, hbm_peak):
     x = torch.where(mask, x * 50.0, x).to(torch.bfloat16)
     nbytes = 2048 * 4096 * 2 + 2048 * 4096 + 2048 * 4
     flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
-    stream = torch.cuda.current_stream()
-    for _ in range(5):
-        ops.per_token_group_quant_int8(x, 4096, 1e-6)
-    times = []
-    for _ in range(20):
-        flush.zero_()
-        s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        s.record(stream)
-        ops.per_token_group_quant_int8(x, 4096, 1e-6)
-        e.record(stream)
-        torch.cuda.synchronize()
-        times.append(s.elapsed_time(e))
-    us = statistics.median(times) * 1e3
-    # back-to-back (amortised launch) number
+    quant = lambda: ops.per_token_group_quant_int8(x, 4096, 1e-6)  # noqa: E731
+    us = time_cold(torch, quant, 30, flush)
+    # back-to-back: the 16.8 MB input stays in L2 between calls
+    us_b2b = time_fn(torch, quant, 200)
+    # host cost of one call through the Python API (what a caller that does not batch sees)
     torch.cuda.synchronize()
-    s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    s.record(stream)
+    t0 = time.perf_counter()
     for _ in range(200):
-        ops.per_token_group_quant_int8(x, 4096, 1e-6)
-    e.record(stream)
+        quant()
     torch.cuda.synchronize()
-    us_b2b = s.elapsed_time(e) / 200 * 1e3
+    us_host = (time.perf_counter() - t0) / 200 * 1e6
     out.append({"workload": "per-token int8 quant bf16 [2048,4096] (BASELINE config 1)", "kernel": "group_quant_rowblock_kernel",
                 "us_per_call_cold_l2": round(us, 3), "us_per_call_back_to_back": round(us_b2b, 3),
+                "us_per_call_host_issue": round(us_host, 3), "timing": "device events behind a device spin",
                 "bytes_per_call": nbytes, "achieved_gbs_cold_l2": round(nbytes / us / 1e3, 1),
                 "frac_cold_l2": round(nbytes / us / 1e3 / hbm_peak, 4)})
     del flush
@@ -426,17 +442,7 @@ def secondary_benchmarks(torch, ops, hbm_peak):
     c = make_c4_inputs(torch, dev, 11)
     step = lambda: ops.paged_fp8_decode(c["q"], c["kc"], c["vc"], c["ks"], c["vs"], c["lens"], c["bt"],  # noqa: E731
                                         k_new=c["k_new"], v_new=c["v_new"], max_seq_len=c["max_len"])
-    for _ in range(5):
-        step()
-    torch.cuda.synchronize()
-    n = 50
-    s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    s.record(stream)
-    for _ in range(n):
-        step()
-    e.record(stream)
-    torch.cuda.synchronize()
-    us = s.elapsed_time(e) / n * 1e3
+    us = time_fn(torch, step, 50, warm=5)
     nbytes = c4_bytes(c)
     flops = 4 * 128 * 32 * c["sum_ctx"]
     out.append({"workload": "paged FP8 KV write + GQA decode, B=64, 32/8 heads, D=128, bs=16, ctx~U[512,8192] "

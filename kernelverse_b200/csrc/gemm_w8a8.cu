@@ -224,24 +224,43 @@ __device__ __forceinline__ float load_bias(const void* p, int dt, int n) {
   return reinterpret_cast<const float*>(p)[n];
 }
 
-// Scale / bias / convert 32 accumulator columns starting at global column n0 into output
-// words: 32 words for 32-bit outputs, 16 packed pairs for 16-bit outputs.
-__device__ __forceinline__ void epilogue32(const GemmArgs& g, const uint32_t (&r)[32], int n0, float sa, int32_t rs,
-                                           uint32_t* w) {
+// Per-column epilogue operands of 32 columns: lane j holds column n0 + j (clamped to the last
+// column).  One coalesced load per operand per 32 columns; the values reach the other lanes by
+// shuffles.  (Per-element loads of the same address by all 32 lanes serialised behind the L2
+// latency and made the epilogue as long as the main loop.)
+struct ColVals {
+  float sb, bias, azp, adj;
+};
+
+__device__ __forceinline__ ColVals load_cols(const GemmArgs& g, int n0, int lane) {
+  ColVals c{0.0f, 0.0f, 0.0f, 0.0f};
+  if (g.out_dtype == KVB_I32) return c;   // int32-accumulator mode has no column operands
+  const int n = min(n0 + lane, g.N - 1);
+  c.sb = g.sb[n];
+  if (g.bias) c.bias = load_bias(g.bias, g.bias_dtype, n);
+  if (g.azp) c.azp = g.azp[n];
+  if (g.azp_adj) c.adj = g.azp_adj[n];
+  return c;
+}
+
+// Scale / bias / convert 32 accumulator columns (operands in c) into output words: 32 words for
+// 32-bit outputs, 16 packed pairs for 16-bit outputs.  All 32 lanes must be converged.
+__device__ __forceinline__ void epilogue32(const GemmArgs& g, const uint32_t (&r)[32], const ColVals& c, float sa,
+                                           int32_t rs, uint32_t* w) {
   if (g.out_dtype == KVB_I32) {
 #pragma unroll
     for (int j = 0; j < 32; ++j) w[j] = r[j];
     return;
   }
+  constexpr unsigned kAll = 0xffffffffu;
   float f[32];
 #pragma unroll
   for (int j = 0; j < 32; ++j) {
-    const int n = n0 + j < g.N ? n0 + j : g.N - 1;
     int32_t acc = (int32_t)r[j];
-    if (g.azp) acc -= (int32_t)g.azp[n] * rs;
-    float y = __fmul_rn(__fmul_rn((float)acc, sa), g.sb[n]);
-    if (g.azp_adj) y = __fadd_rn(y, g.azp_adj[n]);
-    if (g.bias) y = __fadd_rn(y, load_bias(g.bias, g.bias_dtype, n));
+    if (g.azp) acc -= (int32_t)__shfl_sync(kAll, c.azp, j) * rs;
+    float y = __fmul_rn(__fmul_rn((float)acc, sa), __shfl_sync(kAll, c.sb, j));
+    if (g.azp_adj) y = __fadd_rn(y, __shfl_sync(kAll, c.adj, j));
+    if (g.bias) y = __fadd_rn(y, __shfl_sync(kAll, c.bias, j));
     f[j] = y;
   }
   if (g.out_dtype == KVB_F32) {
@@ -374,7 +393,6 @@ __global__ void __launch_bounds__(kThreads, 1) w8a8_gemm_kernel(const __grid_con
             ok = false;
             break;
           }
-          tc_fence_after();
           const uint8_t* a_s = smem + s * kStageBytes;
           const uint8_t* b_s = a_s + kABytes;
 #pragma unroll
@@ -410,8 +428,7 @@ __global__ void __launch_bounds__(kThreads, 1) w8a8_gemm_kernel(const __grid_con
     uint32_t local = 0;
     for (int t = tile0; t < g.tiles; t += tstride, ++local) {
       const uint32_t ab = local & 1u, v = local >> 1;
-      if (!mbar_wait_bounded(&tmem_full[ab], v & 1u)) break;
-      tc_fence_after();
+      // The row and first-chunk column operands are loaded before the accumulator is ready.
       int mb, nb;
       tile_coords(g, t, mb, nb);
       const int row0 = mb * kTileM + (int)crank * kBM + q * 32;   // first output row of this warp
@@ -419,18 +436,27 @@ __global__ void __launch_bounds__(kThreads, 1) w8a8_gemm_kernel(const __grid_con
       const bool mrow = m < g.M;
       const float sa = (mrow && g.sa) ? g.sa[m] : 0.0f;   // no scales in int32-accumulator mode
       const int32_t rs = (g.azp && mrow) ? g.rowsum[m] : 0;
+      ColVals cv0 = load_cols(g, nb * BN, lane);
+      ColVals cv1 = esize == 2 && 32 < BN ? load_cols(g, nb * BN + 32, lane) : ColVals{0.0f, 0.0f, 0.0f, 0.0f};
+      if (!mbar_wait_bounded(&tmem_full[ab], v & 1u)) break;
+      tc_fence_after();
 #pragma unroll 1
       for (int c0 = 0; c0 < BN; c0 += CW) {
         const int n0 = nb * BN + c0;
+        const ColVals cur0 = cv0, cur1 = cv1;
+        if (c0 + CW < BN) {                 // prefetch the next chunk's column operands
+          cv0 = load_cols(g, n0 + CW, lane);
+          if (esize == 2 && c0 + CW + 32 < BN) cv1 = load_cols(g, n0 + CW + 32, lane);
+        }
         uint32_t w[32];
         uint32_t r[32];
         __syncwarp();                       // tcgen05.ld is .sync.aligned: reconverge first
         tmem_ld32(tmem_base + ((uint32_t)(q * 32) << 16) + ab * BN + c0, r);
-        epilogue32(g, r, n0, sa, rs, w);
+        epilogue32(g, r, cur0, sa, rs, w);
         if (esize == 2 && c0 + 32 < BN) {
           __syncwarp();
           tmem_ld32(tmem_base + ((uint32_t)(q * 32) << 16) + ab * BN + c0 + 32, r);
-          epilogue32(g, r, n0 + 32, sa, rs, w + 16);
+          epilogue32(g, r, cur1, sa, rs, w + 16);
         }
         if (n0 >= g.N) continue;
         const bool full_chunk = c0 + CW <= BN && n0 + CW <= g.N;
@@ -758,9 +784,9 @@ extern "C" int kvb_w8a8_scaled_mm(const int8_t* a, const int8_t* b, int b_layout
     if (rc) return rc;
     g.rowsum = rs;
   }
-  // Small M streams B from HBM: 208-column tiles make N = 28672 exactly 138 tiles (one wave on
-  // 148 SMs) and keep ~1.9 waves at two M blocks.  Large M is tensor-bound: 256-column tiles.
+  // M <= 128 streams B from HBM: 208-column tiles make N = 28672 exactly 138 tiles (one wave on
+  // 148 SMs).  Larger M: CTA pairs with 256 x 256 tiles (half the B bytes per SM per k-block).
   void* dests[1] = {out};
-  if (M <= 256) return launch_gemm<208, 5, false, false>(a, b_nk, g, dests, 1, N, st);
+  if (M <= 128) return launch_gemm<208, 5, false, false>(a, b_nk, g, dests, 1, N, st);
   return launch_gemm<256, 6, false, true>(a, b_nk, g, dests, 1, N, st);
 }
