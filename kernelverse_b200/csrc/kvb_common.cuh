@@ -219,6 +219,28 @@ __device__ __forceinline__ int8_t quant_int8(float x, const Divisor& d) {
   return static_cast<int8_t>(__float2int_rn(q));
 }
 
+// True when the divisor lies in the Markstein domain (2^-120 <= b <= 2^120).  If in addition b
+// is a group's amax / qmax (qmax = 127 or 448, possibly rounded to a 16-bit type) or larger,
+// the unchecked quantisers below are exact for every value of the group: values with
+// |x| >= d.thresh get the correctly rounded quotient, and smaller ones have |x / b| < 2^-100,
+// whose int8 or e4m3 code is (signed) zero however the last bit of the quotient falls.
+__device__ __forceinline__ bool fast_divisor(const Divisor& d) { return d.thresh < __int_as_float(0x7f800000); }
+
+// int8 codes of four values under fast_divisor(d), |x| <= 127 * b * (1 + 2^-8):
+//  * |quotient| <= 127.25, so round-half-even then clamp to +-127 is round-half-even alone;
+//  * rounding is the addition of 1.5 * 2^23 (one round-to-nearest-even add puts the integer
+//    in the low mantissa bits; its low byte is the two's-complement code), which replaces a
+//    quarter-rate float-to-int conversion, and byte permutes pack four codes into a word
+//    (a0 in the low byte).
+__device__ __forceinline__ uint32_t quant4_fast(float a0, float a1, float a2, float a3, const Divisor& d) {
+  constexpr float kRound = 12582912.0f;   // 1.5 * 2^23
+  const uint32_t b0 = __float_as_uint(__fadd_rn(div_rn_fast(a0, d), kRound));
+  const uint32_t b1 = __float_as_uint(__fadd_rn(div_rn_fast(a1, d), kRound));
+  const uint32_t b2 = __float_as_uint(__fadd_rn(div_rn_fast(a2, d), kRound));
+  const uint32_t b3 = __float_as_uint(__fadd_rn(div_rn_fast(a3, d), kRound));
+  return __byte_perm(__byte_perm(b0, b1, 0x0040), __byte_perm(b2, b3, 0x0040), 0x5410);
+}
+
 // e4m3fn codes of clamp(x / scale, +-448) for two values (a in the low byte).  The
 // hardware conversion (cvt.rn.satfinite.e4m3x2.f32) rounds to nearest even and
 // saturates to +-448, which is exactly clamp-then-cast.

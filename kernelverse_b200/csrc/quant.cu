@@ -12,23 +12,25 @@
 namespace kvb {
 namespace {
 
-// Packs eight int8 codes of one Vec8 into a 64-bit word (little-endian order).
-template <bool kChecked, typename T>
-__device__ __forceinline__ uint2 quant8(const Vec8<T>& v, const Divisor& d) {
+// Packs eight int8 codes of one Vec8 into a 64-bit word (little-endian order); the general
+// path for any divisor (IEEE division below the Markstein threshold, clamp to +-127).
+template <typename T>
+__device__ __forceinline__ uint2 quant8_checked(const Vec8<T>& v, const Divisor& d) {
   float f[8];
   v.unpack(f);
   uint32_t lo = 0, hi = 0;
 #pragma unroll
-  for (int i = 0; i < 4; ++i) lo |= (uint32_t)(uint8_t)quant_int8<kChecked>(f[i], d) << (8 * i);
+  for (int i = 0; i < 4; ++i) lo |= (uint32_t)(uint8_t)quant_int8<true>(f[i], d) << (8 * i);
 #pragma unroll
-  for (int i = 0; i < 4; ++i) hi |= (uint32_t)(uint8_t)quant_int8<kChecked>(f[4 + i], d) << (8 * i);
+  for (int i = 0; i < 4; ++i) hi |= (uint32_t)(uint8_t)quant_int8<true>(f[4 + i], d) << (8 * i);
   return make_uint2(lo, hi);
 }
-// Quantises one vector, skipping the per-element division guard when the vector's
-// smallest magnitude already satisfies it (the common case).
+
 template <typename T>
-__device__ __forceinline__ uint2 quant8(const Vec8<T>& v, const Divisor& d, float vmin) {
-  return vmin >= d.thresh ? quant8<false>(v, d) : quant8<true>(v, d);
+__device__ __forceinline__ uint2 quant8_fast(const Vec8<T>& v, const Divisor& d) {
+  float f[8];
+  v.unpack(f);
+  return make_uint2(quant4_fast(f[0], f[1], f[2], f[3], d), quant4_fast(f[4], f[5], f[6], f[7], d));
 }
 
 template <typename T>
@@ -39,15 +41,6 @@ __device__ __forceinline__ float vec_amax(const Vec8<T>& v) {
   for (int i = 0; i < 8; ++i) m = fmaxf(m, fabsf(f[i]));
   return m;
 }
-template <typename T>
-__device__ __forceinline__ float vec_amin(const Vec8<T>& v) {
-  float f[8], m = __int_as_float(0x7f800000);
-  v.unpack(f);
-#pragma unroll
-  for (int i = 0; i < 8; ++i) m = fminf(m, fabsf(f[i]));
-  return m;
-}
-
 // ---------------------------------------------------------------- per-tensor
 // Pass 1: amax(|x|) -> *amax_bits (float bits; non-negative floats order like uint32).
 template <typename T>
@@ -87,7 +80,7 @@ __global__ void __launch_bounds__(256) tensor_quant_kernel(const T* __restrict__
   for (int64_t v = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; v < nvec; v += stride) {
     Vec8<T> a;
     a.load(x + v * 8);
-    reinterpret_cast<uint2*>(q)[v] = quant8(a, d, vec_amin(a));
+    reinterpret_cast<uint2*>(q)[v] = fast_divisor(d) ? quant8_fast(a, d) : quant8_checked(a, d);
   }
   for (int64_t i = nvec * 8 + (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < numel; i += stride)
     q[i] = quant_int8(Elem<T>::to_f(x[i]), d);
@@ -114,7 +107,8 @@ __global__ void __launch_bounds__(256) group_quant_subwarp_kernel(const T* __res
     m = group_max(m, lanes);
     const float scale = fmaxf(__fdiv_rn(m, kInt8Max), eps);
     if (live) {
-      reinterpret_cast<uint2*>(q)[v] = quant8(a, make_divisor(scale), vec_amin(a));
+      const Divisor d = make_divisor(scale);
+      reinterpret_cast<uint2*>(q)[v] = fast_divisor(d) ? quant8_fast(a, d) : quant8_checked(a, d);
       if ((v & (lanes - 1)) == 0) scales[v / lanes] = scale;
     }
   }
@@ -122,39 +116,41 @@ __global__ void __launch_bounds__(256) group_quant_subwarp_kernel(const T* __res
 
 // ---------------------------------------------------------------- per-group, large groups
 // One CTA per group (e.g. one token row); the group stays in registers between the
-// amax reduction and the quantisation, so x is read from HBM exactly once.
-template <typename T, int VPT>
-__global__ void __launch_bounds__(1024) group_quant_rowblock_kernel(const T* __restrict__ x, int64_t group_vecs, float eps,
-                                            int8_t* __restrict__ q, float* __restrict__ scales) {
+// amax reduction and the quantisation, so x is read from HBM exactly once.  kMinBlocks
+// bounds the registers so that a whole BASELINE-sized batch (2048 rows of 128 threads)
+// is resident in one wave.
+template <typename T, int VPT, int kMaxThreads, int kMinBlocks>
+__global__ void __launch_bounds__(kMaxThreads, kMinBlocks)
+    group_quant_rowblock_kernel(const T* __restrict__ x, int group_vecs, float eps, int8_t* __restrict__ q,
+                                float* __restrict__ scales) {
   __shared__ float scratch[32];
   const int64_t g = blockIdx.x;
   const T* xg = x + g * group_vecs * 8;
   Vec8<T> a[VPT];
-  float m = 0.0f, mn = __int_as_float(0x7f800000);
+  float m = 0.0f;
 #pragma unroll
   for (int j = 0; j < VPT; ++j) {
-    const int64_t v = threadIdx.x + (int64_t)j * blockDim.x;
-    if (v < group_vecs) {
-      a[j].load_stream(xg + v * 8);
-      m = fmaxf(m, vec_amax(a[j]));
-      mn = fminf(mn, vec_amin(a[j]));
-    }
+    const int v = threadIdx.x + j * blockDim.x;
+    if (v < group_vecs) a[j].load_stream(xg + (int64_t)v * 8);
   }
-  m = block_reduce<true>(m, scratch);
+#pragma unroll
+  for (int j = 0; j < VPT; ++j)
+    if (threadIdx.x + j * blockDim.x < group_vecs) m = fmaxf(m, vec_amax(a[j]));
+  m = block_reduce_1bar<true>(m, scratch);   // the block's only reduction
   const float scale = fmaxf(__fdiv_rn(m, kInt8Max), eps);
   const Divisor d = make_divisor(scale);
   uint2* qg = reinterpret_cast<uint2*>(q + g * group_vecs * 8);
-  if (mn >= d.thresh) {
+  if (fast_divisor(d)) {
 #pragma unroll
     for (int j = 0; j < VPT; ++j) {
-      const int64_t v = threadIdx.x + (int64_t)j * blockDim.x;
-      if (v < group_vecs) qg[v] = quant8<false>(a[j], d);
+      const int v = threadIdx.x + j * blockDim.x;
+      if (v < group_vecs) qg[v] = quant8_fast(a[j], d);
     }
   } else {
 #pragma unroll
     for (int j = 0; j < VPT; ++j) {
-      const int64_t v = threadIdx.x + (int64_t)j * blockDim.x;
-      if (v < group_vecs) qg[v] = quant8<true>(a[j], d);
+      const int v = threadIdx.x + j * blockDim.x;
+      if (v < group_vecs) qg[v] = quant8_checked(a[j], d);
     }
   }
   if (threadIdx.x == 0) scales[g] = scale;
@@ -214,7 +210,10 @@ int launch_rowblock(const T* x, int64_t ngroups, int64_t gvec, float eps, int8_t
   int threads = (int)((gvec + VPT - 1) / VPT);
   threads = ((threads + 31) / 32) * 32;
   if (threads > 1024) return set_error(KVB_E_SHAPE, "group too large for the register-resident path");
-  group_quant_rowblock_kernel<T, VPT><<<(unsigned)ngroups, threads, 0, st>>>(x, gvec, eps, q, scales);
+  if (threads <= 128)
+    group_quant_rowblock_kernel<T, VPT, 128, 16><<<(unsigned)ngroups, threads, 0, st>>>(x, (int)gvec, eps, q, scales);
+  else
+    group_quant_rowblock_kernel<T, VPT, 1024, 1><<<(unsigned)ngroups, threads, 0, st>>>(x, (int)gvec, eps, q, scales);
   return check_launch("group_quant_rowblock_kernel");
 }
 

@@ -194,12 +194,15 @@ __device__ __forceinline__ void store_codes(const float (&s)[VPT][8], const Divi
       if (MODE == kQuantE4m3) {
         lo = quant_e4m3x2<kChecked>(s[j][0], s[j][1], dv) | ((uint32_t)quant_e4m3x2<kChecked>(s[j][2], s[j][3], dv) << 16);
         hi = quant_e4m3x2<kChecked>(s[j][4], s[j][5], dv) | ((uint32_t)quant_e4m3x2<kChecked>(s[j][6], s[j][7], dv) << 16);
+      } else if (!kChecked) {
+        lo = quant4_fast(s[j][0], s[j][1], s[j][2], s[j][3], dv);
+        hi = quant4_fast(s[j][4], s[j][5], s[j][6], s[j][7], dv);
       } else {
         lo = hi = 0;
 #pragma unroll
         for (int e = 0; e < 4; ++e) {
-          lo |= (uint32_t)(uint8_t)quant_int8<kChecked>(s[j][e], dv) << (8 * e);
-          hi |= (uint32_t)(uint8_t)quant_int8<kChecked>(s[j][4 + e], dv) << (8 * e);
+          lo |= (uint32_t)(uint8_t)quant_int8<true>(s[j][e], dv) << (8 * e);
+          hi |= (uint32_t)(uint8_t)quant_int8<true>(s[j][4 + e], dv) << (8 * e);
         }
       }
       __stcs(crow + v, make_uint2(lo, hi));
@@ -308,7 +311,7 @@ __global__ void __launch_bounds__(512) add_rmsnorm_pipe_kernel(const T* __restri
       }
       continue;
     }
-    float amax = 0.0f, amin = __int_as_float(0x7f800000);
+    float amax = 0.0f;
 #pragma unroll
     for (int j = 0; j < VPT; ++j) {
       const int v = tid + j * nthr;
@@ -322,7 +325,6 @@ __global__ void __launch_bounds__(512) add_rmsnorm_pipe_kernel(const T* __restri
         for (int e = 0; e < 8; ++e) {
           s[j][e] = __fmul_rn(__fmul_rn(s[j][e], rinv), wf[j][e]);
           amax = fmaxf(amax, fabsf(s[j][e]));
-          amin = fminf(amin, fabsf(s[j][e]));
         }
       }
     }
@@ -331,9 +333,9 @@ __global__ void __launch_bounds__(512) add_rmsnorm_pipe_kernel(const T* __restri
     const float scale = fmaxf(__fdiv_rn(amax, qmax), kMinScalingFactor);
     const Divisor dv = make_divisor(scale);
     uint2* crow = reinterpret_cast<uint2*>(codes + row * (int64_t)nvec * 8);
-    // One check per thread and row instead of one per element: the FMA-corrected
-    // division is valid for every value this thread holds when the smallest one is.
-    if (amin >= dv.thresh)
+    // The scale is the row's amax / qmax (or the floor above it), so one check of the
+    // divisor's range covers every value of the row (fast_divisor).
+    if (fast_divisor(dv))
       store_codes<VPT, MODE, false>(s, dv, crow, tid, nthr, nvec);
     else
       store_codes<VPT, MODE, true>(s, dv, crow, tid, nthr, nvec);
