@@ -212,7 +212,7 @@ KVB_API size_t kvb_paged_attention_workspace_size(int batch, int num_q_heads, in
  * k_new / v_new [B, Hkv, D] (new_dtype, optional, e4m3 caches only): each sequence's newest
  * token (position seq_len - 1) is first quantised (e4m3(clamp(x / scale[h]))) and written
  * to its slot, and the attention uses the written codes.
- * partition_size: tokens per split-KV partition (multiple of 16; 0 = 256).
+ * partition_size: tokens per split-KV partition (multiple of 16; 0 = 512).
  * exp_sums, max_logits [B, Hq, max_partitions] and tmp_out [B, Hq, max_partitions, D]
  * (out_dtype, optional, all or none): the v2 partition outputs; then out uses the v2
  * normalisation (global_sum + 1e-6) and max_partitions must equal

@@ -39,15 +39,17 @@ template <> struct CacheTraits<uint8_t> { static constexpr int kBytes = 1; stati
 template <> struct CacheTraits<__half> { static constexpr int kBytes = 2; static constexpr bool kBf16 = false; };
 template <> struct CacheTraits<__nv_bfloat16> { static constexpr int kBytes = 2; static constexpr bool kBf16 = true; };
 
+// Not volatile: the MMA has outputs, and the compiler may interleave it with the surrounding
+// conversions and shared-memory loads.
 __device__ __forceinline__ void mma16816(float (&d)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1, bool bf16) {
   if (bf16) {
-    asm volatile(
+    asm(
         "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
         "{%0,%1,%2,%3};"
         : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
         : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
   } else {
-    asm volatile(
+    asm(
         "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
         "{%0,%1,%2,%3};"
         : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
@@ -164,6 +166,9 @@ __global__ void __launch_bounds__(MAXT, MAXT <= 288 ? 2 : 1) paged_decode_kernel
   extern __shared__ __align__(128) uint8_t smem[];
   __shared__ uint64_t full[kStagesMax], empty[kStagesMax];
 
+  // The merge grid (a programmatic dependent) may be scheduled once every CTA of this grid has
+  // started; it waits for this grid's completion before reading anything this grid writes.
+  asm volatile("griddepcontrol.launch_dependents;");
   const int p = blockIdx.x, b = blockIdx.y;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int ncons = a.hkv * a.tiles_per_kv;          // consumer warps; warp ncons is the producer
@@ -209,9 +214,10 @@ __global__ void __launch_bounds__(MAXT, MAXT <= 288 ? 2 : 1) paged_decode_kernel
       const uint64_t pol = policy_evict_first();
       const uint8_t* kc = reinterpret_cast<const uint8_t*>(a.k_cache);
       const uint8_t* vc = reinterpret_cast<const uint8_t*>(a.v_cache);
-      for (int i = 0; i < nchunks; ++i) {
-        const int s = i % S;
-        if (i >= S && !mbar_wait_bounded(&empty[s], (uint32_t)((i / S) - 1) & 1u)) break;
+      int s = 0;
+      uint32_t ph = 0;                               // stage i % S and phase (i / S) & 1, without divisions
+      for (int i = 0; i < nchunks; ++i, s = (s + 1 == S) ? 0 : s + 1, ph ^= (s == 0) ? 1u : 0u) {
+        if (i >= S && !mbar_wait_bounded(&empty[s], ph ^ 1u)) break;
         const int64_t t0 = t_begin + (int64_t)i * kChunk;
         const int64_t t1 = t_end < t0 + kChunk ? t_end : t0 + kChunk;   // rows past the end are not copied
         // The chunk is copied as runs of rows that stay inside one block (any block size).
@@ -273,9 +279,10 @@ __global__ void __launch_bounds__(MAXT, MAXT <= 288 ? 2 : 1) paged_decode_kernel
   const int64_t new_tok = a.k_new ? L - 1 : -1;
 
   bool failed = false;
-  for (int i = 0; i < nchunks; ++i) {
-    const int s = i % S;
-    if (!mbar_wait_bounded(&full[s], (uint32_t)(i / S) & 1u)) {
+  int s = 0;
+  uint32_t ph = 0;                                   // stage i % S and phase (i / S) & 1
+  for (int i = 0; i < nchunks; ++i, s = (s + 1 == S) ? 0 : s + 1, ph ^= (s == 0) ? 1u : 0u) {
+    if (!mbar_wait_bounded(&full[s], ph)) {
       failed = true;
       break;
     }
@@ -557,25 +564,63 @@ __global__ void __launch_bounds__(128) paged_decode_f32_kernel(const __grid_cons
 }
 
 // out[b, h, :] = sum_p 2^(m_p - M) o_p / (sum_p 2^(m_p - M) l_p + eps)   (paged_attention_v2.py:163-173)
+// Combines the partitions of one (sequence, query head): out = sum_p o_p 2^(m_p - M) /
+// (sum_p l_p 2^(m_p - M) + eps).  The partition weights are computed once into shared memory
+// (dynamic, pmax floats) and every thread then sums one output dimension with independent loads.
 __global__ void __launch_bounds__(128) decode_merge_kernel(const float* __restrict__ m_part, const float* __restrict__ l_part,
                                                            const float* __restrict__ o_part, const void* seq_lens, int sl64,
                                                            int hq, int D, int part, int pmax, float eps, void* out,
                                                            int out_dtype) {
+  extern __shared__ float wgt[];        // [pmax]
+  __shared__ float red[32];
   const int bh = blockIdx.x, b = bh / hq;
   const int64_t L = sl64 ? reinterpret_cast<const int64_t*>(seq_lens)[b] : (int64_t)reinterpret_cast<const int32_t*>(seq_lens)[b];
   const int64_t npl = (L + part - 1) / part;
   const int np = (int)(npl < pmax ? npl : pmax);
+  // Launched as a programmatic dependent of the decode grid: wait until that grid has
+  // completed and its partials are visible (returns at once without a prerequisite grid).
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+  const float* mp = m_part + (int64_t)bh * pmax;
+  const float* lp = l_part + (int64_t)bh * pmax;
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nwarps = blockDim.x >> 5;
+  // block max of the (possibly negative) log2-domain maxima; idle lanes contribute -inf
   float M = -INFINITY;
-  for (int p = 0; p < np; ++p) M = fmaxf(M, m_part[(int64_t)bh * pmax + p]);
+  for (int p = threadIdx.x; p < np; p += blockDim.x) M = fmaxf(M, mp[p]);
+#pragma unroll
+  for (int off = 16; off > 0; off >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, off));
+  if (lane == 0) red[warp] = M;
+  __syncthreads();
+  M = lane < nwarps ? red[lane] : -INFINITY;
+#pragma unroll
+  for (int off = 16; off > 0; off >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, off));
   const float Mu = M == -INFINITY ? 0.0f : M;
-  float Ls = 0.0f;
-  for (int p = 0; p < np; ++p) Ls += l_part[(int64_t)bh * pmax + p] * exp2f(m_part[(int64_t)bh * pmax + p] - Mu);
-  const float inv = np > 0 ? 1.0f / (Ls + eps) : 0.0f;
+  float ls = 0.0f;
+  for (int p = threadIdx.x; p < np; p += blockDim.x) {
+    const float w = exp2f(mp[p] - Mu);
+    wgt[p] = w;
+    ls += lp[p] * w;
+  }
+#pragma unroll
+  for (int off = 16; off > 0; off >>= 1) ls += __shfl_xor_sync(0xffffffffu, ls, off);
+  __syncthreads();                       // every warp has read red; wgt is complete
+  if (lane == 0) red[warp] = ls;
+  __syncthreads();
+  ls = lane < nwarps ? red[lane] : 0.0f;
+#pragma unroll
+  for (int off = 16; off > 0; off >>= 1) ls += __shfl_xor_sync(0xffffffffu, ls, off);
+  const float inv = np > 0 ? 1.0f / (ls + eps) : 0.0f;
+  const float* op = o_part + (int64_t)bh * pmax * D;
   for (int d = threadIdx.x; d < D; d += blockDim.x) {
-    float acc = 0.0f;
-    for (int p = 0; p < np; ++p)
-      acc += o_part[((int64_t)bh * pmax + p) * D + d] * exp2f(m_part[(int64_t)bh * pmax + p] - Mu);
-    store_any(out, out_dtype, (int64_t)bh * D + d, acc * inv);
+    float acc0 = 0.0f, acc1 = 0.0f, acc2 = 0.0f, acc3 = 0.0f;
+    int p = 0;
+    for (; p + 4 <= np; p += 4) {
+      acc0 += op[(int64_t)p * D + d] * wgt[p];
+      acc1 += op[(int64_t)(p + 1) * D + d] * wgt[p + 1];
+      acc2 += op[(int64_t)(p + 2) * D + d] * wgt[p + 2];
+      acc3 += op[(int64_t)(p + 3) * D + d] * wgt[p + 3];
+    }
+    for (; p < np; ++p) acc0 += op[(int64_t)p * D + d] * wgt[p];
+    store_any(out, out_dtype, (int64_t)bh * D + d, ((acc0 + acc1) + (acc2 + acc3)) * inv);
   }
 }
 
@@ -652,9 +697,13 @@ extern "C" int kvb_paged_attention(const void* query, int q_dtype, const void* k
   const int group = num_q_heads / num_kv_heads;
   const int tiles = (group + 7) / 8;
   if (num_kv_heads * tiles > 16) return set_error(KVB_E_SHAPE, "paged_attention: more than 16 (kv head, 8-query) tiles");
-  int part = partition_size > 0 ? partition_size : 256;
+  int part = partition_size > 0 ? partition_size : 512;
   if (part % kChunk) return set_error(KVB_E_SHAPE, "paged_attention: partition_size must be a multiple of 16");
-  int pmax = (int)((max_seq_len + part - 1) / part);
+  const int64_t pmax64 = (max_seq_len + part - 1) / part;
+  if (pmax64 > 12288)
+    return set_error(KVB_E_SHAPE, "paged_attention: %lld partitions (> 12288); use a larger partition_size",
+                     (long long)pmax64);
+  int pmax = (int)pmax64;
   if (pmax < 1) pmax = 1;
   if (exp_sums || max_logits || tmp_out) {
     if (!exp_sums || !max_logits || !tmp_out) return set_error(KVB_E_ARG, "paged_attention: v2 outputs come together");
@@ -703,8 +752,26 @@ extern "C" int kvb_paged_attention(const void* query, int q_dtype, const void* k
   }
   if (rc) return rc;
   const float eps = exp_sums ? 1e-6f : 0.0f;
-  decode_merge_kernel<<<batch * num_q_heads, 128, 0, st>>>(a.m_part, a.l_part, a.o_part, seq_lens, a.sl64, num_q_heads,
-                                                           head_dim, part, pmax, eps, out, out_dtype);
+  // Programmatic dependent launch: the merge grid is scheduled while the decode grid drains
+  // (every decode CTA allows it as it starts) and waits on the device for its partials, which
+  // hides the launch gap between the two kernels.
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3((unsigned)(batch * num_q_heads));
+  cfg.blockDim = dim3(128);
+  cfg.dynamicSmemBytes = (size_t)pmax * sizeof(float);   // partition weights
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  const float* mp = a.m_part;
+  const float* lp = a.l_part;
+  const float* op = a.o_part;
+  const int sl64 = a.sl64;
+  cudaError_t e = cudaLaunchKernelEx(&cfg, decode_merge_kernel, mp, lp, op, seq_lens, sl64, num_q_heads, head_dim, part,
+                                     pmax, eps, out, out_dtype);
+  if (e != cudaSuccess) return set_error(KVB_E_LAUNCH, "decode_merge_kernel: %s", cudaGetErrorString(e));
   return check_launch("decode_merge_kernel");
 }
 
@@ -759,7 +826,7 @@ extern "C" int kvb_paged_attention_noalloc(const void* query, int q_dtype, const
                                            void* stream) {
   if (batch < 0 || num_q_heads <= 0 || head_dim <= 0 || max_seq_len < 0)
     return set_error(KVB_E_ARG, "paged_attention_noalloc: bad sizes");
-  const int part = partition_size > 0 ? partition_size : 256;
+  const int part = partition_size > 0 ? partition_size : 512;
   int64_t pmax = (max_seq_len + part - 1) / part;
   if (pmax < 1) pmax = 1;
   const size_t need = kvb_paged_attention_workspace_size(batch, num_q_heads, head_dim, (int)pmax);

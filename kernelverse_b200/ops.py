@@ -187,7 +187,7 @@ def _paged_attention(query, key_cache, value_cache, seq_lens, block_table, *, nu
     b, hq, d = query.shape
     out_dtype = out_dtype or query.dtype
     out = torch.empty((b, hq, d), dtype=out_dtype, device=dev)
-    part = partition_size if partition_size else 256
+    part = partition_size if partition_size else 512
     pmax = max(1, -(-int(max_seq_len) // part))
     es = ml = tmp = None
     if v2:

@@ -115,3 +115,46 @@ def test_repeat_calls_are_deterministic():
     c = _ops().dynamic_scaled_int8_quant(x)
     d = _ops().dynamic_scaled_int8_quant(x)
     assert torch.equal(c[0], d[0]) and torch.equal(c[1], d[1])
+
+
+def _edge_rows(k):
+    """FP32 rows that exercise the quotient edge cases of the fast quantiser path:
+    row 0  amax 127 (scale exactly 1): ties k + 0.5 must round half to even;
+    row 1  amax 1: values far below the FMA-division threshold (tiny normals, subnormals,
+           signed zeros) next to ordinary ones;
+    row 2  amax 1e-30 with a subnormal eps: a tiny but in-range scale;
+    row 3  amax 1e-37: a scale below 2^-120, which takes the checked path."""
+    rng = seeded(k)
+    x = np.zeros((4, k), np.float32)
+    ties = np.arange(-126, 127, dtype=np.float32) + np.float32(0.5)
+    x[0] = rng.choice(ties, k)
+    x[0, 0] = 127.0
+    tiny = np.array([1e-30, -1e-30, 1e-38, -1e-38, 1e-40, -1e-40, 1e-45, -1e-45, 0.0, -0.0], np.float32)
+    x[1] = np.where(rng.random(k) < 0.5, rng.choice(tiny, k), rng.standard_normal(k).astype(np.float32) * 0.3)
+    x[1, 0] = 1.0
+    x[2] = (rng.standard_normal(k) * 1e-31).astype(np.float32)
+    x[2, 0] = 1e-30
+    x[3] = (rng.standard_normal(k) * 1e-38).astype(np.float32)
+    x[3, 0] = 1e-37
+    return x
+
+
+@pytest.mark.parametrize("g", [128, 4096])
+def test_group_quant_ties_and_tiny_values(g):
+    """Bit-exact codes where the quotient is a tie, far below the division threshold, or the
+    scale itself is tiny (a subnormal eps lets the scale follow the amax) -- the subwarp
+    (g = 128) and row-block (g = 4096) kernels."""
+    x = _edge_rows(4096)
+    eps = float(np.float32(1e-44))
+    q, s = _ops().per_token_group_quant_int8(dev(x, torch.float32), g, eps)
+    rq, rs = quant.per_token_group_quant_int8(x, g, eps)
+    np.testing.assert_array_equal(host(s), rs)
+    np.testing.assert_array_equal(host(q), rq)
+
+
+def test_dynamic_quant_ties_and_tiny_values():
+    x = _edge_rows(1024)[:2]                   # per-tensor: amax 127, so scale is exactly 1
+    q, s, _ = _ops().dynamic_scaled_int8_quant(dev(x, torch.float32))
+    rq, rs, _ = quant.dynamic_scaled_int8_quant(x, "FP32")
+    np.testing.assert_array_equal(host(s), rs)
+    np.testing.assert_array_equal(host(q), rq)

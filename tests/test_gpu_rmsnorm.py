@@ -124,3 +124,27 @@ def test_add_rmsnorm_shapes(dt, shape):
     ref = rmsnorm.add_rmsnorm(host(x), host(r), host(w), 1e-6, dt)
     tol = OUT_TOL[dt]
     np.testing.assert_allclose(host(out), ref, rtol=tol, atol=tol)
+
+
+@pytest.mark.parametrize("kind", ["e4m3", "int8"])
+def test_fused_tiny_values_quantise_to_zero(kind):
+    """Rows whose normalised values span from ordinary magnitudes down to far below the
+    FMA-division threshold: the tiny ones must give (signed) zero codes, as the oracle does."""
+    rng = seeded(21)
+    m, h = 8, 4096
+    x = bf16_normal(rng, (m, h))
+    tiny = numerics.round_bf16(np.array([1e-30, -1e-30, 1e-36, -1e-36, 0.0, -0.0], np.float32))
+    mask = rng.random((m, h)) < 0.5
+    x = np.where(mask, rng.choice(tiny, (m, h)), x).astype(np.float32)
+    r = np.zeros((m, h), np.float32)
+    w = bf16_normal(rng, (h,), std=0.02, mean=1.0)
+    bf = torch.bfloat16
+    qd = torch.float8_e4m3fn if kind == "e4m3" else torch.int8
+    got = _ops().add_rmsnorm_quant(dev(x, bf), dev(r, bf), dev(w, bf), 1e-6, quant_dtype=qd)
+    _check_fused(x, r, w, got, kind)
+    codes = host(got[1])
+    small = np.abs(x) < 1e-20
+    if kind == "e4m3":
+        assert np.all((codes.view(np.uint8)[small] & 0x7F) == 0)
+    else:
+        assert np.all(codes[small] == 0)
