@@ -100,6 +100,17 @@ KVB_API int kvb_per_token_group_quant_int8(const void* x, int x_dtype, int64_t t
                                    int64_t group_size, float eps, int8_t* q, float* scales,
                                    void* stream);
 
+/*
+ * Static-scale int8 quantisation.
+ * Replaces operators/quantization/static_scaled_int8_quant/static_scaled_int8_quant.py:28-32
+ * (MIN_SCALE at helpers.py:8), float32 arithmetic (the reference's correctness mode):
+ *   q = clamp(round_half_even(x / max(scale, 1/(448*512)) + azp), -127, 127).
+ * x: `numel` elements of x_dtype (KVB_F32/F16/BF16); scale: 1 float32 and azp: 1 int32 (may
+ * be NULL: 0), both in device memory; q: numel int8.  One kernel, no host synchronisation.
+ */
+KVB_API int kvb_static_scaled_int8_quant(const void* x, int x_dtype, int64_t numel, const float* scale,
+                                         const int32_t* azp, int8_t* q, void* stream);
+
 /* ---------------------------------------------------------------- residual add + RMSNorm */
 
 /*
@@ -188,6 +199,22 @@ KVB_API int kvb_paged_kv_cache_update(const void* to_cache, const void* kv_cache
 KVB_API int kvb_paged_fp8_kv_write(const void* x_new, int x_dtype, void* cache, const void* slot_mapping,
                                    int index_dtype, const float* head_scales, int64_t num_tokens, int64_t num_slots,
                                    int num_heads, int head_dim, void* stream);
+
+/*
+ * KV-cache write into [batch, heads, max_seq_len, head_dim] caches.
+ * Replaces operators/kv_cache/kv_cache_write/kv_cache_write.py:24-58: k_cache_out / v_cache_out
+ * become copies of k_cache_in / v_cache_in (no copy when an input is NULL or equals its output),
+ * then k_cache_out[b, h, pos(b, w), :] = key[b, h, w, :] and likewise for V, with
+ * pos(b, w) = positions[w] (per_batch == 0, positions [write_len]) or positions[b, w]
+ * (per_batch != 0, [batch, write_len]), KVB_I32 or KVB_I64.  A negative position counts from
+ * the end as torch indexing does; positions outside [-max_seq_len, max_seq_len) are skipped
+ * and flagged in kvb_device_status.  key/value: [batch, heads, write_len, head_dim]; all
+ * tensors of `dtype`.  Launches one copy per cache and one scatter kernel.
+ */
+KVB_API int kvb_kv_cache_write(const void* key, const void* value, const void* k_cache_in, const void* v_cache_in,
+                               void* k_cache_out, void* v_cache_out, const void* positions, int index_dtype,
+                               int per_batch, int dtype, int64_t batch, int64_t heads, int64_t max_seq_len,
+                               int64_t write_len, int64_t head_dim, void* stream);
 
 /* ---------------------------------------------------------------- paged decode attention */
 

@@ -27,6 +27,7 @@ SIGNATURES = {
     "kvb_dynamic_scaled_int8_quant_workspace_size": (_SZ, []),
     "kvb_dynamic_scaled_int8_quant": (_I, [_P, _I, _I64, _P, _P, _P, _P, _SZ, _P]),
     "kvb_per_token_group_quant_int8": (_I, [_P, _I, _I64, _I64, _I64, _F, _P, _P, _P]),
+    "kvb_static_scaled_int8_quant": (_I, [_P, _I, _I64, _P, _P, _P, _P]),
     "kvb_add_rmsnorm": (_I, [_P, _P, _P, _I, _I64, _I64, _F, _P, _P]),
     "kvb_add_rmsnorm_quant": (_I, [_P, _P, _P, _I, _I64, _I64, _F, _P, _P, _I, _P, _P]),
     "kvb_w8a8_workspace_size": (_SZ, [_I64, _I64, _I64, _I, _I]),
@@ -34,6 +35,7 @@ SIGNATURES = {
     "kvb_w8a8_scaled_mm_allgather": (_I, [_P, _P, _P, _P, _P, _I, _I64, _I64, _I64, _P, _I, _I, _I64, _I, _P]),
     "kvb_paged_kv_cache_update": (_I, [_P, _P, _P, _P, _I, _I, _I64, _I64, _I64, _P]),
     "kvb_paged_fp8_kv_write": (_I, [_P, _I, _P, _P, _I, _P, _I64, _I64, _I, _I, _P]),
+    "kvb_kv_cache_write": (_I, [_P, _P, _P, _P, _P, _P, _P, _I, _I, _I, _I64, _I64, _I64, _I64, _I64, _P]),
     "kvb_paged_attention_workspace_size": (_SZ, [_I, _I, _I, _I]),
     "kvb_paged_attention": (_I, [_P, _I, _P, _P, _I, _P, _P, _P, _I, _P, _I64, _I, _I, _I, _I, _I, _I64, _I64, _F,
                                  _P, _P, _I, _I, _P, _I, _P, _P, _P, _I, _P, _SZ, _P]),

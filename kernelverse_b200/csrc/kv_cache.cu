@@ -6,6 +6,9 @@
 //   slot_mapping[i] (skipped when negative).
 // * kvb_paged_fp8_kv_write: the BASELINE fourth config's write -- token i, head h is stored
 //   as e4m3(clamp(x / scale[h], +-448)) codes in slot slot_mapping[i].
+// * kvb_kv_cache_write: operators/kv_cache/kv_cache_write/kv_cache_write.py:24-58 -- copies
+//   of the [batch, heads, max_seq_len, head_dim] caches with the new rows scattered in at
+//   their positions.
 // Slots are bounds-checked on the device: an index >= num_slots is skipped and recorded in
 // the status word (kvb_device_status bit 1).
 #include "kvb_common.cuh"
@@ -78,6 +81,33 @@ __global__ void __launch_bounds__(256) fp8_kv_write_kernel(const T* __restrict__
   }
 }
 
+// kv_cache_write: one warp per written row (b, h, w) of K (blockIdx.y == 0) or V (1); the row of
+// head_dim elements goes to position positions[w] (shared) or positions[b, w] (per batch).
+__global__ void __launch_bounds__(128) kv_write_rows_kernel(const uint8_t* __restrict__ key, const uint8_t* __restrict__ value,
+                                                            uint8_t* __restrict__ k_out, uint8_t* __restrict__ v_out,
+                                                            const void* positions, int idx64, int per_batch, int64_t rows,
+                                                            int64_t heads, int64_t max_seq_len, int64_t write_len,
+                                                            int64_t row_bytes, int vec16) {
+  const int64_t r = (int64_t)blockIdx.x * 4 + (threadIdx.x >> 5);
+  if (r >= rows) return;
+  const int lane = threadIdx.x & 31;
+  const int64_t w = r % write_len, bh = r / write_len, b = bh / heads;
+  int64_t pos = load_slot(positions, idx64, per_batch ? b * write_len + w : w);
+  if (pos < 0) pos += max_seq_len;                 // torch indexing: negative positions count from the end
+  if (pos < 0 || pos >= max_seq_len) {
+    if (lane == 0) atomicOr(&g_tu_status, kStatusBadSlot);
+    return;
+  }
+  const uint8_t* src = (blockIdx.y ? value : key) + r * row_bytes;
+  uint8_t* dst = (blockIdx.y ? v_out : k_out) + (bh * max_seq_len + pos) * row_bytes;
+  if (vec16) {
+    for (int64_t k = lane; k < row_bytes / 16; k += 32)
+      reinterpret_cast<uint4*>(dst)[k] = reinterpret_cast<const uint4*>(src)[k];
+  } else {
+    for (int64_t k = lane; k < row_bytes; k += 32) dst[k] = src[k];
+  }
+}
+
 int grid_for(int64_t work, int threads) {
   int dev = 0, sms = 148;
   cudaGetDevice(&dev);
@@ -122,6 +152,46 @@ extern "C" int kvb_paged_kv_cache_update(const void* to_cache, const void* kv_ca
                                                             reinterpret_cast<uint8_t*>(kv_cache_out), slot_mapping,
                                                             index_dtype == KVB_I64, num_slots, slot_bytes, vec16);
   return check_launch("scatter_rows_kernel");
+}
+
+namespace {
+int copy_cache(const void* in, void* out, int64_t n, cudaStream_t st) {
+  if (!in || in == out || n == 0) return KVB_OK;
+  if (aligned16(in) && aligned16(out) && n % 16 == 0)
+    copy16_kernel<<<grid_for(n / 16, 256), 256, 0, st>>>(reinterpret_cast<const uint4*>(in), reinterpret_cast<uint4*>(out),
+                                                        n / 16);
+  else
+    copy1_kernel<<<grid_for(n, 256), 256, 0, st>>>(reinterpret_cast<const uint8_t*>(in), reinterpret_cast<uint8_t*>(out), n);
+  return check_launch("copy_kernel");
+}
+}  // namespace
+
+extern "C" int kvb_kv_cache_write(const void* key, const void* value, const void* k_cache_in, const void* v_cache_in,
+                                  void* k_cache_out, void* v_cache_out, const void* positions, int index_dtype,
+                                  int per_batch, int dtype, int64_t batch, int64_t heads, int64_t max_seq_len,
+                                  int64_t write_len, int64_t head_dim, void* stream) {
+  if (batch < 0 || heads < 0 || max_seq_len < 0 || write_len < 0 || head_dim < 0)
+    return set_error(KVB_E_ARG, "kv_cache_write: negative size");
+  if (index_dtype != KVB_I32 && index_dtype != KVB_I64) return set_error(KVB_E_DTYPE, "kv_cache_write: index dtype");
+  const int es = dtype == KVB_E4M3 ? 1 : dtype_size(dtype);
+  if (es <= 0) return set_error(KVB_E_DTYPE, "kv_cache_write: dtype %d", dtype);
+  if (!k_cache_out || !v_cache_out) return set_error(KVB_E_ARG, "kv_cache_write: null output");
+  const int64_t rows = batch * heads * write_len, row_bytes = head_dim * es;
+  if (rows > 0 && (!key || !value || !positions)) return set_error(KVB_E_ARG, "kv_cache_write: null pointer");
+  cudaStream_t st = as_stream(stream);
+  const int64_t cache_bytes = batch * heads * max_seq_len * row_bytes;
+  int rc = copy_cache(k_cache_in, k_cache_out, cache_bytes, st);
+  if (!rc) rc = copy_cache(v_cache_in, v_cache_out, cache_bytes, st);
+  if (rc || rows == 0 || row_bytes == 0) return rc;
+  if ((rows + 3) / 4 > 0x7fffffffLL) return set_error(KVB_E_SHAPE, "kv_cache_write: too many rows");
+  const int vec16 = row_bytes % 16 == 0 && aligned16(key) && aligned16(value) && aligned16(k_cache_out) &&
+                    aligned16(v_cache_out);
+  dim3 grid((unsigned)((rows + 3) / 4), 2);
+  kv_write_rows_kernel<<<grid, 128, 0, st>>>(reinterpret_cast<const uint8_t*>(key), reinterpret_cast<const uint8_t*>(value),
+                                             reinterpret_cast<uint8_t*>(k_cache_out), reinterpret_cast<uint8_t*>(v_cache_out),
+                                             positions, index_dtype == KVB_I64, per_batch, rows, heads, max_seq_len,
+                                             write_len, row_bytes, vec16);
+  return check_launch("kv_write_rows_kernel");
 }
 
 extern "C" int kvb_paged_fp8_kv_write(const void* x_new, int x_dtype, void* cache, const void* slot_mapping,

@@ -86,6 +86,61 @@ __global__ void __launch_bounds__(256) tensor_quant_kernel(const T* __restrict__
     q[i] = quant_int8(Elem<T>::to_f(x[i]), d);
 }
 
+// ---------------------------------------------------------------- static scale
+// q = clamp(round_half_even(x / max(scale, MIN_SCALE) + azp), +-127) in float32
+// (static_scaled_int8_quant.py:28-32 in its float32 correctness mode).  The scale is not an
+// amax here, so x is first clamped to +-(|azp| + 256) * s: beyond that the result is +-127
+// either way, and inside it the quotient is in the FMA-division domain (values below the
+// division threshold still give quotients under 2^-100, which round away against azp).
+__device__ __forceinline__ uint32_t static_code4(const float (&f)[8], int base, const Divisor& d, float lim, float z) {
+  constexpr float kRound = 12582912.0f;   // 1.5 * 2^23: rounds half to even into the low byte
+  uint32_t b[4];
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const float xc = fminf(fmaxf(f[base + i], -lim), lim);
+    const float v = fminf(fmaxf(__fadd_rn(div_rn_fast(xc, d), z), -kInt8Max), kInt8Max);
+    b[i] = __float_as_uint(__fadd_rn(v, kRound));
+  }
+  return __byte_perm(__byte_perm(b[0], b[1], 0x0040), __byte_perm(b[2], b[3], 0x0040), 0x5410);
+}
+__device__ __forceinline__ int8_t static_code_checked(float x, float s, float z) {
+  const float v = fminf(fmaxf(__fadd_rn(__fdiv_rn(x, s), z), -kInt8Max), kInt8Max);
+  return (int8_t)__float2int_rn(v);
+}
+
+template <typename T>
+__global__ void __launch_bounds__(256) static_quant_kernel(const T* __restrict__ x, int64_t numel, int64_t nvec,
+                                                           const float* __restrict__ scale,
+                                                           const int32_t* __restrict__ azp, int8_t* __restrict__ q) {
+  const float s = fmaxf(*scale, kMinScalingFactor);
+  const float z = azp ? (float)*azp : 0.0f;
+  const Divisor d = make_divisor(s);
+  const bool fast = fast_divisor(d) && fabsf(z) <= 0x1p90f;
+  const float lim = (fabsf(z) + 256.0f) * s;
+  const int64_t stride = (int64_t)gridDim.x * blockDim.x;
+  for (int64_t v = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; v < nvec; v += stride) {
+    Vec8<T> a;
+    a.load_stream(x + v * 8);
+    float f[8];
+    a.unpack(f);
+    uint2 out;
+    if (fast) {
+      out = make_uint2(static_code4(f, 0, d, lim, z), static_code4(f, 4, d, lim, z));
+    } else {
+      uint32_t lo = 0, hi = 0;
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        lo |= (uint32_t)(uint8_t)static_code_checked(f[i], s, z) << (8 * i);
+        hi |= (uint32_t)(uint8_t)static_code_checked(f[4 + i], s, z) << (8 * i);
+      }
+      out = make_uint2(lo, hi);
+    }
+    reinterpret_cast<uint2*>(q)[v] = out;
+  }
+  for (int64_t i = nvec * 8 + (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < numel; i += stride)
+    q[i] = static_code_checked(Elem<T>::to_f(x[i]), s, z);
+}
+
 // ---------------------------------------------------------------- per-group, small groups
 // One 8-element vector per thread; a group of G = 8*L elements spans L consecutive lanes
 // (L a power of two <= 32), so its amax is an L-lane shuffle reduction.
@@ -264,6 +319,33 @@ extern "C" int kvb_dynamic_scaled_int8_quant(const void* x, int x_dtype, int64_t
     case KVB_F16: return launch_tensor_quant<__half>(x, numel, q, scale, azp, amax, st);
     case KVB_BF16: return launch_tensor_quant<__nv_bfloat16>(x, numel, q, scale, azp, amax, st);
     default: return set_error(KVB_E_DTYPE, "dynamic_scaled_int8_quant: x dtype %d unsupported", x_dtype);
+  }
+}
+
+template <typename T>
+int launch_static_quant(const void* xv, int64_t numel, const float* scale, const int32_t* azp, int8_t* q,
+                        cudaStream_t st) {
+  const T* x = static_cast<const T*>(xv);
+  const bool vec = aligned16(x) && aligned8(q);
+  const int64_t nvec = vec ? numel / 8 : 0;
+  const int64_t work = nvec > 0 ? nvec : numel;
+  int blocks = (int)std::min<int64_t>((work + 255) / 256, (int64_t)sm_count() * 8);
+  if (blocks < 1) blocks = 1;
+  static_quant_kernel<T><<<blocks, 256, 0, st>>>(x, numel, nvec, scale, azp, q);
+  return check_launch("static_quant_kernel");
+}
+
+extern "C" int kvb_static_scaled_int8_quant(const void* x, int x_dtype, int64_t numel, const float* scale,
+                                            const int32_t* azp, int8_t* q, void* stream) {
+  if (numel < 0) return set_error(KVB_E_ARG, "static_scaled_int8_quant: numel < 0");
+  if (numel == 0) return KVB_OK;
+  if (!x || !q || !scale) return set_error(KVB_E_ARG, "static_scaled_int8_quant: null pointer");
+  cudaStream_t st = as_stream(stream);
+  switch (x_dtype) {
+    case KVB_F32: return launch_static_quant<float>(x, numel, scale, azp, q, st);
+    case KVB_F16: return launch_static_quant<__half>(x, numel, scale, azp, q, st);
+    case KVB_BF16: return launch_static_quant<__nv_bfloat16>(x, numel, scale, azp, q, st);
+    default: return set_error(KVB_E_DTYPE, "static_scaled_int8_quant: x dtype %d unsupported", x_dtype);
   }
 }
 

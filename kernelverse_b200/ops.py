@@ -78,6 +78,22 @@ def dynamic_scaled_int8_quant(x: torch.Tensor) -> Tuple[torch.Tensor, torch.Tens
     return q, scale, azp
 
 
+def static_scaled_int8_quant(x: torch.Tensor, scale: torch.Tensor, azp: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """operators/quantization/static_scaled_int8_quant/static_scaled_int8_quant.py:28-32 (float32
+    arithmetic): ``clamp(round(x / max(scale, MIN_SCALE) + azp), -127, 127)`` as int8, shape of x.
+    ``scale`` is a one-element float tensor and ``azp`` a one-element integer tensor on the device."""
+    dev = _cuda(x, scale, azp)
+    x = x.contiguous()
+    if scale.numel() != 1 or (azp is not None and azp.numel() != 1):
+        raise ValueError("static_scaled_int8_quant: scale and azp must have one element")
+    s = scale.reshape(1).to(torch.float32)
+    z = azp.reshape(1).to(torch.int32) if azp is not None else None
+    q = torch.empty(x.shape, dtype=torch.int8, device=dev)
+    call("kvb_static_scaled_int8_quant", _ptr(x), kvb_dtype(x.dtype), x.numel(), _ptr(s), _ptr(z) if z is not None else None,
+         _ptr(q), _stream(dev))
+    return q
+
+
 def per_token_group_quant_int8(x: torch.Tensor, group_size: int, eps: float) -> Tuple[torch.Tensor, torch.Tensor]:
     """operators/quantization/per_token_group_quant_int8/per_token_group_quant_int8.py:23-32."""
     dev = _cuda(x)
@@ -159,6 +175,37 @@ def paged_kv_cache_update(to_cache: torch.Tensor, kv_cache: torch.Tensor, slot_m
     return out
 
 
+def kv_cache_write(key_cache: torch.Tensor, value_cache: torch.Tensor, key: torch.Tensor, value: torch.Tensor,
+                   positions: torch.Tensor) -> Tuple[torch.Tensor, torch.Tensor]:
+    """operators/kv_cache/kv_cache_write/kv_cache_write.py:24-58 -> new (key_cache, value_cache).
+
+    Caches [batch, heads, max_seq_len, head_dim]; key/value [batch, heads, write_len, head_dim]
+    (converted to the cache dtype); positions [write_len] (shared) or [batch, write_len]."""
+    dev = _cuda(key_cache, value_cache, key, value, positions)
+    key_cache, value_cache = key_cache.contiguous(), value_cache.contiguous()
+    if key_cache.dim() != 4 or value_cache.shape != key_cache.shape:
+        raise ValueError("kv_cache_write: caches must both be [batch, heads, max_seq_len, head_dim]")
+    b, h, smax, d = key_cache.shape
+    key = key.to(key_cache.dtype).contiguous()
+    value = value.to(key_cache.dtype).contiguous()
+    if key.dim() != 4 or key.shape[:2] != (b, h) or key.shape[3] != d or value.shape != key.shape:
+        raise ValueError("kv_cache_write: key/value must be [batch, heads, write_len, head_dim] like the caches")
+    w = key.shape[2]
+    positions = positions.contiguous()
+    if positions.dim() == 1:
+        per_batch = 0
+        if positions.shape[0] != w:
+            raise ValueError("kv_cache_write: shared positions must have write_len entries")
+    elif positions.dim() == 2 and tuple(positions.shape) == (b, w):
+        per_batch = 1
+    else:
+        raise ValueError("kv_cache_write: positions must be [write_len] or [batch, write_len]")
+    k_out, v_out = torch.empty_like(key_cache), torch.empty_like(value_cache)
+    call("kvb_kv_cache_write", _ptr(key), _ptr(value), _ptr(key_cache), _ptr(value_cache), _ptr(k_out), _ptr(v_out),
+         _ptr(positions), _index_dtype(positions), per_batch, kvb_dtype(key_cache.dtype), b, h, smax, w, d, _stream(dev))
+    return k_out, v_out
+
+
 def paged_fp8_kv_write(x_new: torch.Tensor, cache: torch.Tensor, slot_mapping: torch.Tensor,
                        head_scales: torch.Tensor) -> torch.Tensor:
     """Quantise x_new [T, Hkv, D] into the e4m3 cache [num_blocks, block_size, Hkv, D] in place."""
@@ -238,6 +285,48 @@ def paged_attention_v2(query, key_cache, value_cache, seq_lens, block_table, par
     return _paged_attention(query, key_cache, value_cache, seq_lens, block_table, num_kv_heads=hkv, block_size=bs,
                             num_blocks=nb, max_seq_len=max_len, scale=scale, partition_size=partition_size,
                             out_dtype=output_dtype, v2=True)
+
+
+_FLASH_DECODE_INDEX = {}
+
+
+def _flash_decode_index(dev, b, h, sq, s, causal):
+    """(block table or None, seq_lens) mapping each (batch, head, query token) of a
+    [B, H, S, D] cache to one single-head sequence; cached per shape."""
+    key = (dev, b, h, sq, s, causal)
+    if key not in _FLASH_DECODE_INDEX:
+        bt = None
+        if sq > 1:   # the sq queries of (b, h) share block b * h
+            bt = torch.arange(b * h, dtype=torch.int32, device=dev).repeat_interleave(sq).view(b * h * sq, 1)
+        i = torch.arange(sq, dtype=torch.int32, device=dev)
+        lens = (s - sq + 1 + i) if causal else torch.full((sq,), s, dtype=torch.int32, device=dev)
+        _FLASH_DECODE_INDEX[key] = (bt, lens.repeat(b * h).contiguous())
+    return _FLASH_DECODE_INDEX[key]
+
+
+def flash_decoding_attention(query, key_cache, value_cache, chunk_size: int, causal: bool = False,
+                             scale: Optional[float] = None):
+    """operators/attention/flash_decoding_attention/flash_decoding_attention.py:30-87 ->
+    (output [B, H, Sq, D], exp_sums [B, H, Sq, P], max_logits [B, H, Sq, P], partial_outputs
+    [B, H, Sq, P, D]) with P = ceil(S / chunk_size), all in the query dtype.
+
+    query [B, H, Sq, D]; caches [B, H, S, D] (one KV head per query head).  Every (b, h, query
+    token) is one single-head sequence of the split-KV decode kernel whose partitions are the
+    reference's chunks; a causal query i attends to the first S - Sq + 1 + i keys."""
+    b, h, sq, d = query.shape
+    s = key_cache.shape[2]
+    if key_cache.shape != (b, h, s, d) or value_cache.shape != key_cache.shape:
+        raise ValueError("flash_decoding_attention: caches must be [batch, heads, kv_len, head_dim]")
+    dev = _cuda(query, key_cache, value_cache)
+    scale = d ** -0.5 if scale is None else scale
+    bt, lens = _flash_decode_index(dev, b, h, sq, s, bool(causal))
+    kc = key_cache.contiguous().view(b * h, s, 1, d)
+    vc = value_cache.contiguous().view(b * h, s, 1, d)
+    q = query.contiguous().view(b * h * sq, 1, d)
+    out, es, ml, tmp = _paged_attention(q, kc, vc, lens, bt, num_kv_heads=1, block_size=s, num_blocks=b * h,
+                                        max_seq_len=s, scale=scale, partition_size=chunk_size, v2=True)
+    p = es.shape[-1]
+    return (out.view(b, h, sq, d), es.view(b, h, sq, p), ml.view(b, h, sq, p), tmp.view(b, h, sq, p, d))
 
 
 def batched_decode_attention(q, k_cache, v_cache, seq_lens, scale: Optional[float] = None,

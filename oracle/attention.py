@@ -19,6 +19,9 @@ The oracle, like the device kernels, takes caches as ``[num_blocks, bs, Hkv, D]`
   over a dense ``[B, L, Hkv, D]`` cache with a ``pos < seq_len`` mask.
 * ``paged_fp8_decode``: the BASELINE fourth config: the cache holds e4m3fn
   codes with per-KV-head float32 scales; values are ``code * scale[h]``.
+* ``flash_decoding_attention``: ``operators/attention/flash_decoding_attention/flash_decoding_attention.py:30-87``
+  over ``[B, H, S, D]`` caches in chunks of ``chunk_size`` keys, with the causal mask of
+  ``:89-101`` (query i of Sq sees keys ``<= S - Sq + i``).
 
 Everything is evaluated in float64 and returned as float32.
 """
@@ -131,3 +134,42 @@ def paged_fp8_decode(query, k_codes, v_codes, k_scale, v_scale, seq_lens, block_
         for h in range(hq):
             out[b, h], _ = _attend(q[b, h], k[:, h // grp], v[:, h // grp], scale)
     return out.astype(np.float32)
+
+
+def flash_decoding_attention(query, key_cache, value_cache, chunk_size: int, causal: bool, scale: float):
+    """Returns ``(output [B,H,Sq,D], exp_sums [B,H,Sq,P], max_logits [B,H,Sq,P], partial
+    outputs [B,H,Sq,P,D])``.  Per chunk: ``max`` of the scaled scores (-inf when the chunk is
+    fully masked), ``exp_sum`` of ``exp(score - max)`` (0 when masked), ``partial = weighted /
+    max(exp_sum, 1e-6)``; merged as ``sum(partial * w) / max(sum(w), 1e-6)`` with
+    ``w = exp_sum * exp(max - global_max)`` (flash_decoding_attention.py:46-87)."""
+    q = np.asarray(query, np.float64)
+    k = np.asarray(key_cache, np.float64)
+    v = np.asarray(value_cache, np.float64)
+    b_, h_, sq, d = q.shape
+    s_ = k.shape[2]
+    nch = (s_ + chunk_size - 1) // chunk_size
+    es = np.zeros((b_, h_, sq, nch))
+    mx = np.full((b_, h_, sq, nch), -np.inf)
+    po = np.zeros((b_, h_, sq, nch, d))
+    out = np.zeros((b_, h_, sq, d))
+    for b in range(b_):
+        for h in range(h_):
+            for i in range(sq):
+                limit = s_ - sq + i if causal else s_ - 1        # last visible key
+                for c in range(nch):
+                    k0, k1 = c * chunk_size, min((c + 1) * chunk_size, s_)
+                    k1v = min(k1, limit + 1)
+                    if k1v <= k0:
+                        continue
+                    sc = (k[b, h, k0:k1v] @ q[b, h, i]) * scale
+                    m = sc.max()
+                    p = np.exp(sc - m)
+                    mx[b, h, i, c] = m
+                    es[b, h, i, c] = p.sum()
+                    po[b, h, i, c] = (p @ v[b, h, k0:k1v]) / max(p.sum(), 1e-6)
+                gm = mx[b, h, i].max()
+                w = es[b, h, i] * np.exp(mx[b, h, i] - gm)
+                out[b, h, i] = (po[b, h, i] * w[:, None]).sum(0) / max(w.sum(), 1e-6)
+    f = np.float32
+    return out.astype(f), es.astype(f), mx.astype(f), po.astype(f)
+

@@ -44,3 +44,22 @@ def paged_fp8_kv_write(x_new: np.ndarray, cache_codes: np.ndarray, slot_mapping:
         if s >= 0:
             flat[s] = codes[i]
     return out
+
+
+def kv_cache_write(key_cache, value_cache, key, value, positions):
+    """operators/kv_cache/kv_cache_write/kv_cache_write.py:24-58: copies of the
+    ``[B, H, S, D]`` caches with ``key[b, h, w]`` written at position ``positions[w]``
+    (shared, 1-D) or ``positions[b, w]`` (per batch, 2-D); negative positions count
+    from the end, as torch indexing does."""
+    kc, vc = np.array(key_cache, copy=True), np.array(value_cache, copy=True)
+    pos = np.asarray(positions, np.int64)
+    b_, h_, s_, _ = kc.shape
+    w_ = key.shape[2]
+    for b in range(b_):
+        for w in range(w_):
+            p = int(pos[w] if pos.ndim == 1 else pos[b, w])
+            p = p + s_ if p < 0 else p
+            kc[b, :, p] = key[b, :, w]
+            vc[b, :, p] = value[b, :, w]
+    return kc, vc
+

@@ -6,7 +6,10 @@ Restates, in numpy, the reference operators
   (per-tensor scale, computed in the input dtype, clamped at MIN_SCALING_FACTOR;
   constants at ``.../helpers.py:7-8``), and
 * ``operators/quantization/per_token_group_quant_int8/per_token_group_quant_int8.py:23-32``
-  (per-(token, group) fp32 scale, ``clamp_min(eps)``).
+  (per-(token, group) fp32 scale, ``clamp_min(eps)``), and
+* ``operators/quantization/static_scaled_int8_quant/static_scaled_int8_quant.py:28-32``
+  (static scale and zero point; MIN_SCALE at ``.../helpers.py:8``), in its float32
+  correctness mode.
 
 Low-precision inputs are float32 arrays holding exactly representable values
 (see ``oracle.numerics``).  Only tests, ``smoke()`` and ``bench.py``'s CPU
@@ -55,3 +58,16 @@ def per_token_group_quant_int8(x: np.ndarray, group_size: int, eps: float):
     scales = np.maximum(amax.astype(np.float32) / np.float32(INT8_QMAX), np.float32(eps)).astype(np.float32)
     q = np.clip(np.rint(grouped / scales[..., None]), -INT8_QMAX, INT8_QMAX).astype(np.int8)
     return q.reshape(t, h), scales
+
+
+def static_scaled_int8_quant(x: np.ndarray, scale, azp=0):
+    """Static-scale int8 quantisation (static_scaled_int8_quant.py:28-32, float32 mode):
+    ``q = clamp(round_half_even(x / max(scale, MIN_SCALE) + azp), -127, 127)`` with the
+    quotient and the sum each rounded to float32.  Returns int8 of x's shape."""
+    x = np.asarray(x, dtype=np.float32)
+    s = np.maximum(np.float32(np.asarray(scale, np.float32).reshape(-1)[0]), MIN_SCALING_FACTOR).astype(np.float32)
+    z = np.float32(np.asarray(azp).reshape(-1)[0])
+    with np.errstate(divide="ignore", invalid="ignore", over="ignore"):
+        centered = (x / s).astype(np.float32) + z
+    return np.clip(np.rint(centered), -INT8_QMAX, INT8_QMAX).astype(np.int8)
+

@@ -4,6 +4,9 @@ Run once, in a container where the KernelVerse reference is importable::
 
     KV_REFERENCE_ROOT=<path to KernelVerse checkout> python tests/golden/make_golden.py
 
+``KV_GOLDEN_ONLY=prefix1,prefix2`` writes only the fixtures whose names start with one of
+the prefixes (the others are computed but left untouched).
+
 Each fixture is a small ``.npz`` holding the seeded inputs (made by the
 reference's own ``generate_inputs`` where one exists) and the outputs of the
 reference's ``Model.forward`` on CPU.  bf16 tensors are stored as uint16 bit
@@ -52,7 +55,12 @@ def _np(t: torch.Tensor):
     return t.numpy()
 
 
+ONLY = [p for p in os.environ.get("KV_GOLDEN_ONLY", "").split(",") if p]
+
+
 def save(name: str, meta: dict, **tensors):
+    if ONLY and not any(name.startswith(p) for p in ONLY):   # regenerate a subset only
+        return
     arrays = {}
     for k, v in tensors.items():
         if isinstance(v, torch.Tensor):
@@ -231,6 +239,44 @@ def main():
         save(f"paged_fp8_decode_{i}", shape, query=q, k_cache=kc, v_cache=vc, k_scale=k_scale, v_scale=v_scale,
              k_new=k_new, v_new=v_new, seq_lens=sl, block_table=bt, slot_mapping=slots,
              k_cache_after=kc_after, v_cache_after=vc_after, out=out)
+
+    # --- next rows: static_scaled_int8_quant (reference op, correctness mode), incl. a zero point,
+    #     a scale below MIN_SCALE and values that clamp
+    for i, (dims, dt, sc, zp) in enumerate([([16, 64], "FP32", 0.125, 0), ([4, 96], "BF16", 0.05, 3),
+                                            ([2, 8, 40], "FP16", 1e-9, -2), ([300], "FP32", 0.01, 0)]):
+        shape = {"dims": dims, "dtype": dt}
+        x, _, _ = gen_inputs("quantization", "static_scaled_int8_quant", shape, 1100 + i)
+        if i == 3:
+            x = x * 2.0                                            # a share of values beyond +-127 * scale
+        scale = torch.tensor([sc], dtype=torch.float32)
+        azp = torch.tensor([zp], dtype=torch.int32)
+        q = run_model("quantization", "static_scaled_int8_quant", shape, (x, scale, azp))
+        save(f"static_scaled_int8_quant_{i}", shape, x=x, scale=scale, azp=azp, q=q)
+
+    # --- next rows: kv_cache_write (reference op, performance mode as its config.json sets), shared and
+    #     per-batch positions
+    for i, (b, h, smax, w, d, mode, dt) in enumerate([(2, 2, 32, 1, 16, "shared", "FP32"),
+                                                     (3, 2, 40, 5, 32, "per_batch", "BF16"),
+                                                     (2, 1, 24, 8, 80, "per_batch", "FP16")]):
+        shape = {"batch_size": b, "num_kv_heads": h, "max_seq_len": smax, "write_seq_len": w, "head_dim": d,
+                 "position_mode": mode, "dtype": dt}
+        kc, vc, k, v, pos = gen_inputs("kv_cache", "kv_cache_write", shape, 1200 + i)
+        ko, vo = run_model("kv_cache", "kv_cache_write", shape, (kc, vc, k, v, pos), mode="performance")
+        save(f"kv_cache_write_{i}", shape, key_cache=kc, value_cache=vc, key=k, value=v, positions=pos,
+             key_out=ko, value_out=vo)
+
+    # --- next rows: flash_decoding_attention (reference op, correctness mode), single and multi query,
+    #     causal and not
+    for i, (b, sq, s, h, d, ch, causal, dt) in enumerate([(2, 1, 300, 2, 64, 64, False, "FP32"),
+                                                        (1, 4, 200, 2, 128, 64, True, "BF16"),
+                                                        (2, 3, 96, 3, 64, 32, False, "FP16"),
+                                                        (1, 32, 64, 1, 64, 16, True, "FP32")]):
+        shape = {"batch_size": b, "query_seq_len": sq, "kv_seq_len": s, "num_heads": h, "head_dim": d,
+                 "chunk_size": ch, "causal": causal, "dtype": dt}
+        qq, kk, vv = gen_inputs("attention", "flash_decoding_attention", shape, 1300 + i)
+        out, es, ml, po = run_model("attention", "flash_decoding_attention", shape, (qq, kk, vv))
+        save(f"flash_decoding_attention_{i}", shape, query=qq, key_cache=kk, value_cache=vv, out=out,
+             exp_sums=es, max_logits=ml, partial_out=po)
 
     (HERE / "VERSIONS.txt").write_text(f"torch {torch.__version__}\nnumpy {np.__version__}\n")
 

@@ -218,3 +218,75 @@ def test_kv_cache_update_large_and_int32():
     slots[::7] = -1
     out = _ops().paged_kv_cache_update(dev(to), dev(cache), dev(slots))
     np.testing.assert_array_equal(host(out), kv_cache.paged_kv_cache_update(to, cache, slots))
+
+
+@pytest.mark.parametrize("name", golden_names("kv_cache_write"))
+def test_kv_cache_write_golden(name):
+    meta, g = load_golden(name)
+    dt = {"FP32": torch.float32, "FP16": torch.float16, "BF16": torch.bfloat16}[meta["dtype"]]
+    ko, vo = _ops().kv_cache_write(dev(g["key_cache"][0], dt), dev(g["value_cache"][0], dt), dev(g["key"][0], dt),
+                                   dev(g["value"][0], dt), dev(g["positions"][0]))
+    np.testing.assert_array_equal(host(ko), g["key_out"][0].astype(np.float32) if dt != torch.float32 else g["key_out"][0])
+    np.testing.assert_array_equal(host(vo), g["value_out"][0].astype(np.float32) if dt != torch.float32 else g["value_out"][0])
+
+
+@pytest.mark.parametrize("per_batch", [False, True])
+def test_kv_cache_write_large_and_negative_positions(per_batch):
+    """A prefill-sized write (16 heads x 512 rows) with int32 positions, negative ones counting
+    from the end as torch indexing does; inputs stay untouched."""
+    rng = seeded(31)
+    b, h, s, w, d = 4, 16, 2048, 512, 128
+    kc = rng.standard_normal((b, h, s, d)).astype(np.float32)
+    vc = rng.standard_normal((b, h, s, d)).astype(np.float32)
+    k = rng.standard_normal((b, h, w, d)).astype(np.float32)
+    v = rng.standard_normal((b, h, w, d)).astype(np.float32)
+    if per_batch:
+        pos = np.stack([np.arange(w) + 100 * i for i in range(b)]).astype(np.int32)
+        pos[:, -3:] -= s                                      # the last three as negative indices
+    else:
+        pos = (np.arange(w) + 1000).astype(np.int32)
+        pos[:5] = pos[:5] - s
+    bf = torch.bfloat16
+    kct, vct = dev(kc, bf), dev(vc, bf)
+    keep = kct.clone()
+    ko, vo = _ops().kv_cache_write(kct, vct, dev(k, bf), dev(v, bf), dev(pos))
+    rk, rv = kv_cache.kv_cache_write(host(kct), host(vct), host(dev(k, bf)), host(dev(v, bf)), pos)
+    np.testing.assert_array_equal(host(ko), rk)
+    np.testing.assert_array_equal(host(vo), rv)
+    assert torch.equal(kct, keep)
+
+
+@pytest.mark.parametrize("name", golden_names("flash_decoding_attention"))
+def test_flash_decoding_golden(name):
+    meta, g = load_golden(name)
+    dt = {"FP32": torch.float32, "FP16": torch.float16, "BF16": torch.bfloat16}[meta["dtype"]]
+    out, es, ml, po = _ops().flash_decoding_attention(dev(g["query"][0], dt), dev(g["key_cache"][0], dt),
+                                                      dev(g["value_cache"][0], dt), meta["chunk_size"], meta["causal"])
+    tight = dt == torch.float32
+    tol = 5e-4 if tight else (1e-2 if dt == torch.float16 else 1.5e-2)   # the reference's config.json tolerances
+    for got, ref in ((out, g["out"][0]), (po, g["partial_out"][0]), (es, g["exp_sums"][0])):
+        np.testing.assert_allclose(host(got), ref.astype(np.float32), rtol=tol, atol=tol)
+    ref_ml = g["max_logits"][0].astype(np.float32)
+    got_ml = host(ml)
+    assert np.array_equal(np.isneginf(got_ml), np.isneginf(ref_ml))
+    fin = np.isfinite(ref_ml)
+    np.testing.assert_allclose(got_ml[fin], ref_ml[fin], rtol=tol, atol=tol)
+
+
+@pytest.mark.parametrize("dt", ["FP32", "BF16"])
+@pytest.mark.parametrize("b,sq,s,h,d,chunk,causal", [(4, 1, 2048, 16, 128, 256, False), (2, 16, 2048, 8, 64, 256, True),
+                                                     (1, 64, 1024, 4, 128, 128, True), (2, 8, 520, 3, 64, 64, False)])
+def test_flash_decoding_shapes(dt, b, sq, s, h, d, chunk, causal):
+    rng = seeded(b * 100 + sq)
+    q = rng.standard_normal((b, h, sq, d)).astype(np.float32)
+    k = rng.standard_normal((b, h, s, d)).astype(np.float32)
+    v = rng.standard_normal((b, h, s, d)).astype(np.float32)
+    tdt = TORCH_DT[dt]
+    qt, kt, vt = dev(q, tdt), dev(k, tdt), dev(v, tdt)
+    out, es, ml, po = _ops().flash_decoding_attention(qt, kt, vt, chunk, causal)
+    r_out, r_es, r_ml, r_po = attention.flash_decoding_attention(host(qt), host(kt), host(vt), chunk, causal, d ** -0.5)
+    tight = dt == "FP32"
+    _close(host(out), r_out, tight)
+    _close(host(po), r_po, tight)
+    np.testing.assert_allclose(host(es), r_es, rtol=1e-5 if tight else 1e-2, atol=1e-5 if tight else 1e-2)
+    assert np.array_equal(np.isneginf(host(ml)), np.isneginf(r_ml))

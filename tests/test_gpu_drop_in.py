@@ -139,3 +139,33 @@ def test_baseline_packages_model_vs_modelnew(op, shape):
     if op == "paged_fp8_decode":      # the fused write must leave the caches identical
         assert torch.equal(ins[1].view(torch.uint8), ins2[1].view(torch.uint8))
         assert torch.equal(ins[2].view(torch.uint8), ins2[2].view(torch.uint8))
+
+
+@pytest.mark.parametrize("name", golden_names("static_scaled_int8_quant"))
+def test_static_scaled_int8_quant(name):
+    meta, g = load_golden(name)
+    q = modelnew("static_scaled_int8_quant", meta)(_as_dev(*g["x"]), dev(g["scale"][0]), dev(g["azp"][0]))
+    assert q.dtype == torch.int8
+    _check(q, g["q"][0], "int8", {"max_abs_diff": 0})      # config.json allows 1; the kernel is exact
+
+
+@pytest.mark.parametrize("name", golden_names("kv_cache_write"))
+def test_kv_cache_write(name):
+    meta, g = load_golden(name)
+    ins = [_as_dev(*g[k]) for k in ("key_cache", "value_cache", "key", "value", "positions")]
+    ko, vo = modelnew("kv_cache_write", meta)(*ins)
+    np.testing.assert_array_equal(host(ko), g["key_out"][0].astype(np.float32))
+    np.testing.assert_array_equal(host(vo), g["value_out"][0].astype(np.float32))
+
+
+@pytest.mark.parametrize("name", golden_names("flash_decoding_attention"))
+def test_flash_decoding_attention(name):
+    meta, g = load_golden(name)
+    outs = modelnew("flash_decoding_attention", meta)(*(_as_dev(*g[k]) for k in ("query", "key_cache", "value_cache")))
+    tol = TOL[meta["dtype"]]
+    for got, key in zip(outs, ("out", "exp_sums", "max_logits", "partial_out")):
+        assert got.dtype == TORCH_DT[meta["dtype"]]
+        ref = g[key][0].astype(np.float32)
+        fin = np.isfinite(ref)
+        assert np.array_equal(np.isfinite(host(got)), fin)
+        np.testing.assert_allclose(host(got)[fin], ref[fin], rtol=tol["rtol"], atol=tol["atol"])

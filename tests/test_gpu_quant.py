@@ -158,3 +158,28 @@ def test_dynamic_quant_ties_and_tiny_values():
     rq, rs, _ = quant.dynamic_scaled_int8_quant(x, "FP32")
     np.testing.assert_array_equal(host(s), rs)
     np.testing.assert_array_equal(host(q), rq)
+
+
+@pytest.mark.parametrize("name", golden_names("static_scaled_int8_quant"))
+def test_static_quant_golden(name):
+    meta, g = load_golden(name)
+    x, xdt = g["x"]
+    q = _ops().static_scaled_int8_quant(dev(x, TORCH_DT[xdt]), dev(g["scale"][0]), dev(g["azp"][0]))
+    np.testing.assert_array_equal(host(q), g["q"][0])
+
+
+@pytest.mark.parametrize("dt", ["FP32", "FP16", "BF16"])
+@pytest.mark.parametrize("dims,scale,azp", [([512, 4096], 0.125, 0), ([7, 13], 0.02, 5), ([3, 1000], 1e-9, -7),
+                                             ([2, 16, 1024], 3.0, 127), ([8191], 0.05, -128)])
+def test_static_quant_shapes(dt, dims, scale, azp):
+    """Odd sizes (scalar tail), a zero point, a scale below MIN_SCALE (clamped), ties and values far
+    beyond +-127 * scale, against the oracle bit for bit."""
+    rng = seeded(len(dims) * 5 + dims[0])
+    x = (rng.standard_normal(dims) * 4).astype(np.float32)
+    x.reshape(-1)[::97] = (np.arange(x.size)[::97] % 50 - 25 + 0.5) * np.float32(scale)   # exact ties
+    xt = dev(x, TORCH_DT[dt])
+    x = host(xt).astype(np.float32)
+    s = dev(np.array([scale], np.float32))
+    z = dev(np.array([azp], np.int32))
+    q = _ops().static_scaled_int8_quant(xt, s, z)
+    np.testing.assert_array_equal(host(q), quant.static_scaled_int8_quant(x, scale, azp))

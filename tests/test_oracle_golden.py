@@ -115,3 +115,36 @@ def test_paged_fp8_decode(name):
     out = attention.paged_fp8_decode(g["query"][0], kc, vc, g["k_scale"][0], g["v_scale"][0], g["seq_lens"][0],
                                      g["block_table"][0], meta["head_dim"] ** -0.5)
     np.testing.assert_allclose(out, g["out"][0], rtol=1e-5, atol=1e-5)
+
+
+@pytest.mark.parametrize("name", golden_names("static_scaled_int8_quant"))
+def test_static_scaled_int8_quant(name):
+    meta, g = load_golden(name)
+    q = quant.static_scaled_int8_quant(g["x"][0], g["scale"][0], g["azp"][0])
+    np.testing.assert_array_equal(q, g["q"][0])              # bit-exact codes
+
+
+@pytest.mark.parametrize("name", golden_names("kv_cache_write"))
+def test_kv_cache_write(name):
+    meta, g = load_golden(name)
+    ko, vo = kv_cache.kv_cache_write(g["key_cache"][0], g["value_cache"][0], g["key"][0], g["value"][0],
+                                     g["positions"][0])
+    np.testing.assert_array_equal(ko, g["key_out"][0])
+    np.testing.assert_array_equal(vo, g["value_out"][0])
+
+
+@pytest.mark.parametrize("name", golden_names("flash_decoding_attention"))
+def test_flash_decoding_attention(name):
+    meta, g = load_golden(name)
+    d = meta["head_dim"]
+    out, es, ml, po = attention.flash_decoding_attention(g["query"][0], g["key_cache"][0], g["value_cache"][0],
+                                                         meta["chunk_size"], meta["causal"], d ** -0.5)
+    # the reference computes in float32 and rounds to the output dtype; the oracle in float64
+    tol = {"FP32": 2e-5, "FP16": 2e-3, "BF16": 1.6e-2}[meta["dtype"]]
+    np.testing.assert_allclose(out, g["out"][0], rtol=tol, atol=tol)
+    np.testing.assert_allclose(po, g["partial_out"][0], rtol=tol, atol=tol)
+    np.testing.assert_allclose(es, g["exp_sums"][0], rtol=tol, atol=tol)
+    ref_ml = g["max_logits"][0]
+    assert np.array_equal(np.isinf(ml), np.isinf(ref_ml))      # fully masked chunks: -inf
+    fin = np.isfinite(ref_ml)
+    np.testing.assert_allclose(ml[fin], ref_ml[fin], rtol=tol, atol=tol)
