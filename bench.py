@@ -318,6 +318,18 @@ def gemm_benchmarks(torch, ops, hbm_peak):
             entry["frac_of_nominal_4500_tops"] = round(entry["tops"] / 4500.0, 4)
         res.append(entry)
         del a, b
+    # the gate+up projection (N = 57344 = 2 x 28672) with SwiGLU fused into the epilogue, against
+    # the same GEMM storing both halves (the activation would be a further pass over them)
+    for M in (4096, 16):
+        a, b, sa, sb, bias = make_c3_inputs(torch, dev, 31 + M, M, N=2 * N)
+        us_plain = time_fn(torch, lambda: ops.w8a8_scaled_mm(a, b, sa, sb, bias), 10 if M == 4096 else 30)
+        us_act = time_fn(torch, lambda: ops.w8a8_scaled_mm_act(a, b, sa, sb, bias, "swiglu"), 10 if M == 4096 else 30)
+        ops_ = 2 * M * 2 * N * K
+        res.append({"workload": f"W8A8 gate+up GEMM + SwiGLU, M={M}, N={2 * N} -> {N} outputs, K={K}, bf16 out",
+                    "kernel": "w8a8_gemm_kernel, gated epilogue (act 1)", "us_per_call": round(us_act, 2),
+                    "tops": round(ops_ / us_act / 1e6, 1), "us_same_gemm_storing_both_halves": round(us_plain, 2),
+                    "output_bytes": M * N * 2, "output_bytes_unfused": M * 2 * N * 2})
+        del a, b
     return res
 
 
@@ -365,7 +377,18 @@ def multi_gpu_benchmarks(torch, ops, dist, world: int, rank: int, hbm_peak: floa
                 "bytes_received_per_rank": recv,
                 "nvlink_gbs_per_rank_fused": round(recv / us_fused / 1e3, 1),
                 "note": "fused = kvb_w8a8_scaled_mm_allgather (peer stores from the epilogue into symmetric memory)"})
-    del tp, gathered, a, b
+    del tp, gathered, b
+    # gate+up with SwiGLU in the epilogue: each rank gathers half the bytes
+    ib = torch.randint(-127, 128, (nw, K), generator=gr, device=dev, dtype=torch.int8)   # interleaved shard
+    tpa = TPW8A8(dist.group.WORLD, M, ib, sb, bias, act="swiglu")
+    us_act = timed(lambda: tpa(a, sa), 10)
+    recv_act = (world - 1) * M * (nw // 2) * 2
+    res.append({"workload": f"TP W8A8 gate+up GEMM + SwiGLU, M={M}, N={N} (x{world} shards of {nw}) -> {N // 2} "
+                            "outputs, K={K}, bf16 out".replace("{K}", str(K)),
+                "us_fused_gemm_swiglu_allgather": round(us_act, 1), "bytes_received_per_rank": recv_act,
+                "nvlink_gbs_per_rank": round(recv_act / us_act / 1e3, 1),
+                "note": "kvb_w8a8_scaled_mm_act_allgather: activation in the epilogue, then peer stores"})
+    del tpa, ib, a
     torch.cuda.empty_cache()
     # batch-sharded decode, batch 512 balanced by context length
     gl = torch.Generator(device="cpu").manual_seed(77)

@@ -176,6 +176,37 @@ KVB_API int kvb_w8a8_scaled_mm_allgather(const int8_t* a, const int8_t* b_shard,
                                          int64_t M, int64_t N_shard, int64_t K, void* const* out_ptrs, int world,
                                          int rank, int64_t ldo, int out_dtype, void* stream);
 
+/*
+ * W8A8 GEMM with a gated-activation epilogue: the gate+up projection of an MLP followed by
+ * SwiGLU in one kernel (SURVEY "next" row: operators/activation/swiglu/swiglu.py:24-28 and
+ * operators/activation/mul_and_silu/mul_and_silu.py:24-29 applied to this GEMM's output).
+ * b_nk [N, K] holds the two operand weights with their rows interleaved in blocks of 128:
+ * rows [256 j, 256 j + 128) are rows [128 j, 128 j + 128) of the first operand's weight and
+ * rows [256 j + 128, 256 j + 256) the same rows of the second's; b_scales and bias [N] follow
+ * the same order.  With f = (acc * a_scales[m]) * b_scales[n] + bias[n] rounded to out_dtype
+ * (exactly what kvb_w8a8_scaled_mm would store), output column c of row m is
+ *   act 1: silu(f_first) * f_second      (SwiGLU: gate first)
+ *   act 2: f_first * silu(f_second)      (mul-and-silu: value first)
+ * in float32 (silu(x) = x * rcp(1 + e^-x) with the fast exponential: within a few float32
+ * ulps), rounded to out_dtype.  out: [M, N / 2] (pitch ldo).
+ * N must be a multiple of 256; out_dtype KVB_BF16, KVB_F16 or KVB_F32.
+ */
+KVB_API int kvb_w8a8_scaled_mm_act(const int8_t* a, const int8_t* b_nk, const float* a_scales, const float* b_scales,
+                                   const void* bias, int bias_dtype, int64_t M, int64_t N, int64_t K, int act,
+                                   void* out, int out_dtype, int64_t ldo, void* stream);
+
+/*
+ * kvb_w8a8_scaled_mm_act, column-sharded over `world` ranks with the all-gather fused into the
+ * epilogue as in kvb_w8a8_scaled_mm_allgather: rank `rank` holds the interleaved rows of its
+ * N_shard / 2 output columns (N_shard a multiple of 256) and stores them at columns
+ * rank * N_shard / 2 of every rank's [M, ldo] buffer (ldo >= world * N_shard / 2).  The
+ * gathered bytes are half those of gathering the gate+up output.
+ */
+KVB_API int kvb_w8a8_scaled_mm_act_allgather(const int8_t* a, const int8_t* b_shard, const float* a_scales,
+                                             const float* b_scales_shard, const void* bias_shard, int bias_dtype,
+                                             int64_t M, int64_t N_shard, int64_t K, int act, void* const* out_ptrs,
+                                             int world, int rank, int64_t ldo, int out_dtype, void* stream);
+
 /* ---------------------------------------------------------------- paged KV-cache writes */
 
 /*

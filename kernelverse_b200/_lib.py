@@ -33,6 +33,8 @@ SIGNATURES = {
     "kvb_w8a8_workspace_size": (_SZ, [_I64, _I64, _I64, _I, _I]),
     "kvb_w8a8_scaled_mm": (_I, [_P, _P, _I, _P, _P, _P, _I, _P, _P, _I64, _I64, _I64, _P, _I, _I64, _P, _SZ, _P]),
     "kvb_w8a8_scaled_mm_allgather": (_I, [_P, _P, _P, _P, _P, _I, _I64, _I64, _I64, _P, _I, _I, _I64, _I, _P]),
+    "kvb_w8a8_scaled_mm_act": (_I, [_P, _P, _P, _P, _P, _I, _I64, _I64, _I64, _I, _P, _I, _I64, _P]),
+    "kvb_w8a8_scaled_mm_act_allgather": (_I, [_P, _P, _P, _P, _P, _I, _I64, _I64, _I64, _I, _P, _I, _I, _I64, _I, _P]),
     "kvb_paged_kv_cache_update": (_I, [_P, _P, _P, _P, _I, _I, _I64, _I64, _I64, _P]),
     "kvb_paged_fp8_kv_write": (_I, [_P, _I, _P, _P, _I, _P, _I64, _I64, _I, _I, _P]),
     "kvb_kv_cache_write": (_I, [_P, _P, _P, _P, _P, _P, _P, _I, _I, _I, _I64, _I64, _I64, _I64, _I64, _P]),

@@ -8,14 +8,18 @@
 // (operators/gemm/int8_scaled_mm_azp/int8_scaled_mm_azp.py:61-85, with its dequantise-then-float
 // matmul replaced by the exact integer form) and the BASELINE third config (azp off, bias on).
 //
-// Structure: a persistent kernel, one CTA per SM, 128 x BN output tiles (BN = 256 or 128).
-//   warp 0: TMA producer -- A [128 x 128 B] and B [BN x 128 B] K-major boxes with 128-byte
-//           swizzle into a kStages-deep shared-memory ring (mbarrier complete_tx);
+// Structure: a persistent, warp-specialised kernel; 128 x BN tiles on one SM, or 256 x BN tiles
+// on a CTA pair (cluster of 2, tcgen05 cta_group::2: each CTA loads its 128 rows of A and BN/2
+// rows of B and the pair leader issues the MMAs for both).
+//   warp 0: TMA producer -- A [128 x 128 B] and B [rows x 128 B] K-major boxes with 128-byte
+//           swizzle into a STAGES-deep shared-memory ring (mbarrier complete_tx);
 //   warp 1: allocates 2 x BN TMEM columns (double-buffered accumulator) and one lane issues
-//           4 x tcgen05.mma (M=128, N=BN, K=32) per stage, committing the stage back to the
-//           producer and each finished tile to the epilogue;
-//   warps 2-5: epilogue -- tcgen05.ld 32 columns at a time from their TMEM lane quarter,
-//           scale / bias / convert, store; then release the accumulator buffer.
+//           4 x tcgen05.mma (K = 32 each) per stage, committing the stage back to the producer
+//           and each finished tile to the epilogue;
+//   warps 2-9: epilogue -- two warps per TMEM lane quarter, each taking every other 128-byte
+//           output chunk: tcgen05.ld 32 columns at a time, scale / bias (optionally a gated
+//           activation) / convert, store (direct 16-byte stores, or TMA tensor stores to every
+//           rank's buffer for the fused all-gather); then release the accumulator buffer.
 // Every mbarrier wait is bounded (kvb_async.cuh); on a timeout the roles drain and the CTA
 // frees its TMEM before exiting.
 #include <cuda.h>
@@ -33,7 +37,8 @@ namespace {
 constexpr int kBM = 128;
 constexpr int kBK = 128;          // bytes of K per stage = one 128-byte swizzle row
 constexpr int kUmmaK = 32;        // K of one kind::i8 MMA
-constexpr int kThreads = 192;     // 6 warps
+constexpr int kEpiWarps = 8;      // two epilogue warps per TMEM lane quarter
+constexpr int kThreads = 64 + 32 * kEpiWarps;   // producer, MMA issuer, epilogue warps
 
 struct GemmArgs {
   int M, N, K;
@@ -55,6 +60,12 @@ struct GemmArgs {
   void* outs[8];
   int tma_store;         // 1: full 128-byte output chunks go through TMA tensor stores (omaps)
   int ndest;             // number of valid output maps (destinations) for the TMA-store path
+  // Gated activation epilogue (act != 0): B's rows are interleaved in blocks of BN/2 = 128, so
+  // accumulator columns [0, 128) of a 256-column tile are the first operand and [128, 256) the
+  // second of the same 128 output columns; out = silu(first) * second (act 1, SwiGLU) or
+  // first * silu(second) (act 2, mul-and-silu), each operand rounded to the output type first.
+  int act;
+  int n_out;             // output columns: N, or N / 2 with act
 };
 
 // Output tensor maps, one per destination buffer (own buffer first), for TMA stores of
@@ -243,17 +254,11 @@ __device__ __forceinline__ ColVals load_cols(const GemmArgs& g, int n0, int lane
   return c;
 }
 
-// Scale / bias / convert 32 accumulator columns (operands in c) into output words: 32 words for
-// 32-bit outputs, 16 packed pairs for 16-bit outputs.  All 32 lanes must be converged.
-__device__ __forceinline__ void epilogue32(const GemmArgs& g, const uint32_t (&r)[32], const ColVals& c, float sa,
-                                           int32_t rs, uint32_t* w) {
-  if (g.out_dtype == KVB_I32) {
-#pragma unroll
-    for (int j = 0; j < 32; ++j) w[j] = r[j];
-    return;
-  }
+// Scale / bias 32 accumulator columns (operands in c) into float32 values.  All 32 lanes must
+// be converged.
+__device__ __forceinline__ void epi_values(const GemmArgs& g, const uint32_t (&r)[32], const ColVals& c, float sa,
+                                           int32_t rs, float (&f)[32]) {
   constexpr unsigned kAll = 0xffffffffu;
-  float f[32];
 #pragma unroll
   for (int j = 0; j < 32; ++j) {
     int32_t acc = (int32_t)r[j];
@@ -263,6 +268,10 @@ __device__ __forceinline__ void epilogue32(const GemmArgs& g, const uint32_t (&r
     if (g.bias) y = __fadd_rn(y, __shfl_sync(kAll, c.bias, j));
     f[j] = y;
   }
+}
+
+// Output words of 32 float32 values: 32 words for float32 outputs, 16 packed pairs for 16-bit.
+__device__ __forceinline__ void pack_out(const GemmArgs& g, const float (&f)[32], uint32_t* w) {
   if (g.out_dtype == KVB_F32) {
 #pragma unroll
     for (int j = 0; j < 32; ++j) w[j] = __float_as_uint(f[j]);
@@ -277,6 +286,49 @@ __device__ __forceinline__ void epilogue32(const GemmArgs& g, const uint32_t (&r
         w[j] = *reinterpret_cast<uint32_t*>(&h);
       }
     }
+  }
+}
+
+// Scale / bias / convert 32 accumulator columns (operands in c) into output words.
+__device__ __forceinline__ void epilogue32(const GemmArgs& g, const uint32_t (&r)[32], const ColVals& c, float sa,
+                                           int32_t rs, uint32_t* w) {
+  if (g.out_dtype == KVB_I32) {
+#pragma unroll
+    for (int j = 0; j < 32; ++j) w[j] = r[j];
+    return;
+  }
+  float f[32];
+  epi_values(g, r, c, sa, rs, f);
+  pack_out(g, f, w);
+}
+
+// The value the unfused GEMM would have stored, back in float32.
+__device__ __forceinline__ float round_out(const GemmArgs& g, float x) {
+  if (g.out_dtype == KVB_BF16) return __bfloat162float(__float2bfloat16_rn(x));
+  if (g.out_dtype == KVB_F16) return __half2float(__float2half_rn(x));
+  return x;
+}
+// silu(x) = x / (1 + e^-x) in float32 from the fast exponential and the correctly rounded
+// reciprocal (a few float32 ulps; the result is then rounded to the 16-bit output type).
+__device__ __forceinline__ float silu(float x) { return __fmul_rn(x, __frcp_rn(__fadd_rn(1.0f, __expf(-x)))); }
+
+// Scale and bias of one column per lane (gated epilogue, where there are no zero points).
+__device__ __forceinline__ float2 load_sb_bias(const GemmArgs& g, int n0, int lane) {
+  const int n = min(n0 + lane, g.N - 1);
+  return make_float2(g.sb[n], g.bias ? load_bias(g.bias, g.bias_dtype, n) : 0.0f);
+}
+__device__ __forceinline__ float2 pick4(const float2 (&v)[4], int k) {   // v[k] without local memory
+  return k == 0 ? v[0] : k == 1 ? v[1] : k == 2 ? v[2] : v[3];
+}
+// Gated-epilogue values of 32 columns: scale / bias with the per-lane column operands c.
+__device__ __forceinline__ void act_values(const GemmArgs& g, const uint32_t (&r)[32], float2 c, float sa,
+                                           float (&f)[32]) {
+  constexpr unsigned kAll = 0xffffffffu;
+#pragma unroll
+  for (int j = 0; j < 32; ++j) {
+    float y = __fmul_rn(__fmul_rn((float)(int32_t)r[j], sa), __shfl_sync(kAll, c.x, j));
+    if (g.bias) y = __fadd_rn(y, __shfl_sync(kAll, c.y, j));
+    f[j] = y;
   }
 }
 
@@ -317,7 +369,7 @@ __global__ void __launch_bounds__(kThreads, 1) w8a8_gemm_kernel(const __grid_con
     }
     for (int j = 0; j < 2; ++j) {
       mbar_init(&tmem_full[j], 1);
-      mbar_init(&tmem_empty[j], k2Sm ? 8 : 4);   // every epilogue warp of the pair releases the buffer
+      mbar_init(&tmem_empty[j], k2Sm ? 2 * kEpiWarps : kEpiWarps);   // every epilogue warp of the pair releases it
     }
     mbar_init(&mma_done, 1);
     fence_mbar_init();
@@ -418,13 +470,15 @@ __global__ void __launch_bounds__(kThreads, 1) w8a8_gemm_kernel(const __grid_con
       mbar_wait_bounded(&mma_done, 0);   // the leader's MMAs also write this CTA's TMEM
     }
   } else {
-    // ------------------------------------------------------------ epilogue (warps 2..5)
-    // Each warp owns 32 TMEM lanes (= 32 output rows) and two 4 KB staging buffers.
+    // ------------------------------------------------------------ epilogue (warps 2..9)
+    // Each warp owns 32 TMEM lanes (= 32 output rows: quarter warp % 4) and every other 128-byte
+    // column chunk of them (its half), and one 4 KB staging buffer.
     const int q = warp & 3;                 // TMEM lane quarter this warp may access
+    const int ew = warp - 2;                // epilogue warp index
+    const int half = ew >> 2;               // which alternate chunks
     const int esize = (g.out_dtype == KVB_I32 || g.out_dtype == KVB_F32) ? 4 : 2;
     const int CW = 128 / esize;             // columns per 128-byte chunk
-    uint8_t* stage_base = smem + (size_t)STAGES * kStageBytes + (size_t)q * 8192;
-    int sbuf = 0;
+    uint8_t* stage_buf = smem + (size_t)STAGES * kStageBytes + (size_t)ew * 4096;
     uint32_t local = 0;
     for (int t = tile0; t < g.tiles; t += tstride, ++local) {
       const uint32_t ab = local & 1u, v = local >> 1;
@@ -436,35 +490,71 @@ __global__ void __launch_bounds__(kThreads, 1) w8a8_gemm_kernel(const __grid_con
       const bool mrow = m < g.M;
       const float sa = (mrow && g.sa) ? g.sa[m] : 0.0f;   // no scales in int32-accumulator mode
       const int32_t rs = (g.azp && mrow) ? g.rowsum[m] : 0;
-      ColVals cv0 = load_cols(g, nb * BN, lane);
-      ColVals cv1 = esize == 2 && 32 < BN ? load_cols(g, nb * BN + 32, lane) : ColVals{0.0f, 0.0f, 0.0f, 0.0f};
+      const int OC = g.act ? BN / 2 : BN;   // output columns of a tile
+      const uint32_t tm = tmem_base + ((uint32_t)(q * 32) << 16) + ab * BN;   // this warp's accumulator
+      ColVals cv0{0.0f, 0.0f, 0.0f, 0.0f}, cv1{0.0f, 0.0f, 0.0f, 0.0f};
+      float2 af[4], as[4];                  // gated: the 4 x 32 columns of each operand (OC = 128)
+      if (g.act) {
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+          af[k] = load_sb_bias(g, nb * BN + 32 * k, lane);
+          as[k] = load_sb_bias(g, nb * BN + OC + 32 * k, lane);
+        }
+      } else {
+        cv0 = load_cols(g, nb * BN + half * CW, lane);
+        if (esize == 2 && half * CW + 32 < BN) cv1 = load_cols(g, nb * BN + half * CW + 32, lane);
+      }
       if (!mbar_wait_bounded(&tmem_full[ab], v & 1u)) break;
       tc_fence_after();
 #pragma unroll 1
-      for (int c0 = 0; c0 < BN; c0 += CW) {
-        const int n0 = nb * BN + c0;
-        const ColVals cur0 = cv0, cur1 = cv1;
-        if (c0 + CW < BN) {                 // prefetch the next chunk's column operands
-          cv0 = load_cols(g, n0 + CW, lane);
-          if (esize == 2 && c0 + CW + 32 < BN) cv1 = load_cols(g, n0 + CW + 32, lane);
-        }
+      for (int c0 = half * CW; c0 < OC; c0 += 2 * CW) {
+        const int o0 = nb * OC + c0;        // first output column of the chunk
         uint32_t w[32];
-        uint32_t r[32];
-        __syncwarp();                       // tcgen05.ld is .sync.aligned: reconverge first
-        tmem_ld32(tmem_base + ((uint32_t)(q * 32) << 16) + ab * BN + c0, r);
-        epilogue32(g, r, cur0, sa, rs, w);
-        if (esize == 2 && c0 + 32 < BN) {
-          __syncwarp();
-          tmem_ld32(tmem_base + ((uint32_t)(q * 32) << 16) + ab * BN + c0 + 32, r);
-          epilogue32(g, r, cur1, sa, rs, w + 16);
+        if (g.act) {
+          // gated: 32 output columns at a time from accumulator columns c and OC + c
+#pragma unroll
+          for (int h = 0; h < 2; ++h) {
+            if (h * 32 >= CW) break;
+            const int c = c0 + 32 * h;
+            uint32_t r[32];
+            float fa[32], fb[32];
+            __syncwarp();                   // tcgen05.ld is .sync.aligned: reconverge first
+            tmem_ld32(tm + c, r);
+            act_values(g, r, pick4(af, c >> 5), sa, fa);
+            __syncwarp();
+            tmem_ld32(tm + OC + c, r);
+            act_values(g, r, pick4(as, c >> 5), sa, fb);
+#pragma unroll
+            for (int j = 0; j < 32; ++j) {
+              const float x = round_out(g, fa[j]), y = round_out(g, fb[j]);
+              fa[j] = g.act == 1 ? __fmul_rn(silu(x), y) : __fmul_rn(x, silu(y));
+            }
+            pack_out(g, fa, w + 16 * h);    // h > 0 only for 16-bit outputs (16 words per 32 columns)
+          }
+        } else {
+          const int n0 = nb * BN + c0;
+          const ColVals cur0 = cv0, cur1 = cv1;
+          if (c0 + 2 * CW < BN) {           // prefetch this warp's next chunk's column operands
+            cv0 = load_cols(g, n0 + 2 * CW, lane);
+            if (esize == 2 && c0 + 2 * CW + 32 < BN) cv1 = load_cols(g, n0 + 2 * CW + 32, lane);
+          }
+          uint32_t r[32];
+          __syncwarp();                     // tcgen05.ld is .sync.aligned: reconverge first
+          tmem_ld32(tm + c0, r);
+          epilogue32(g, r, cur0, sa, rs, w);
+          if (esize == 2 && c0 + 32 < BN) {
+            __syncwarp();
+            tmem_ld32(tm + c0 + 32, r);
+            epilogue32(g, r, cur1, sa, rs, w + 16);
+          }
         }
-        if (n0 >= g.N) continue;
-        const bool full_chunk = c0 + CW <= BN && n0 + CW <= g.N;
+        if (o0 >= g.n_out) continue;
+        const bool full_chunk = c0 + CW <= OC && o0 + CW <= g.n_out;
         if (kTmaStore && g.tma_store && full_chunk) {
           // Stage the warp's [32 x 128 B] chunk with the 128-byte swizzle, then one TMA store per
           // destination; rows past M are clipped by the tensor map.
-          uint8_t* buf = stage_base + sbuf * 4096;
-          if (lane == 0) asm volatile("cp.async.bulk.wait_group.read 1;" ::: "memory");   // buf is free again
+          uint8_t* buf = stage_buf;
+          if (lane == 0) asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory");   // buf is free again
           __syncwarp();
 #pragma unroll
           for (int j = 0; j < 8; ++j)
@@ -474,19 +564,18 @@ __global__ void __launch_bounds__(kThreads, 1) w8a8_gemm_kernel(const __grid_con
           __syncwarp();
           if (lane == 0) {
             for (int d = 0; d < g.ndest; ++d)
-              tma_store_2d(&om.m[d], buf, (int)(g.col_off + n0), row0);
+              tma_store_2d(&om.m[d], buf, (int)(g.col_off + o0), row0);
             asm volatile("cp.async.bulk.commit_group;" ::: "memory");
           }
-          sbuf ^= 1;
           continue;
         }
         if (!mrow) continue;
         // Direct stores of the valid columns to every destination: 16-byte vectors for a full,
         // aligned chunk, element stores at a ragged edge.
-        const int ncols = min(min(CW, BN - c0), g.N - n0);
+        const int ncols = min(min(CW, OC - c0), g.n_out - o0);
         for (int d = g.nout ? 0 : -1; d < g.nout; ++d) {
-          uint8_t* ob = esize == 4 ? reinterpret_cast<uint8_t*>(dst_ptr<uint32_t>(g, d, m, n0))
-                                   : reinterpret_cast<uint8_t*>(dst_ptr<uint16_t>(g, d, m, n0));
+          uint8_t* ob = esize == 4 ? reinterpret_cast<uint8_t*>(dst_ptr<uint32_t>(g, d, m, o0))
+                                   : reinterpret_cast<uint8_t*>(dst_ptr<uint16_t>(g, d, m, o0));
           if (ncols == CW && (reinterpret_cast<uintptr_t>(ob) & 15) == 0) {
 #pragma unroll
             for (int j = 0; j < 8; ++j)
@@ -494,12 +583,12 @@ __global__ void __launch_bounds__(kThreads, 1) w8a8_gemm_kernel(const __grid_con
             continue;
           }
           if (esize == 4) {
-            uint32_t* o = dst_ptr<uint32_t>(g, d, m, n0);
+            uint32_t* o = dst_ptr<uint32_t>(g, d, m, o0);
 #pragma unroll
             for (int j = 0; j < 32; ++j)
               if (j < ncols) o[j] = w[j];
           } else {
-            uint16_t* o = dst_ptr<uint16_t>(g, d, m, n0);
+            uint16_t* o = dst_ptr<uint16_t>(g, d, m, o0);
 #pragma unroll
             for (int j = 0; j < 64; ++j)
               if (j < ncols) o[j] = (uint16_t)(w[j >> 1] >> ((j & 1) * 16));
@@ -650,7 +739,7 @@ int launch_gemm(const int8_t* a, const int8_t* b_nk, GemmArgs& g, void* const* d
     rc = make_out_map(&om.m[d], dests[d], g.out_dtype, g.M, map_cols, g.ldo);
     if (rc) return rc;
   }
-  constexpr size_t kStaging = kTmaStore ? 4 * 8192 : 0;   // 4 epilogue warps x 2 x [32 rows x 128 B]
+  constexpr size_t kStaging = kTmaStore ? kEpiWarps * 4096 : 0;   // one [32 rows x 128 B] buffer per epilogue warp
   const size_t smem = (size_t)STAGES * (kBM * kBK + kBRows * kBK) + kStaging + 1024;
   auto kern = w8a8_gemm_kernel<BN, STAGES, kTmaStore, k2Sm>;
   static int set_dev = -1;
@@ -723,6 +812,7 @@ extern "C" int kvb_w8a8_scaled_mm_allgather(const int8_t* a, const int8_t* b_sha
   g.M = (int)M; g.N = (int)N_shard; g.K = (int)K;
   g.sa = a_scales; g.sb = b_scales_shard; g.bias = bias_shard; g.bias_dtype = bias_dtype;
   g.out = out_ptrs[rank]; g.ldo = ldo; g.out_dtype = out_dtype;
+  g.n_out = g.N;
   g.nout = world;
   g.col_off = (int64_t)rank * N_shard;
   void* dests[8];
@@ -777,6 +867,7 @@ extern "C" int kvb_w8a8_scaled_mm(const int8_t* a, const int8_t* b, int b_layout
   g.M = (int)M; g.N = (int)N; g.K = (int)K;
   g.sa = a_scales; g.sb = b_scales; g.bias = bias; g.bias_dtype = bias_dtype;
   g.azp = azp; g.azp_adj = azp_adj; g.out = out; g.ldo = ldo; g.out_dtype = out_dtype;
+  g.n_out = g.N;
   if (azp) {
     int32_t* rs = reinterpret_cast<int32_t*>(ws);
     rowsum_i8_kernel<<<(unsigned)std::min<int64_t>((M + 7) / 8, 148 * 16), 256, 0, st>>>(a, (int)M, (int)K, rs);
@@ -790,3 +881,72 @@ extern "C" int kvb_w8a8_scaled_mm(const int8_t* a, const int8_t* b, int b_layout
   if (M <= 128) return launch_gemm<208, 5, false, false>(a, b_nk, g, dests, 1, N, st);
   return launch_gemm<256, 6, false, true>(a, b_nk, g, dests, 1, N, st);
 }
+
+namespace {
+// Checks shared by the gated-activation entry points (N here is the weight row count).
+int check_act_args(const char* who, const int8_t* a, const int8_t* b, const float* sa, const float* sb, int bias_dtype,
+                   const void* bias, int64_t M, int64_t N, int64_t K, int act, int out_dtype) {
+  if (M < 0 || N < 0 || K <= 0) return set_error(KVB_E_ARG, "%s: bad sizes", who);
+  if (act != 1 && act != 2) return set_error(KVB_E_ARG, "%s: act must be 1 (silu(first) * second) or 2 (first * silu(second))", who);
+  if (N % 256 != 0) return set_error(KVB_E_SHAPE, "%s: weight rows (%lld) must be a multiple of 256", who, (long long)N);
+  if (out_dtype != KVB_BF16 && out_dtype != KVB_F16 && out_dtype != KVB_F32)
+    return set_error(KVB_E_DTYPE, "%s: out dtype %d (bf16, f16 or f32)", who, out_dtype);
+  if (bias && bias_dtype != KVB_BF16 && bias_dtype != KVB_F16 && bias_dtype != KVB_F32)
+    return set_error(KVB_E_DTYPE, "%s: bias dtype %d", who, bias_dtype);
+  if (K % 16 != 0) return set_error(KVB_E_SHAPE, "%s: K must be a multiple of 16", who);
+  if (M > 0x7fffffff || N > 0x7fffffff || K > 0x7fffffff) return set_error(KVB_E_SHAPE, "%s: size too large", who);
+  if (M > 0 && (!a || !b || !sa || !sb)) return set_error(KVB_E_ARG, "%s: null pointer", who);
+  if (M > 0 && (!aligned16(a) || !aligned16(b))) return set_error(KVB_E_ALIGN, "%s: A/B must be 16-byte aligned", who);
+  if (!is_sm100()) return set_error(KVB_E_DEVICE, "%s: needs an sm_100 device", who);
+  return KVB_OK;
+}
+}  // namespace
+
+extern "C" int kvb_w8a8_scaled_mm_act(const int8_t* a, const int8_t* b_nk, const float* a_scales, const float* b_scales,
+                                      const void* bias, int bias_dtype, int64_t M, int64_t N, int64_t K, int act,
+                                      void* out, int out_dtype, int64_t ldo, void* stream) {
+  int rc = check_act_args("w8a8_scaled_mm_act", a, b_nk, a_scales, b_scales, bias_dtype, bias, M, N, K, act, out_dtype);
+  if (rc) return rc;
+  if (M == 0 || N == 0) return KVB_OK;
+  if (!out) return set_error(KVB_E_ARG, "w8a8_scaled_mm_act: null output");
+  if (ldo < N / 2) return set_error(KVB_E_SHAPE, "w8a8_scaled_mm_act: ldo < N / 2");
+  GemmArgs g{};
+  g.M = (int)M; g.N = (int)N; g.K = (int)K;
+  g.sa = a_scales; g.sb = b_scales; g.bias = bias; g.bias_dtype = bias_dtype;
+  g.out = out; g.ldo = ldo; g.out_dtype = out_dtype;
+  g.act = act; g.n_out = (int)(N / 2);
+  cudaStream_t st = as_stream(stream);
+  void* dests[1] = {out};
+  if (M <= 128) return launch_gemm<256, 4, false, false>(a, b_nk, g, dests, 1, N / 2, st);
+  return launch_gemm<256, 6, false, true>(a, b_nk, g, dests, 1, N / 2, st);
+}
+
+extern "C" int kvb_w8a8_scaled_mm_act_allgather(const int8_t* a, const int8_t* b_shard, const float* a_scales,
+                                                const float* b_scales_shard, const void* bias_shard, int bias_dtype,
+                                                int64_t M, int64_t N_shard, int64_t K, int act, void* const* out_ptrs,
+                                                int world, int rank, int64_t ldo, int out_dtype, void* stream) {
+  if (world < 1 || world > 8 || rank < 0 || rank >= world)
+    return set_error(KVB_E_ARG, "w8a8_act_allgather: world 1..8, 0 <= rank < world");
+  int rc = check_act_args("w8a8_act_allgather", a, b_shard, a_scales, b_scales_shard, bias_dtype, bias_shard, M,
+                          N_shard, K, act, out_dtype);
+  if (rc) return rc;
+  if (!out_ptrs) return set_error(KVB_E_ARG, "w8a8_act_allgather: null out_ptrs");
+  for (int r = 0; r < world; ++r)
+    if (!out_ptrs[r]) return set_error(KVB_E_ARG, "w8a8_act_allgather: null output pointer of rank %d", r);
+  if (M == 0 || N_shard == 0) return KVB_OK;
+  const int64_t out_shard = N_shard / 2;
+  if (ldo < (int64_t)world * out_shard) return set_error(KVB_E_SHAPE, "w8a8_act_allgather: ldo < world * N_shard / 2");
+  GemmArgs g{};
+  g.M = (int)M; g.N = (int)N_shard; g.K = (int)K;
+  g.sa = a_scales; g.sb = b_scales_shard; g.bias = bias_shard; g.bias_dtype = bias_dtype;
+  g.out = out_ptrs[rank]; g.ldo = ldo; g.out_dtype = out_dtype;
+  g.act = act; g.n_out = (int)out_shard;
+  g.nout = world;
+  g.col_off = (int64_t)rank * out_shard;
+  void* dests[8];
+  for (int d = 0; d < world; ++d) dests[d] = g.outs[d] = out_ptrs[(rank + d) % world];   // own buffer first, then peers
+  cudaStream_t st = as_stream(stream);
+  if (M <= 128) return launch_gemm<256, 4, true, false>(a, b_shard, g, dests, world, ldo, st);
+  return launch_gemm<256, 6, true, true>(a, b_shard, g, dests, world, ldo, st);
+}
+

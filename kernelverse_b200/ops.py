@@ -385,6 +385,52 @@ def w8a8_int32_acc(a: torch.Tensor, b: torch.Tensor) -> torch.Tensor:
     return _gemm(a, b, 0, None, None, None, None, None, torch.int32)
 
 
+_ACT = {"swiglu": 1, "mul_and_silu": 2}
+
+
+def gated_weight_layout(first: torch.Tensor, second: torch.Tensor, first_scales: torch.Tensor,
+                        second_scales: torch.Tensor, first_bias: Optional[torch.Tensor] = None,
+                        second_bias: Optional[torch.Tensor] = None):
+    """One-time weight preparation for :func:`w8a8_scaled_mm_act`: the two operand weights
+    [I, K] (I a multiple of 128; e.g. gate and up projections) with their per-row scales and
+    biases, interleaved in blocks of 128 rows -> (b [2I, K], b_scales [2I], bias [2I] or None)."""
+    i, k = first.shape
+    if second.shape != (i, k) or i % 128:
+        raise ValueError("gated_weight_layout: two [I, K] weights with I a multiple of 128")
+
+    def inter(x, y):
+        return torch.stack((x.reshape(i // 128, 128, *x.shape[1:]), y.reshape(i // 128, 128, *y.shape[1:])),
+                           dim=1).reshape(2 * i, *x.shape[1:]).contiguous()
+    bias = None
+    if first_bias is not None or second_bias is not None:
+        fb = first_bias if first_bias is not None else torch.zeros_like(second_bias)
+        sb = second_bias if second_bias is not None else torch.zeros_like(first_bias)
+        bias = inter(fb, sb)
+    return inter(first, second), inter(first_scales.to(torch.float32), second_scales.to(torch.float32)), bias
+
+
+def w8a8_scaled_mm_act(a: torch.Tensor, b: torch.Tensor, a_scales: torch.Tensor, b_scales: torch.Tensor,
+                       bias: Optional[torch.Tensor] = None, act: str = "swiglu",
+                       out_dtype: torch.dtype = torch.bfloat16) -> torch.Tensor:
+    """W8A8 GEMM + gated activation in one kernel: with f = the W8A8 epilogue value rounded to
+    out_dtype, out[:, c] = silu(f_first) * f_second ("swiglu", operators/activation/swiglu) or
+    f_first * silu(f_second) ("mul_and_silu", operators/activation/mul_and_silu).  b, b_scales
+    and bias in the interleaved order of :func:`gated_weight_layout`; out [M, N / 2]."""
+    dev = _cuda(a, b, a_scales, b_scales, bias)
+    a, b = a.contiguous(), b.contiguous()
+    m, k = a.shape
+    n = b.shape[0]
+    out = torch.empty((m, n // 2), dtype=out_dtype, device=dev)
+    sa = a_scales.to(torch.float32).contiguous()
+    sb = b_scales.to(torch.float32).contiguous()
+    if bias is not None:
+        bias = bias.contiguous()
+    call("kvb_w8a8_scaled_mm_act", _ptr(a), _ptr(b), _ptr(sa), _ptr(sb), _ptr(bias),
+         kvb_dtype(bias.dtype) if bias is not None else 0, m, n, k, _ACT[act], _ptr(out), kvb_dtype(out_dtype), n // 2,
+         _stream(dev))
+    return out
+
+
 def int8_scaled_mm_azp(a, b, a_scales, b_scales, azp_adj, azp, bias, has_azp: bool, has_bias: bool,
                        output_dtype: torch.dtype):
     """operators/gemm/int8_scaled_mm_azp/int8_scaled_mm_azp.py:61-85 (b is [K, N]; azp_adj always added)."""

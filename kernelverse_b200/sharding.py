@@ -55,9 +55,13 @@ class TPW8A8:
     ``b_shard`` [N/g, K] int8, ``b_scales_shard`` [N/g] float32 and ``bias_shard`` [N/g] bf16 are
     this rank's slices; ``__call__(a, a_scales)`` returns the full bf16 output [M, N] (a view of
     this rank's symmetric-memory buffer, valid until the next call).
+
+    With ``act`` ("swiglu" or "mul_and_silu") the shard is this rank's rows of both operand
+    weights in the interleaved order of ``ops.gated_weight_layout`` (N/g a multiple of 256),
+    the gated activation runs in the epilogue, and the gathered output is [M, N/2].
     """
 
-    def __init__(self, group, M: int, b_shard, b_scales_shard, bias_shard=None):
+    def __init__(self, group, M: int, b_shard, b_scales_shard, bias_shard=None, act=None):
         import torch
         import torch.distributed as dist
         import torch.distributed._symmetric_memory as symm_mem
@@ -68,7 +72,8 @@ class TPW8A8:
         self.b, self.sb, self.bias = b_shard.contiguous(), b_scales_shard.float().contiguous(), bias_shard
         self.n_shard, self.k = self.b.shape
         self.M = M
-        self.N = self.n_shard * self.world
+        self.act = act
+        self.N = self.n_shard * self.world // (2 if act else 1)   # gathered output columns
         dev = self.b.device
         self.out = symm_mem.empty((M, self.N), dtype=torch.bfloat16, device=dev)
         self.handle = symm_mem.rendezvous(self.out, group)
@@ -88,9 +93,15 @@ class TPW8A8:
         stream = torch.cuda.current_stream(a.device).cuda_stream
         bias_ptr = self.bias.data_ptr() if self.bias is not None else None
         bias_dt = _lib.BF16 if self.bias is not None else 0
-        _lib.call("kvb_w8a8_scaled_mm_allgather", a.data_ptr(), self.b.data_ptr(), sa.data_ptr(), self.sb.data_ptr(),
-                  bias_ptr, bias_dt, self.M, self.n_shard, self.k, self._ptrs, self.world, self.rank, self.N,
-                  _lib.BF16, stream)
+        if self.act:
+            from .ops import _ACT
+            _lib.call("kvb_w8a8_scaled_mm_act_allgather", a.data_ptr(), self.b.data_ptr(), sa.data_ptr(),
+                      self.sb.data_ptr(), bias_ptr, bias_dt, self.M, self.n_shard, self.k, _ACT[self.act], self._ptrs,
+                      self.world, self.rank, self.N, _lib.BF16, stream)
+        else:
+            _lib.call("kvb_w8a8_scaled_mm_allgather", a.data_ptr(), self.b.data_ptr(), sa.data_ptr(),
+                      self.sb.data_ptr(), bias_ptr, bias_dt, self.M, self.n_shard, self.k, self._ptrs, self.world,
+                      self.rank, self.N, _lib.BF16, stream)
         if sync:
             dist.all_reduce(self._flag, group=self.group)   # every rank's stores have landed after this
         return self.out

@@ -12,6 +12,10 @@
   ``[K, N]``; ``azp_adj`` is always added (``:82``).  The oracle evaluates it
   in float64 (the reference uses float32, so the two agree to float32
   rounding, well inside the reference's tolerances).
+* ``w8a8_scaled_mm_act``: the gate+up GEMM followed by SwiGLU
+  (``operators/activation/swiglu/swiglu.py:24-28``) or mul-and-silu
+  (``operators/activation/mul_and_silu/mul_and_silu.py:24-29``) on the GEMM's
+  stored (rounded) output, in float32.
 """
 from __future__ import annotations
 
@@ -46,3 +50,23 @@ def int8_scaled_mm_azp(a, b_kn, a_scales, b_scales, azp_adj, azp, bias,
     if has_bias:
         out = out + np.asarray(bias, np.float64).reshape(1, -1)
     return round_to(out.astype(np.float32), out_dtype)
+
+
+def silu_f32(x: np.ndarray) -> np.ndarray:
+    """x / (1 + e^-x) in float32 (each operation rounded to float32)."""
+    x = np.asarray(x, np.float32)
+    with np.errstate(over="ignore"):
+        return (x / (np.float32(1.0) + np.exp(-x))).astype(np.float32)
+
+
+def w8a8_scaled_mm_act(a, b_first, b_second, sa, s_first, s_second, bias_first=None, bias_second=None,
+                       act: str = "swiglu", out_dtype: str = "BF16") -> np.ndarray:
+    """The W8A8 GEMM of each operand weight rounded to ``out_dtype`` (what the unfused GEMM
+    stores), then operators/activation/swiglu/swiglu.py:24-28 (``silu(first) * second``) or
+    operators/activation/mul_and_silu/mul_and_silu.py:24-29 (``first * silu(second)``) in
+    float32, rounded to ``out_dtype``."""
+    f = round_to(w8a8_scaled_mm(a, b_first, sa, s_first, bias_first, "FP32"), out_dtype).astype(np.float32)
+    g = round_to(w8a8_scaled_mm(a, b_second, sa, s_second, bias_second, "FP32"), out_dtype).astype(np.float32)
+    y = silu_f32(f) * g if act == "swiglu" else f * silu_f32(g)
+    return round_to(y.astype(np.float32), out_dtype)
+

@@ -38,7 +38,8 @@ def load_golden(name: str):
 
 
 def golden_names(prefix: str):
-    return sorted(p.stem for p in GOLDEN.glob(f"{prefix}_*.npz"))
+    """Fixtures named ``<prefix>_<number>`` (so ``w8a8`` does not also pick up ``w8a8_act_0``)."""
+    return sorted(p.stem for p in GOLDEN.glob(f"{prefix}_*.npz") if p.stem[len(prefix) + 1:].isdigit())
 
 
 @pytest.fixture

@@ -278,6 +278,29 @@ def main():
         save(f"flash_decoding_attention_{i}", shape, query=qq, key_cache=kk, value_cache=vv, out=out,
              exp_sums=es, max_logits=ml, partial_out=po)
 
+    # --- next rows: W8A8 gate+up GEMM followed by the reference's swiglu / mul_and_silu (correctness mode)
+    #     on the bf16 GEMM output (int32 acc via torch._int_mm, float32 epilogue as the w8a8 fixtures)
+    for i, (m, inner, k, act) in enumerate([(33, 256, 256, "swiglu"), (200, 128, 128, "mul_and_silu")]):
+        gen = torch.Generator().manual_seed(1400 + i)
+        a = torch.randint(-127, 128, (m, k), generator=gen, dtype=torch.int8)
+        b1 = torch.randint(-127, 128, (inner, k), generator=gen, dtype=torch.int8)
+        b2 = torch.randint(-127, 128, (inner, k), generator=gen, dtype=torch.int8)
+        sa = torch.rand((m,), generator=gen) * 9e-3 + 1e-3
+        s1 = torch.rand((inner,), generator=gen) * 9e-3 + 1e-3
+        s2 = torch.rand((inner,), generator=gen) * 9e-3 + 1e-3
+        bias1 = (0.1 * torch.randn((inner,), generator=gen)).to(torch.bfloat16)
+        bias2 = (0.1 * torch.randn((inner,), generator=gen)).to(torch.bfloat16)
+        mp = max(m, 17)
+        ap = torch.zeros((mp, k), dtype=torch.int8)
+        ap[:m] = a
+        y1 = ((torch._int_mm(ap, b1.t().contiguous())[:m].float() * sa[:, None]) * s1[None, :] + bias1.float()).to(torch.bfloat16)
+        y2 = ((torch._int_mm(ap, b2.t().contiguous())[:m].float() * sa[:, None]) * s2[None, :] + bias2.float()).to(torch.bfloat16)
+        x = torch.cat([y1, y2], dim=-1)
+        shp = {"shape": [m, 2 * inner], "dim": -1, "dtype": "BF16"}
+        out = run_model("activation", act, shp, (x,))
+        save(f"w8a8_act_{i}", {"M": m, "I": inner, "K": k, "act": act}, a=a, b_first=b1, b_second=b2, sa=sa,
+             s_first=s1, s_second=s2, bias_first=bias1, bias_second=bias2, out=out)
+
     (HERE / "VERSIONS.txt").write_text(f"torch {torch.__version__}\nnumpy {np.__version__}\n")
 
 

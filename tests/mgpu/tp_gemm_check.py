@@ -1,4 +1,5 @@
-"""Fused column-sharded TP W8A8 GEMM + all-gather on N GPUs vs the single-GPU GEMM (bit-exact).
+"""Fused column-sharded TP W8A8 GEMM + all-gather on N GPUs vs the single-GPU GEMM (bit-exact),
+with and without the gated (SwiGLU) epilogue.
 
 Run with: python -m torch.distributed.run --nproc-per-node N --master-addr 127.0.0.1 tests/mgpu/tp_gemm_check.py
 """
@@ -37,6 +38,32 @@ def main():
                 torch.cuda.synchronize()
                 ok = ok and torch.equal(out, ref)
             dist.barrier()
+            if rank == 0 and not ok:
+                print(f"mismatch in the plain case M={M} N={N}", flush=True)
+        # gated (SwiGLU) epilogue: rank r holds rows [r I/g, (r+1) I/g) of the gate and up weights
+        for (M, I, K) in ((200, 256 * world, 512), (4096, 1024 * world, 1024)):
+            g = torch.Generator(device=dev).manual_seed(M + 7)
+            a = torch.randint(-127, 128, (M, K), generator=g, device=dev, dtype=torch.int8)
+            b1 = torch.randint(-127, 128, (I, K), generator=g, device=dev, dtype=torch.int8)
+            b2 = torch.randint(-127, 128, (I, K), generator=g, device=dev, dtype=torch.int8)
+            sa = torch.rand((M,), generator=g, device=dev) * 9e-3 + 1e-3
+            s1 = torch.rand((I,), generator=g, device=dev) * 9e-3 + 1e-3
+            s2 = torch.rand((I,), generator=g, device=dev) * 9e-3 + 1e-3
+            c1 = (0.1 * torch.randn((I,), generator=g, device=dev)).to(torch.bfloat16)
+            c2 = (0.1 * torch.randn((I,), generator=g, device=dev)).to(torch.bfloat16)
+            bl, sl_, cl = ops.gated_weight_layout(b1, b2, s1, s2, c1, c2)
+            ref = ops.w8a8_scaled_mm_act(a, bl, sa, sl_, cl, act="swiglu")
+            i0, iw = column_shard(I, world, rank, align=128)
+            sl = slice(i0, i0 + iw)
+            bs, ss, cs = ops.gated_weight_layout(b1[sl], b2[sl], s1[sl], s2[sl], c1[sl], c2[sl])
+            tp = TPW8A8(dist.group.WORLD, M, bs, ss, cs, act="swiglu")
+            for _ in range(2):
+                out = tp(a, sa)
+                torch.cuda.synchronize()
+                ok = ok and torch.equal(out, ref)
+            dist.barrier()
+            if rank == 0 and not ok:
+                print(f"mismatch in the gated case M={M} I={I}", flush=True)
         flag = torch.tensor([1.0 if ok else 0.0], device=dev)
         dist.all_reduce(flag, op=dist.ReduceOp.MIN)
         from kernelverse_b200 import _lib

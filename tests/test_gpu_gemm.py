@@ -120,3 +120,47 @@ def test_w8a8_rejects_bad_k():
     a = torch.zeros((4, 24), dtype=torch.int8, device="cuda")
     with pytest.raises(_lib.KvbError, match="multiple of 16"):
         _ops().w8a8_int32_acc(a, a)
+
+
+def _act_check(out, ref):
+    """Gated epilogue: float32 silu on the rounded GEMM values; CUDA's and numpy's exp may differ
+    in the last bit, which can move a bf16 rounding by one step."""
+    o, r = host(out).astype(np.float64), np.asarray(ref, np.float64)
+    np.testing.assert_allclose(o, r, rtol=8e-3, atol=1e-6)
+    assert np.mean(o == r) > 0.99
+
+
+@pytest.mark.parametrize("name", golden_names("w8a8_act"))
+def test_w8a8_act_golden(name):
+    meta, g = load_golden(name)
+    bf = torch.bfloat16
+    b, sb, bias = _ops().gated_weight_layout(dev(g["b_first"][0]), dev(g["b_second"][0]), dev(g["s_first"][0]),
+                                             dev(g["s_second"][0]), dev(g["bias_first"][0], bf),
+                                             dev(g["bias_second"][0], bf))
+    out = _ops().w8a8_scaled_mm_act(dev(g["a"][0]), b, dev(g["sa"][0]), sb, bias, meta["act"])
+    assert out.shape == (meta["M"], meta["I"]) and out.dtype == bf
+    _act_check(out, g["out"][0])
+
+
+@pytest.mark.parametrize("act", ["swiglu", "mul_and_silu"])
+@pytest.mark.parametrize("M,I,K", [(1, 128, 64), (16, 384, 256), (128, 256, 1024), (129, 512, 128),
+                                   (300, 1024, 512), (1024, 1280, 2048)])
+def test_w8a8_act_shapes(act, M, I, K):
+    """Single-CTA (M <= 128) and CTA-pair tiles, ragged M, several tile columns."""
+    rng = seeded(M * 3 + I + K)
+    a, b1, b2 = _i8(rng, (M, K)), _i8(rng, (I, K)), _i8(rng, (I, K))
+    sa, s1, s2 = _scales(rng, M), _scales(rng, I), _scales(rng, I)
+    from oracle.numerics import round_bf16
+    bias1 = round_bf16((0.1 * rng.standard_normal(I)).astype(np.float32))
+    bias2 = round_bf16((0.1 * rng.standard_normal(I)).astype(np.float32))
+    bf = torch.bfloat16
+    b, sb, bias = _ops().gated_weight_layout(dev(b1), dev(b2), dev(s1), dev(s2), dev(bias1, bf), dev(bias2, bf))
+    out = _ops().w8a8_scaled_mm_act(dev(a), b, dev(sa), sb, bias, act)
+    _act_check(out, gemm.w8a8_scaled_mm_act(a, b1, b2, sa, s1, s2, bias1, bias2, act, "BF16"))
+
+
+def test_w8a8_act_rejects_unaligned_width():
+    rng = seeded(2)
+    a, b = dev(_i8(rng, (4, 64))), dev(_i8(rng, (384, 64)))     # 384 rows: not a multiple of 256
+    with pytest.raises(Exception, match="multiple of 256"):
+        _ops().w8a8_scaled_mm_act(a, b, dev(_scales(rng, 4)), dev(_scales(rng, 384)))
