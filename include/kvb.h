@@ -286,6 +286,30 @@ KVB_API int kvb_paged_attention(const void* query, int q_dtype, const void* key_
                                 void* max_logits, void* tmp_out, int max_partitions, void* workspace,
                                 size_t workspace_bytes, void* stream);
 
+/* Bytes of workspace kvb_flash_attn_with_kvcache needs. */
+KVB_API size_t kvb_flash_attn_with_kvcache_workspace_size(int batch, int seq_len_q, int num_heads, int head_dim,
+                                                          int64_t seq_len_k);
+
+/*
+ * Attention of seq_len_q query tokens per sequence over a dense KV cache.
+ * Replaces operators/attention/flash_attn_with_kvcache/flash_attn_with_kvcache.py:29-56:
+ * q [batch, seq_len_q, num_heads, D]; k_cache / v_cache [batch, seq_len_k, num_kv_heads, D];
+ * cache_seqlens [batch] (KVB_I32 or KVB_I64, each <= seq_len_k): every query token of
+ * sequence b attends to its first cache_seqlens[b] keys (no causal mask), query head h to KV
+ * head h / (num_heads / num_kv_heads), logits scaled by softmax_scale, float32 softmax.
+ * out [batch, seq_len_q, num_heads, D] in `dtype`; softmax_lse [batch, num_heads, seq_len_q]
+ * float32, the natural-log sum of exp of the scaled logits (may be NULL).  q, caches and out
+ * share `dtype` (KVB_F32, KVB_F16 or KVB_BF16; D = 32, 64 or 128 for the 16-bit types).  Runs
+ * the split-KV decode kernels with one query row per (sequence, query token); KV heads whose
+ * query tiles exceed 16 warps are split across CTAs.  workspace: >=
+ * kvb_flash_attn_with_kvcache_workspace_size() bytes.
+ */
+KVB_API int kvb_flash_attn_with_kvcache(const void* q, const void* k_cache, const void* v_cache, int dtype,
+                                       const void* cache_seqlens, int seqlens_dtype, int batch, int seq_len_q,
+                                       int64_t seq_len_k, int num_heads, int num_kv_heads, int head_dim,
+                                       float softmax_scale, void* out, float* softmax_lse, void* workspace,
+                                       size_t workspace_bytes, void* stream);
+
 /*
  * Allocation-free variant of kvb_paged_attention (no counterpart in the reference).
  * Some callers cannot allocate device memory: a plugin that its host framework hands only

@@ -128,10 +128,14 @@ struct DecodeArgs {
   float sm_scale;
   int batch, hq, hkv, group, bs, part, pmax, tiles_per_kv, stages;
   int q_dtype, new_dtype, sl64, v2_dtype;
+  int qtok;                 // query tokens per cached sequence: query row b reads sequence b / qtok
+  int hc;                   // KV heads per CTA (hkv, or a divisor of it with the heads split over grid.z)
 };
 
+// Length of the cached sequence that query row b attends to.
 __device__ __forceinline__ int64_t seq_len_of(const DecodeArgs& a, int b) {
-  return a.sl64 ? reinterpret_cast<const int64_t*>(a.seq_lens)[b] : (int64_t)reinterpret_cast<const int32_t*>(a.seq_lens)[b];
+  const int sq = b / a.qtok;
+  return a.sl64 ? reinterpret_cast<const int64_t*>(a.seq_lens)[sq] : (int64_t)reinterpret_cast<const int32_t*>(a.seq_lens)[sq];
 }
 
 __device__ __forceinline__ float load_any(const void* p, int dt, int64_t i) {
@@ -145,10 +149,12 @@ __device__ __forceinline__ void store_any(void* p, int dt, int64_t i, float v) {
   else reinterpret_cast<float*>(p)[i] = v;
 }
 
-// Physical row (block * bs + offset) of token t of sequence b; -1 if the table entry is invalid.
+// Physical row (block * bs + offset) of token t of the sequence query row b attends to; -1 if
+// the table entry is invalid.
 __device__ __forceinline__ int64_t token_row(const DecodeArgs& a, int b, int64_t t) {
   const int64_t blk = t / a.bs;
-  const int64_t phys = a.block_table ? (int64_t)a.block_table[(int64_t)b * a.bt_stride + blk] : (int64_t)b;
+  const int64_t sq = b / a.qtok;
+  const int64_t phys = a.block_table ? (int64_t)a.block_table[sq * a.bt_stride + blk] : sq;
   if (phys < 0 || phys >= a.num_blocks) return -1;
   return phys * a.bs + (t - blk * a.bs);
 }
@@ -170,8 +176,9 @@ __global__ void __launch_bounds__(MAXT, MAXT <= 288 ? 2 : 1) paged_decode_kernel
   // started; it waits for this grid's completion before reading anything this grid writes.
   asm volatile("griddepcontrol.launch_dependents;");
   const int p = blockIdx.x, b = blockIdx.y;
+  const int h0 = blockIdx.z * a.hc;                  // first KV head of this CTA
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int ncons = a.hkv * a.tiles_per_kv;          // consumer warps; warp ncons is the producer
+  const int ncons = a.hc * a.tiles_per_kv;           // consumer warps; warp ncons is the producer
   const int64_t L = seq_len_of(a, b);
   const int64_t t_begin = (int64_t)p * a.part;
   const int64_t t_end = (L < t_begin + a.part ? L : t_begin + a.part);
@@ -179,22 +186,25 @@ __global__ void __launch_bounds__(MAXT, MAXT <= 288 ? 2 : 1) paged_decode_kernel
 
   if (t_begin >= L) {
     // Partition past this sequence's end: v2 outputs hold exp_sum 0, max -inf, tmp_out 0.
-    if (a.exp_sums) {
-      for (int i = threadIdx.x; i < a.hq; i += blockDim.x) {
-        const int64_t o = ((int64_t)b * a.hq + i) * a.pmax + p;
+    if (a.exp_sums) {   // this CTA's query heads only: [h0 * group, (h0 + hc) * group)
+      const int qh0 = h0 * a.group, nqh = a.hc * a.group;
+      for (int i = threadIdx.x; i < nqh; i += blockDim.x) {
+        const int64_t o = ((int64_t)b * a.hq + qh0 + i) * a.pmax + p;
         store_any(a.exp_sums, a.v2_dtype, o, 0.0f);
         store_any(a.max_logits, a.v2_dtype, o, -INFINITY);
       }
-      for (int i = threadIdx.x; i < a.hq * D_; i += blockDim.x) {
-        const int h = i / D_, d = i % D_;
+      for (int i = threadIdx.x; i < nqh * D_; i += blockDim.x) {
+        const int h = qh0 + i / D_, d = i % D_;
         store_any(a.tmp_out, a.v2_dtype, (((int64_t)b * a.hq + h) * a.pmax + p) * D_ + d, 0.0f);
       }
     }
     return;
   }
   const int nchunks = (int)((t_end - t_begin + kChunk - 1) / kChunk);
-  const uint32_t row_bytes = (uint32_t)(a.hkv * D * EB);
-  const uint32_t chunk_bytes = kChunk * row_bytes;
+  const uint32_t row_bytes = (uint32_t)(a.hkv * D * EB);   // a token row in the cache (all KV heads)
+  const uint32_t srow = (uint32_t)(a.hc * D * EB);         // its slice of this CTA's heads, as staged
+  const uint32_t head_off = (uint32_t)(h0 * D * EB);
+  const uint32_t chunk_bytes = kChunk * srow;
   const int S = a.stages;
   auto kstage = [&](int s) { return smem + (size_t)s * 2 * chunk_bytes; };
   auto vstage = [&](int s) { return smem + (size_t)s * 2 * chunk_bytes + chunk_bytes; };
@@ -220,14 +230,24 @@ __global__ void __launch_bounds__(MAXT, MAXT <= 288 ? 2 : 1) paged_decode_kernel
         if (i >= S && !mbar_wait_bounded(&empty[s], ph ^ 1u)) break;
         const int64_t t0 = t_begin + (int64_t)i * kChunk;
         const int64_t t1 = t_end < t0 + kChunk ? t_end : t0 + kChunk;   // rows past the end are not copied
-        // The chunk is copied as runs of rows that stay inside one block (any block size).
-        uint32_t bytes = 0;
-        for (int64_t t = t0; t < t1;) {
-          const int64_t n = min(t1 - t, (int64_t)a.bs - t % a.bs);
-          bytes += 2u * (uint32_t)n * row_bytes;
-          t += n;
+        mbar_arrive_expect_tx(&full[s], 2u * (uint32_t)(t1 - t0) * srow);
+        if (srow != row_bytes) {
+          // Heads split over CTAs: each token row's slice of this CTA's heads, one copy each.
+          for (int64_t t = t0; t < t1; ++t) {
+            const int64_t row = token_row(a, b, t);
+            const size_t doff = (size_t)(t - t0) * srow;
+            if (row < 0) {
+              atomicOr(&g_tu_status, kStatusBadIndex);
+              asm volatile("mbarrier.complete_tx.relaxed.cta.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(&full[s])),
+                           "r"(2 * srow) : "memory");
+            } else {
+              bulk_g2s(kstage(s) + doff, kc + row * row_bytes + head_off, srow, &full[s], pol);
+              bulk_g2s(vstage(s) + doff, vc + row * row_bytes + head_off, srow, &full[s], pol);
+            }
+          }
+          continue;
         }
-        mbar_arrive_expect_tx(&full[s], bytes);
+        // All heads: the chunk is copied as runs of rows that stay inside one block (any block size).
         for (int64_t t = t0; t < t1;) {
           const int64_t n = min(t1 - t, (int64_t)a.bs - t % a.bs);
           const int64_t row = token_row(a, b, t);
@@ -253,7 +273,8 @@ __global__ void __launch_bounds__(MAXT, MAXT <= 288 ? 2 : 1) paged_decode_kernel
 
   // ------------------------------------------------------------------ consumer warps
   const int g = lane >> 2, c = lane & 3;
-  const int kvh = warp / a.tiles_per_kv, nt = warp % a.tiles_per_kv;
+  const int kvl = warp / a.tiles_per_kv, nt = warp % a.tiles_per_kv;   // KV head within this CTA's group
+  const int kvh = h0 + kvl;
   const int qn = nt * 8 + g;                         // this lane's query head within the group (B operand col)
   const bool qvalid = qn < a.group;
   const int qhead = kvh * a.group + qn;
@@ -300,7 +321,7 @@ __global__ void __launch_bounds__(MAXT, MAXT <= 288 ? 2 : 1) paged_decode_kernel
                                             make_divisor(ksc));
           const uint16_t vc2 = quant_e4m3x2(load_any(a.v_new, a.new_dtype, src), load_any(a.v_new, a.new_dtype, src + 1),
                                             make_divisor(vsc));
-          const size_t off = (size_t)r * row_bytes + (size_t)kvh * D + d;
+          const size_t off = (size_t)r * srow + (size_t)kvl * D + d;
           *reinterpret_cast<uint16_t*>(ks + off) = kc2;
           *reinterpret_cast<uint16_t*>(vs + off) = vc2;
           if (nt == 0 && row >= 0) {
@@ -317,8 +338,8 @@ __global__ void __launch_bounds__(MAXT, MAXT <= 288 ? 2 : 1) paged_decode_kernel
     const int nvalid = (int)(t_end - t0 < kChunk ? t_end - t0 : kChunk);
     uint32_t kw0[KW], kw1[KW];
     {
-      const uint8_t* r0 = ks + (size_t)g * row_bytes + (size_t)kvh * D * EB + c * KSPAN;
-      const uint8_t* r1 = r0 + 8 * (size_t)row_bytes;
+      const uint8_t* r0 = ks + (size_t)g * srow + (size_t)kvl * D * EB + c * KSPAN;
+      const uint8_t* r1 = r0 + 8 * (size_t)srow;
       if constexpr (KW == 8) {
         // Two 16-byte halves per row: lanes of odd g load them in the opposite order, so the
         // eight lanes of a quarter-warp hit eight different bank groups; selects undo the swap.
@@ -401,7 +422,7 @@ __global__ void __launch_bounds__(MAXT, MAXT <= 288 ? 2 : 1) paged_decode_kernel
       const int toks[4] = {2 * c, 2 * c + 1, 2 * c + 8, 2 * c + 9};
 #pragma unroll
       for (int rr = 0; rr < 4; ++rr) {
-        const uint8_t* src = vs + (size_t)toks[rr] * row_bytes + (size_t)kvh * D * EB + g * VSPAN;
+        const uint8_t* src = vs + (size_t)toks[rr] * srow + (size_t)kvl * D * EB + g * VSPAN;
         load_words<VW>(src, vw[rr]);
         if (toks[rr] >= nvalid) {      // rows past the sequence end hold stale bytes: zero them
 #pragma unroll
@@ -567,14 +588,16 @@ __global__ void __launch_bounds__(128) paged_decode_f32_kernel(const __grid_cons
 // Combines the partitions of one (sequence, query head): out = sum_p o_p 2^(m_p - M) /
 // (sum_p l_p 2^(m_p - M) + eps).  The partition weights are computed once into shared memory
 // (dynamic, pmax floats) and every thread then sums one output dimension with independent loads.
+// With lse, the natural-log sum of exp of the scaled logits of query row b (= sequence b / qtok,
+// query token b % qtok) and head h goes to lse[((b / qtok) * hq + h) * qtok + b % qtok].
 __global__ void __launch_bounds__(128) decode_merge_kernel(const float* __restrict__ m_part, const float* __restrict__ l_part,
                                                            const float* __restrict__ o_part, const void* seq_lens, int sl64,
                                                            int hq, int D, int part, int pmax, float eps, void* out,
-                                                           int out_dtype) {
+                                                           int out_dtype, int qtok, float* __restrict__ lse) {
   extern __shared__ float wgt[];        // [pmax]
   __shared__ float red[32];
-  const int bh = blockIdx.x, b = bh / hq;
-  const int64_t L = sl64 ? reinterpret_cast<const int64_t*>(seq_lens)[b] : (int64_t)reinterpret_cast<const int32_t*>(seq_lens)[b];
+  const int bh = blockIdx.x, b = bh / hq, sq = b / qtok;
+  const int64_t L = sl64 ? reinterpret_cast<const int64_t*>(seq_lens)[sq] : (int64_t)reinterpret_cast<const int32_t*>(seq_lens)[sq];
   const int64_t npl = (L + part - 1) / part;
   const int np = (int)(npl < pmax ? npl : pmax);
   // Launched as a programmatic dependent of the decode grid: wait until that grid has
@@ -609,6 +632,8 @@ __global__ void __launch_bounds__(128) decode_merge_kernel(const float* __restri
 #pragma unroll
   for (int off = 16; off > 0; off >>= 1) ls += __shfl_xor_sync(0xffffffffu, ls, off);
   const float inv = np > 0 ? 1.0f / (ls + eps) : 0.0f;
+  if (lse && threadIdx.x == 0)   // M, in log2 units, plus log2 of the rescaled sum, to natural log
+    lse[((int64_t)sq * hq + bh % hq) * qtok + b % qtok] = np > 0 ? (Mu + log2f(ls)) * kLn2 : -INFINITY;
   const float* op = o_part + (int64_t)bh * pmax * D;
   for (int d = threadIdx.x; d < D; d += blockDim.x) {
     float acc0 = 0.0f, acc1 = 0.0f, acc2 = 0.0f, acc3 = 0.0f;
@@ -638,8 +663,8 @@ int launch_decode_t(DecodeArgs& a, size_t smem, cudaStream_t st) {
     attr_set_dev = dev;
     attr_smem = smem;
   }
-  const int threads = (a.hkv * a.tiles_per_kv + 1) * 32;
-  dim3 grid(a.pmax, a.batch);
+  const int threads = (a.hc * a.tiles_per_kv + 1) * 32;
+  dim3 grid(a.pmax, a.batch, a.hkv / a.hc);
   kern<<<grid, threads, smem, st>>>(a);
   return check_launch("paged_decode_kernel");
 }
@@ -647,7 +672,7 @@ int launch_decode_t(DecodeArgs& a, size_t smem, cudaStream_t st) {
 // Up to 8 consumer warps (+1 producer) get a 288-thread register budget; more use 544.
 template <typename KT, int D>
 int launch_decode(DecodeArgs& a, size_t smem, cudaStream_t st) {
-  if (a.hkv * a.tiles_per_kv <= 8) return launch_decode_t<KT, D, 288>(a, smem, st);
+  if (a.hc * a.tiles_per_kv <= 8) return launch_decode_t<KT, D, 288>(a, smem, st);
   return launch_decode_t<KT, D, 544>(a, smem, st);
 }
 
@@ -668,14 +693,14 @@ extern "C" size_t kvb_paged_attention_workspace_size(int batch, int num_q_heads,
   return (n * (size_t)(head_dim + 2)) * sizeof(float) + 256;
 }
 
-extern "C" int kvb_paged_attention(const void* query, int q_dtype, const void* key_cache, const void* value_cache,
+static int paged_attention_impl(const void* query, int q_dtype, const void* key_cache, const void* value_cache,
                                    int cache_dtype, const float* k_scale, const float* v_scale, const void* seq_lens,
                                    int seq_lens_dtype, const int32_t* block_table, int64_t bt_stride, int batch,
                                    int num_q_heads, int num_kv_heads, int head_dim, int block_size, int64_t num_blocks,
                                    int64_t max_seq_len, float sm_scale, const void* k_new, const void* v_new,
                                    int new_dtype, int partition_size, void* out, int out_dtype, void* exp_sums,
                                    void* max_logits, void* tmp_out, int max_partitions, void* workspace,
-                                   size_t workspace_bytes, void* stream) {
+                                   size_t workspace_bytes, void* stream, int qtok, float* lse) {
   if (batch < 0 || num_q_heads <= 0 || num_kv_heads <= 0 || head_dim <= 0 || block_size <= 0 || max_seq_len < 0)
     return set_error(KVB_E_ARG, "paged_attention: bad sizes");
   if (batch == 0) return KVB_OK;
@@ -696,7 +721,26 @@ extern "C" int kvb_paged_attention(const void* query, int q_dtype, const void* k
     return set_error(KVB_E_ARG, "paged_attention: the fused write needs k_new, v_new and an e4m3 cache");
   const int group = num_q_heads / num_kv_heads;
   const int tiles = (group + 7) / 8;
-  if (num_kv_heads * tiles > 16) return set_error(KVB_E_SHAPE, "paged_attention: more than 16 (kv head, 8-query) tiles");
+  if (qtok < 1 || batch % qtok) return set_error(KVB_E_ARG, "paged_attention: batch must be a multiple of qtok");
+  if ((k_new || v_new) && qtok != 1) return set_error(KVB_E_ARG, "paged_attention: the fused write needs one query per sequence");
+  // KV heads per CTA (tensor-core kernels): all of them when their (kv head, 8-query) tiles fit
+  // 16 consumer warps and two 16-token stages of their K/V fit in shared memory; else the
+  // largest divisor of num_kv_heads whose tiles fit 8 warps and whose stages fit (heads split
+  // over grid.z).
+  int hc = num_kv_heads;
+  if (cache_dtype != KVB_F32) {
+    const size_t head_stage = (size_t)2 * kChunk * head_dim * (cache_dtype == KVB_E4M3 ? 1 : dtype_size(cache_dtype));
+    auto fits = [&](int c, int warps) { return c * tiles <= warps && 2 * head_stage * (size_t)c <= 200 * 1024; };
+    if (!fits(num_kv_heads, 16)) {
+      hc = 0;
+      for (int c = num_kv_heads; c >= 1; --c)
+        if (num_kv_heads % c == 0 && fits(c, 8)) { hc = c; break; }
+      if (hc == 0) {
+        if (!fits(1, 16)) return set_error(KVB_E_SHAPE, "paged_attention: more than 128 query heads per KV head");
+        hc = 1;
+      }
+    }
+  }
   int part = partition_size > 0 ? partition_size : 512;
   if (part % kChunk) return set_error(KVB_E_SHAPE, "paged_attention: partition_size must be a multiple of 16");
   const int64_t pmax64 = (max_seq_len + part - 1) / part;
@@ -719,7 +763,7 @@ extern "C" int kvb_paged_attention(const void* query, int q_dtype, const void* k
   const int64_t row_bytes = (int64_t)num_kv_heads * head_dim * esize;
   if (row_bytes % 16) return set_error(KVB_E_ALIGN, "paged_attention: a token row must be a multiple of 16 bytes");
   if (!aligned16(key_cache) || !aligned16(value_cache)) return set_error(KVB_E_ALIGN, "paged_attention: caches must be 16-byte aligned");
-  const size_t stage_bytes = (size_t)2 * kChunk * row_bytes;
+  const size_t stage_bytes = (size_t)2 * kChunk * (row_bytes / num_kv_heads) * hc;   // this CTA's heads
   int stages = (int)std::min<size_t>(kStagesMax, (200 * 1024) / stage_bytes);
   if (stages > 3 && stage_bytes * 3 >= 96 * 1024) stages = 3;
   if (cache_dtype != KVB_F32 && stages < 2)
@@ -736,6 +780,7 @@ extern "C" int kvb_paged_attention(const void* query, int q_dtype, const void* k
   a.sm_scale = sm_scale;
   a.batch = batch; a.hq = num_q_heads; a.hkv = num_kv_heads; a.group = group; a.bs = block_size; a.part = part;
   a.pmax = pmax; a.tiles_per_kv = tiles; a.stages = stages;
+  a.qtok = qtok; a.hc = hc;
   a.q_dtype = q_dtype; a.new_dtype = new_dtype; a.sl64 = seq_lens_dtype == KVB_I64; a.v2_dtype = out_dtype;
   const size_t smem = stage_bytes * stages;
   cudaStream_t st = as_stream(stream);
@@ -770,9 +815,46 @@ extern "C" int kvb_paged_attention(const void* query, int q_dtype, const void* k
   const float* op = a.o_part;
   const int sl64 = a.sl64;
   cudaError_t e = cudaLaunchKernelEx(&cfg, decode_merge_kernel, mp, lp, op, seq_lens, sl64, num_q_heads, head_dim, part,
-                                     pmax, eps, out, out_dtype);
+                                     pmax, eps, out, out_dtype, qtok, lse);
   if (e != cudaSuccess) return set_error(KVB_E_LAUNCH, "decode_merge_kernel: %s", cudaGetErrorString(e));
   return check_launch("decode_merge_kernel");
+}
+
+extern "C" int kvb_paged_attention(const void* query, int q_dtype, const void* key_cache, const void* value_cache,
+                                   int cache_dtype, const float* k_scale, const float* v_scale, const void* seq_lens,
+                                   int seq_lens_dtype, const int32_t* block_table, int64_t bt_stride, int batch,
+                                   int num_q_heads, int num_kv_heads, int head_dim, int block_size, int64_t num_blocks,
+                                   int64_t max_seq_len, float sm_scale, const void* k_new, const void* v_new,
+                                   int new_dtype, int partition_size, void* out, int out_dtype, void* exp_sums,
+                                   void* max_logits, void* tmp_out, int max_partitions, void* workspace,
+                                   size_t workspace_bytes, void* stream) {
+  return paged_attention_impl(query, q_dtype, key_cache, value_cache, cache_dtype, k_scale, v_scale, seq_lens,
+                              seq_lens_dtype, block_table, bt_stride, batch, num_q_heads, num_kv_heads, head_dim,
+                              block_size, num_blocks, max_seq_len, sm_scale, k_new, v_new, new_dtype, partition_size, out,
+                              out_dtype, exp_sums, max_logits, tmp_out, max_partitions, workspace, workspace_bytes,
+                              stream, 1, nullptr);
+}
+
+extern "C" size_t kvb_flash_attn_with_kvcache_workspace_size(int batch, int seq_len_q, int num_heads, int head_dim,
+                                                             int64_t seq_len_k) {
+  const int64_t pmax = seq_len_k > 0 ? (seq_len_k + 511) / 512 : 1;
+  return kvb_paged_attention_workspace_size(batch * seq_len_q, num_heads, head_dim, (int)pmax);
+}
+
+extern "C" int kvb_flash_attn_with_kvcache(const void* q, const void* k_cache, const void* v_cache, int dtype,
+                                          const void* cache_seqlens, int seqlens_dtype, int batch, int seq_len_q,
+                                          int64_t seq_len_k, int num_heads, int num_kv_heads, int head_dim,
+                                          float softmax_scale, void* out, float* softmax_lse, void* workspace,
+                                          size_t workspace_bytes, void* stream) {
+  if (batch < 0 || seq_len_q <= 0 || seq_len_k <= 0 || num_heads <= 0 || num_kv_heads <= 0)
+    return set_error(KVB_E_ARG, "flash_attn_with_kvcache: bad sizes");
+  if (batch == 0) return KVB_OK;
+  // Query token i of sequence b is query row b * seq_len_q + i (q is [batch, seq_len_q, heads, D]);
+  // all rows of sequence b read block b of the cache, which holds the whole sequence.
+  return paged_attention_impl(q, dtype, k_cache, v_cache, dtype, nullptr, nullptr, cache_seqlens, seqlens_dtype,
+                              nullptr, 0, batch * seq_len_q, num_heads, num_kv_heads, head_dim, (int)seq_len_k, batch,
+                              seq_len_k, softmax_scale, nullptr, nullptr, 0, 0, out, dtype, nullptr, nullptr, nullptr, 0,
+                              workspace, workspace_bytes, stream, seq_len_q, softmax_lse);
 }
 
 // ---------------------------------------------------------------------------------------------

@@ -287,6 +287,31 @@ def paged_attention_v2(query, key_cache, value_cache, seq_lens, block_table, par
                             out_dtype=output_dtype, v2=True)
 
 
+def flash_attn_with_kvcache(q, k_cache, v_cache, cache_seqlens, softmax_scale: Optional[float] = None):
+    """operators/attention/flash_attn_with_kvcache/flash_attn_with_kvcache.py:29-56 ->
+    (output [B, Sq, H, D] in q's dtype, softmax_lse [B, H, Sq] float32).
+
+    q [B, Sq, H, D]; caches [B, Sk, Hkv, D] of q's dtype; cache_seqlens [B]: every query token
+    of sequence b attends to its first cache_seqlens[b] keys."""
+    dev = _cuda(q, k_cache, v_cache, cache_seqlens)
+    b, sq, h, d = q.shape
+    sk, hkv = k_cache.shape[1], k_cache.shape[2]
+    if k_cache.shape != (b, sk, hkv, d) or v_cache.shape != k_cache.shape:
+        raise ValueError("flash_attn_with_kvcache: caches must be [batch, seq_len_k, heads, head_dim]")
+    if k_cache.dtype != q.dtype or v_cache.dtype != q.dtype:
+        raise ValueError("flash_attn_with_kvcache: q and the caches must share a dtype")
+    scale = d ** -0.5 if softmax_scale is None else softmax_scale
+    q, k_cache, v_cache = q.contiguous(), k_cache.contiguous(), v_cache.contiguous()
+    cache_seqlens = cache_seqlens.contiguous()
+    out = torch.empty((b, sq, h, d), dtype=q.dtype, device=dev)
+    lse = torch.empty((b, h, sq), dtype=torch.float32, device=dev)
+    ws = workspace(dev, _lib.lib().kvb_flash_attn_with_kvcache_workspace_size(b, sq, h, d, sk))
+    call("kvb_flash_attn_with_kvcache", _ptr(q), _ptr(k_cache), _ptr(v_cache), kvb_dtype(q.dtype), _ptr(cache_seqlens),
+         _index_dtype(cache_seqlens), b, sq, sk, h, hkv, d, float(scale), _ptr(out), _ptr(lse), _ptr(ws), ws.numel(),
+         _stream(dev))
+    return out, lse
+
+
 _FLASH_DECODE_INDEX = {}
 
 

@@ -19,6 +19,9 @@ The oracle, like the device kernels, takes caches as ``[num_blocks, bs, Hkv, D]`
   over a dense ``[B, L, Hkv, D]`` cache with a ``pos < seq_len`` mask.
 * ``paged_fp8_decode``: the BASELINE fourth config: the cache holds e4m3fn
   codes with per-KV-head float32 scales; values are ``code * scale[h]``.
+* ``flash_attn_with_kvcache``: ``operators/attention/flash_attn_with_kvcache/flash_attn_with_kvcache.py:29-56``
+  -- every query token of sequence b attends to its first ``cache_seqlens[b]`` keys of a
+  dense ``[B, Sk, H, D]`` cache; also the natural-log sum of exp of the scaled logits.
 * ``flash_decoding_attention``: ``operators/attention/flash_decoding_attention/flash_decoding_attention.py:30-87``
   over ``[B, H, S, D]`` caches in chunks of ``chunk_size`` keys, with the causal mask of
   ``:89-101`` (query i of Sq sees keys ``<= S - Sq + i``).
@@ -172,4 +175,27 @@ def flash_decoding_attention(query, key_cache, value_cache, chunk_size: int, cau
                 out[b, h, i] = (po[b, h, i] * w[:, None]).sum(0) / max(w.sum(), 1e-6)
     f = np.float32
     return out.astype(f), es.astype(f), mx.astype(f), po.astype(f)
+
+
+def flash_attn_with_kvcache(q, k_cache, v_cache, cache_seqlens, scale: float):
+    """Returns ``(output [B, Sq, H, D], softmax_lse [B, H, Sq])`` (flash_attn_with_kvcache.py:40-56);
+    query head h reads KV head ``h // (H / Hkv)``."""
+    qf = np.asarray(q, np.float64)
+    k = np.asarray(k_cache, np.float64)
+    v = np.asarray(v_cache, np.float64)
+    b_, sq, h_, d = qf.shape
+    grp = h_ // k.shape[2]
+    out = np.zeros((b_, sq, h_, d))
+    lse = np.zeros((b_, h_, sq))
+    for b in range(b_):
+        L = int(cache_seqlens[b])
+        for h in range(h_):
+            kk, vv = k[b, :L, h // grp], v[b, :L, h // grp]
+            for i in range(sq):
+                sc = (kk @ qf[b, i, h]) * scale
+                m = sc.max()
+                p = np.exp(sc - m)
+                out[b, i, h] = (p @ vv) / p.sum()
+                lse[b, h, i] = m + np.log(p.sum())
+    return out.astype(np.float32), lse.astype(np.float32)
 

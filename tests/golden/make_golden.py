@@ -301,6 +301,19 @@ def main():
         save(f"w8a8_act_{i}", {"M": m, "I": inner, "K": k, "act": act}, a=a, b_first=b1, b_second=b2, sa=sa,
              s_first=s1, s_second=s2, bias_first=bias1, bias_second=bias2, out=out)
 
+    # --- next rows: flash_attn_with_kvcache (reference op, correctness mode): ragged cache lengths,
+    #     several query tokens, and 32 heads (split over CTAs on the device)
+    for i, (b, sq, sk, h, d, pat, dt) in enumerate([(3, 1, 300, 4, 64, "ragged", "FP32"),
+                                                   (3, 4, 200, 2, 128, "ragged", "BF16"),
+                                                   (2, 8, 96, 32, 64, "full", "FP16"),
+                                                   (4, 2, 130, 32, 128, "ragged", "BF16")]):
+        shape = {"batch_size": b, "seq_len_q": sq, "seq_len_k": sk, "num_heads": h, "head_dim": d,
+                 "cache_pattern": pat, "dtype": dt}
+        qq, kk, vv, lens = gen_inputs("attention", "flash_attn_with_kvcache", shape, 1500 + i)
+        out, lse = run_model("attention", "flash_attn_with_kvcache", shape, (qq, kk, vv, lens))
+        save(f"flash_attn_with_kvcache_{i}", shape, q=qq, k_cache=kk, v_cache=vv, cache_seqlens=lens, out=out,
+             softmax_lse=lse)
+
     (HERE / "VERSIONS.txt").write_text(f"torch {torch.__version__}\nnumpy {np.__version__}\n")
 
 

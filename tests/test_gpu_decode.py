@@ -146,6 +146,9 @@ def oracle_fp8(case, fused=True):
     (3, 16, 2, 128, 8, [40, 7, 1], 0),
     (2, 32, 2, 64, 16, [2000, 1], 512),
     (2, 32, 1, 128, 1, [20, 5], 0),
+    # more (kv head, 8-query) tiles than 16 warps: KV heads split over CTAs
+    (2, 64, 32, 128, 16, [300, 77], 0),
+    (1, 256, 8, 64, 16, [70], 128),
 ])
 def test_fp8_decode_shapes(B, hq, hkv, D, bs, lens, part):
     case = make_fp8_case(seeded(B * 100 + hq + D + bs), B, hq, hkv, D, bs, lens)
@@ -290,3 +293,35 @@ def test_flash_decoding_shapes(dt, b, sq, s, h, d, chunk, causal):
     _close(host(po), r_po, tight)
     np.testing.assert_allclose(host(es), r_es, rtol=1e-5 if tight else 1e-2, atol=1e-5 if tight else 1e-2)
     assert np.array_equal(np.isneginf(host(ml)), np.isneginf(r_ml))
+
+
+@pytest.mark.parametrize("name", golden_names("flash_attn_with_kvcache"))
+def test_flash_attn_with_kvcache_golden(name):
+    meta, g = load_golden(name)
+    dt = {"FP32": torch.float32, "FP16": torch.float16, "BF16": torch.bfloat16}[meta["dtype"]]
+    out, lse = _ops().flash_attn_with_kvcache(dev(g["q"][0], dt), dev(g["k_cache"][0], dt), dev(g["v_cache"][0], dt),
+                                              dev(g["cache_seqlens"][0]))
+    tol = 5e-4 if dt == torch.float32 else (1e-2 if dt == torch.float16 else 1.5e-2)   # config.json
+    np.testing.assert_allclose(host(out), g["out"][0].astype(np.float32), rtol=tol, atol=tol)
+    np.testing.assert_allclose(host(lse), g["softmax_lse"][0], rtol=1e-4 if dt == torch.float32 else 2e-3,
+                               atol=1e-4 if dt == torch.float32 else 2e-3)
+
+
+@pytest.mark.parametrize("dt", ["FP32", "BF16", "FP16"])
+@pytest.mark.parametrize("b,sq,sk,h,hkv,d,ragged", [(4, 1, 2048, 16, 16, 128, False), (2, 16, 2048, 16, 16, 64, True),
+                                                    (8, 1, 4096, 32, 32, 128, True), (2, 32, 1000, 32, 8, 128, False),
+                                                    (3, 5, 333, 8, 2, 64, True)])
+def test_flash_attn_with_kvcache_shapes(dt, b, sq, sk, h, hkv, d, ragged):
+    """Query tokens per sequence, ragged lengths, GQA, and 32 KV heads (split over CTAs)."""
+    rng = seeded(b * 1000 + sq * 10 + h)
+    q = rng.standard_normal((b, sq, h, d)).astype(np.float32)
+    k = rng.standard_normal((b, sk, hkv, d)).astype(np.float32)
+    v = rng.standard_normal((b, sk, hkv, d)).astype(np.float32)
+    lens = (rng.integers(1, sk + 1, b) if ragged else np.full(b, sk)).astype(np.int32)
+    tdt = TORCH_DT[dt]
+    qt, kt, vt = dev(q, tdt), dev(k, tdt), dev(v, tdt)
+    out, lse = _ops().flash_attn_with_kvcache(qt, kt, vt, dev(lens))
+    r_out, r_lse = attention.flash_attn_with_kvcache(host(qt), host(kt), host(vt), lens, d ** -0.5)
+    _close(host(out), r_out, dt == "FP32")
+    np.testing.assert_allclose(host(lse), r_lse, rtol=1e-4, atol=1e-4 if dt == "FP32" else 2e-3)
+

@@ -169,3 +169,13 @@ def test_flash_decoding_attention(name):
         fin = np.isfinite(ref)
         assert np.array_equal(np.isfinite(host(got)), fin)
         np.testing.assert_allclose(host(got)[fin], ref[fin], rtol=tol["rtol"], atol=tol["atol"])
+
+
+@pytest.mark.parametrize("name", golden_names("flash_attn_with_kvcache"))
+def test_flash_attn_with_kvcache(name):
+    meta, g = load_golden(name)
+    out, lse = modelnew("flash_attn_with_kvcache", meta)(*(_as_dev(*g[k]) for k in ("q", "k_cache", "v_cache",
+                                                                                       "cache_seqlens")))
+    assert out.dtype == TORCH_DT[meta["dtype"]] and lse.dtype == torch.float32
+    _check(out, g["out"][0], "", TOL[meta["dtype"]])
+    _check(lse, g["softmax_lse"][0], "", TOL["FP32"] if meta["dtype"] == "FP32" else {"rtol": 2e-3, "atol": 2e-3})

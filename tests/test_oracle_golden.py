@@ -159,3 +159,13 @@ def test_w8a8_act(name):
     # numpy's and torch's float32 exp may differ in the last bit, which can move a bf16 rounding
     np.testing.assert_allclose(out, ref, rtol=8e-3, atol=1e-6)
     assert np.mean(out == ref) > 0.99
+
+
+@pytest.mark.parametrize("name", golden_names("flash_attn_with_kvcache"))
+def test_flash_attn_with_kvcache(name):
+    meta, g = load_golden(name)
+    out, lse = attention.flash_attn_with_kvcache(g["q"][0], g["k_cache"][0], g["v_cache"][0], g["cache_seqlens"][0],
+                                                 meta["head_dim"] ** -0.5)
+    tol = {"FP32": 2e-5, "FP16": 2e-3, "BF16": 1.6e-2}[meta["dtype"]]
+    np.testing.assert_allclose(out, g["out"][0], rtol=tol, atol=tol)
+    np.testing.assert_allclose(lse, g["softmax_lse"][0], rtol=2e-5, atol=2e-5)
