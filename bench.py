@@ -647,7 +647,7 @@ def main():
                          "frac": round(achieved_gbs / hbm_peak, 4), "traffic": traffic,
                          "peak_source": f"{peak_kind} (MEASURED_PEAKS.json hbm_gbs)" if peak_kind == "measured"
                          else "fallback 6.65 TB/s", "algorithmic_bytes_per_launch": per_step_bytes,
-                         "kernel": "add_rmsnorm_pipe_kernel<bf16,2,e4m3>"},
+                         "kernel": "add_rmsnorm_pipe_kernel<bf16,4,e4m3> (256 threads x 4 vectors per row)"},
             "e2e": {"value": round(e2e_tbs, 5), "unit": "TB/s", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
                     "ms_per_step": round(e2e_ms / e2e_steps, 4), "steps": e2e_steps,
                     "path": "kernelverse_b200.ops.add_rmsnorm_quant with pinned host buffers"},

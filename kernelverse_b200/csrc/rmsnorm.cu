@@ -413,7 +413,10 @@ int launch(const void* xv, const void* rv, const void* wv, int64_t rows, int64_t
   if (vec && hidden / 8 >= 256 && row_bytes <= 24 * 1024) {
     const int64_t nvec = hidden / 8;
     if (nvec <= 512) return launch_pipe<T, 1, MODE>(x, r, w, rows, nvec, eps, out, codes, scales, st);
-    if (nvec <= 1024) return launch_pipe<T, 2, MODE>(x, r, w, rows, nvec, eps, out, codes, scales, st);
+    // Up to 1024 vectors: 4 per thread (256 threads) rather than 2 (512): the per-row work every
+    // thread repeats (two reductions, the rsqrt, the scale and its reciprocal) is amortised
+    // over twice the elements -- 83.9 -> 82.5 us at [8192, 8192].
+    if (nvec <= 1024) return launch_pipe<T, 4, MODE>(x, r, w, rows, nvec, eps, out, codes, scales, st);
     return launch_pipe<T, 3, MODE>(x, r, w, rows, nvec, eps, out, codes, scales, st);
   }
   if (vec) {
