@@ -255,36 +255,55 @@ __device__ __forceinline__ ColVals load_cols(const GemmArgs& g, int n0, int lane
 }
 
 // Scale / bias 32 accumulator columns (operands in c) into float32 values.  All 32 lanes must
-// be converged.
-__device__ __forceinline__ void epi_values(const GemmArgs& g, const uint32_t (&r)[32], const ColVals& c, float sa,
-                                           int32_t rs, float (&f)[32]) {
+// be converged.  The optional operands are template flags: a per-column test around the
+// shuffles (convergent operations, which the compiler does not hoist) cost a uniform branch
+// per column and made one call ~3000 cycles.
+template <bool kAzp, bool kAdj, bool kBias>
+__device__ __forceinline__ void epi_values_t(const uint32_t (&r)[32], const ColVals& c, float sa, int32_t rs,
+                                             float (&f)[32]) {
   constexpr unsigned kAll = 0xffffffffu;
 #pragma unroll
   for (int j = 0; j < 32; ++j) {
     int32_t acc = (int32_t)r[j];
-    if (g.azp) acc -= (int32_t)__shfl_sync(kAll, c.azp, j) * rs;
+    if constexpr (kAzp) acc -= (int32_t)__shfl_sync(kAll, c.azp, j) * rs;
     float y = __fmul_rn(__fmul_rn((float)acc, sa), __shfl_sync(kAll, c.sb, j));
-    if (g.azp_adj) y = __fadd_rn(y, __shfl_sync(kAll, c.adj, j));
-    if (g.bias) y = __fadd_rn(y, __shfl_sync(kAll, c.bias, j));
+    if constexpr (kAdj) y = __fadd_rn(y, __shfl_sync(kAll, c.adj, j));
+    if constexpr (kBias) y = __fadd_rn(y, __shfl_sync(kAll, c.bias, j));
     f[j] = y;
   }
 }
+__device__ __forceinline__ void epi_values(const GemmArgs& g, const uint32_t (&r)[32], const ColVals& c, float sa,
+                                           int32_t rs, float (&f)[32]) {
+  const int mask = (g.azp ? 4 : 0) | (g.azp_adj ? 2 : 0) | (g.bias ? 1 : 0);
+  switch (mask) {
+    case 0: epi_values_t<false, false, false>(r, c, sa, rs, f); break;
+    case 1: epi_values_t<false, false, true>(r, c, sa, rs, f); break;
+    case 2: epi_values_t<false, true, false>(r, c, sa, rs, f); break;
+    case 3: epi_values_t<false, true, true>(r, c, sa, rs, f); break;
+    case 4: epi_values_t<true, false, false>(r, c, sa, rs, f); break;
+    case 5: epi_values_t<true, false, true>(r, c, sa, rs, f); break;
+    case 6: epi_values_t<true, true, false>(r, c, sa, rs, f); break;
+    default: epi_values_t<true, true, true>(r, c, sa, rs, f); break;
+  }
+}
 
-// Output words of 32 float32 values: 32 words for float32 outputs, 16 packed pairs for 16-bit.
+// Output words of 32 float32 values: 32 words for float32 outputs, 16 packed pairs for 16-bit
+// (one branch on the type, outside the loops).
 __device__ __forceinline__ void pack_out(const GemmArgs& g, const float (&f)[32], uint32_t* w) {
   if (g.out_dtype == KVB_F32) {
 #pragma unroll
     for (int j = 0; j < 32; ++j) w[j] = __float_as_uint(f[j]);
+  } else if (g.out_dtype == KVB_BF16) {
+#pragma unroll
+    for (int j = 0; j < 16; ++j) {
+      __nv_bfloat162 h = __floats2bfloat162_rn(f[2 * j], f[2 * j + 1]);
+      w[j] = *reinterpret_cast<uint32_t*>(&h);
+    }
   } else {
 #pragma unroll
     for (int j = 0; j < 16; ++j) {
-      if (g.out_dtype == KVB_BF16) {
-        __nv_bfloat162 h = __floats2bfloat162_rn(f[2 * j], f[2 * j + 1]);
-        w[j] = *reinterpret_cast<uint32_t*>(&h);
-      } else {
-        __half2 h = __floats2half2_rn(f[2 * j], f[2 * j + 1]);
-        w[j] = *reinterpret_cast<uint32_t*>(&h);
-      }
+      __half2 h = __floats2half2_rn(f[2 * j], f[2 * j + 1]);
+      w[j] = *reinterpret_cast<uint32_t*>(&h);
     }
   }
 }
@@ -324,11 +343,14 @@ __device__ __forceinline__ float2 pick4(const float2 (&v)[4], int k) {   // v[k]
 __device__ __forceinline__ void act_values(const GemmArgs& g, const uint32_t (&r)[32], float2 c, float sa,
                                            float (&f)[32]) {
   constexpr unsigned kAll = 0xffffffffu;
+  if (g.bias) {   // one branch outside the loop (the shuffles are convergent)
 #pragma unroll
-  for (int j = 0; j < 32; ++j) {
-    float y = __fmul_rn(__fmul_rn((float)(int32_t)r[j], sa), __shfl_sync(kAll, c.x, j));
-    if (g.bias) y = __fadd_rn(y, __shfl_sync(kAll, c.y, j));
-    f[j] = y;
+    for (int j = 0; j < 32; ++j)
+      f[j] = __fadd_rn(__fmul_rn(__fmul_rn((float)(int32_t)r[j], sa), __shfl_sync(kAll, c.x, j)),
+                       __shfl_sync(kAll, c.y, j));
+  } else {
+#pragma unroll
+    for (int j = 0; j < 32; ++j) f[j] = __fmul_rn(__fmul_rn((float)(int32_t)r[j], sa), __shfl_sync(kAll, c.x, j));
   }
 }
 
