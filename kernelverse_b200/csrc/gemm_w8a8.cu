@@ -10,7 +10,8 @@
 //
 // Structure: a persistent, warp-specialised kernel; 128 x BN tiles on one SM, or 256 x BN tiles
 // on a CTA pair (cluster of 2, tcgen05 cta_group::2: each CTA loads its 128 rows of A and BN/2
-// rows of B and the pair leader issues the MMAs for both).
+// rows of B and the pair leader issues the MMAs for both); with NSUB = 2 a tile is two such
+// N = BN sub-tiles sharing the A tile.
 //   warp 0: TMA producer -- A [128 x 128 B] and B [rows x 128 B] K-major boxes with 128-byte
 //           swizzle into a STAGES-deep shared-memory ring (mbarrier complete_tx);
 //   warp 1: allocates 2 x BN TMEM columns (double-buffered accumulator) and one lane issues
@@ -356,19 +357,25 @@ __device__ __forceinline__ void act_values(const GemmArgs& g, const uint32_t (&r
 
 // k2Sm: CTA pairs (cluster of 2) compute 256 x BN tiles with cta_group::2 MMAs; each CTA loads
 // its 128 rows of A and BN/2 rows of B, so a k-block moves 32 KB per SM instead of 48 KB.
-template <int BN, int STAGES, bool kTmaStore, bool k2Sm>
+// NSUB = 2: a tile is two N = BN MMA sub-tiles sharing the A tile (2 x 256 = 512 columns, the
+// whole TMEM, so one accumulator buffer); a k-block then moves 48 KB per SM for twice the MACs.
+template <int BN, int STAGES, bool kTmaStore, bool k2Sm, int NSUB = 1>
 __global__ void __launch_bounds__(kThreads, 1) w8a8_gemm_kernel(const __grid_constant__ CUtensorMap tmap_a,
                                                                  const __grid_constant__ CUtensorMap tmap_b,
                                                                  const __grid_constant__ GemmArgs g,
                                                                  const __grid_constant__ OutMaps om) {
   constexpr int kTileM = k2Sm ? 2 * kBM : kBM;
-  constexpr int kBRows = k2Sm ? BN / 2 : BN;
+  constexpr int TN = BN * NSUB;                 // tile columns
+  constexpr int kNBuf = NSUB == 1 ? 2 : 1;      // accumulator buffers in TMEM
+  constexpr int kBRows = k2Sm ? BN / 2 : BN;    // B rows this CTA loads per sub-tile
   constexpr uint32_t kABytes = kBM * kBK;
-  constexpr uint32_t kBBytes = kBRows * kBK;
+  constexpr uint32_t kBBytes = NSUB * kBRows * kBK;
   constexpr uint32_t kStageBytes = kABytes + kBBytes;
   static_assert(!k2Sm || BN % 32 == 0, "cta_group::2 kind::i8 needs N % 32 == 0");
-  // two accumulator buffers of BN columns; the allocation is a power of two >= 32
-  constexpr uint32_t kTmemCols = 2 * BN <= 32 ? 32 : 2 * BN <= 64 ? 64 : 2 * BN <= 128 ? 128 : 2 * BN <= 256 ? 256 : 512;
+  // kNBuf accumulator buffers of TN columns; the allocation is a power of two >= 32
+  constexpr int kAcc = kNBuf * TN;
+  static_assert(kAcc <= 512, "TMEM holds 512 columns");
+  constexpr uint32_t kTmemCols = kAcc <= 32 ? 32 : kAcc <= 64 ? 64 : kAcc <= 128 ? 128 : kAcc <= 256 ? 256 : 512;
   static_assert(BN % 16 == 0 && BN >= 16 && BN <= 256, "tcgen05 kind::i8 with M=128 needs N % 16 == 0, N <= 256");
   constexpr uint32_t kIdesc = idesc_i8(kTileM, BN);
 
@@ -389,7 +396,7 @@ __global__ void __launch_bounds__(kThreads, 1) w8a8_gemm_kernel(const __grid_con
       mbar_init(&full[s], 1);
       mbar_init(&empty[s], 1);
     }
-    for (int j = 0; j < 2; ++j) {
+    for (int j = 0; j < kNBuf; ++j) {
       mbar_init(&tmem_full[j], 1);
       mbar_init(&tmem_empty[j], k2Sm ? 2 * kEpiWarps : kEpiWarps);   // every epilogue warp of the pair releases it
     }
@@ -422,7 +429,7 @@ __global__ void __launch_bounds__(kThreads, 1) w8a8_gemm_kernel(const __grid_con
       for (int t = tile0; t < g.tiles && ok; t += tstride) {
         int mb, nb;
         tile_coords(g, t, mb, nb);
-        const int ya = mb * kTileM + (int)crank * kBM, yb = nb * BN + (int)crank * kBRows;
+        const int ya = mb * kTileM + (int)crank * kBM, yb = nb * TN + (int)crank * kBRows;
         for (int kb = 0; kb < KB; ++kb, ++it) {
           const int s = it % STAGES;
           const uint32_t use = it / STAGES;
@@ -436,11 +443,15 @@ __global__ void __launch_bounds__(kThreads, 1) w8a8_gemm_kernel(const __grid_con
             const uint32_t bar = mapa_shared(smem_u32(&full[s]), 0);
             if (leader) mbar_arrive_expect_tx(&full[s], 2 * kStageBytes);
             tma_load_2d_pair(sa_, &tmap_a, kb * kBK, ya, bar, pol_a);
-            tma_load_2d_pair(sa_ + kABytes, &tmap_b, kb * kBK, yb, bar, pol_b);
+#pragma unroll
+            for (int n = 0; n < NSUB; ++n)   // sub-tile n: this CTA's kBRows rows of columns [n BN, n BN + BN)
+              tma_load_2d_pair(sa_ + kABytes + n * kBRows * kBK, &tmap_b, kb * kBK, yb + n * BN, bar, pol_b);
           } else {
             mbar_arrive_expect_tx(&full[s], kStageBytes);
             tma_load_2d(sa_, &tmap_a, kb * kBK, ya, &full[s], pol_a);
-            tma_load_2d(sa_ + kABytes, &tmap_b, kb * kBK, yb, &full[s], pol_b);
+#pragma unroll
+            for (int n = 0; n < NSUB; ++n)
+              tma_load_2d(sa_ + kABytes + n * kBRows * kBK, &tmap_b, kb * kBK, yb + n * BN, &full[s], pol_b);
           }
         }
       }
@@ -454,13 +465,13 @@ __global__ void __launch_bounds__(kThreads, 1) w8a8_gemm_kernel(const __grid_con
       uint32_t it = 0, local = 0;
       bool ok = true;
       for (int t = tile0; t < g.tiles && ok; t += tstride, ++local) {
-        const uint32_t ab = local & 1u, v = local >> 1;
+        const uint32_t ab = kNBuf == 2 ? (local & 1u) : 0u, v = kNBuf == 2 ? (local >> 1) : local;
         if (v > 0 && !mbar_wait_bounded(&tmem_empty[ab], (v - 1) & 1u)) {
           ok = false;
           break;
         }
         tc_fence_after();
-        const uint32_t d_tmem = tmem_base + ab * BN;
+        const uint32_t d_tmem = tmem_base + ab * TN;
         for (int kb = 0; kb < KB; ++kb, ++it) {
           const int s = it % STAGES;
           if (!mbar_wait_bounded(&full[s], (it / STAGES) & 1u)) {
@@ -471,9 +482,13 @@ __global__ void __launch_bounds__(kThreads, 1) w8a8_gemm_kernel(const __grid_con
           const uint8_t* b_s = a_s + kABytes;
 #pragma unroll
           for (int kk = 0; kk < kBK / kUmmaK; ++kk) {
-            const uint64_t ad = smem_desc_k128(a_s + kk * kUmmaK), bd = smem_desc_k128(b_s + kk * kUmmaK);
-            if constexpr (k2Sm) mma_i8_pair(d_tmem, ad, bd, kIdesc, (kb | kk) != 0);
-            else mma_i8(d_tmem, ad, bd, kIdesc, (kb | kk) != 0);
+            const uint64_t ad = smem_desc_k128(a_s + kk * kUmmaK);
+#pragma unroll
+            for (int n = 0; n < NSUB; ++n) {   // sub-tile n -> accumulator columns [n BN, n BN + BN)
+              const uint64_t bd = smem_desc_k128(b_s + n * kBRows * kBK + kk * kUmmaK);
+              if constexpr (k2Sm) mma_i8_pair(d_tmem + n * BN, ad, bd, kIdesc, (kb | kk) != 0);
+              else mma_i8(d_tmem + n * BN, ad, bd, kIdesc, (kb | kk) != 0);
+            }
           }
           // stage s is free (in both CTAs) once these MMAs have read it
           if constexpr (k2Sm) mma_commit_pair(&empty[s]);
@@ -503,7 +518,7 @@ __global__ void __launch_bounds__(kThreads, 1) w8a8_gemm_kernel(const __grid_con
     uint8_t* stage_buf = smem + (size_t)STAGES * kStageBytes + (size_t)ew * 4096;
     uint32_t local = 0;
     for (int t = tile0; t < g.tiles; t += tstride, ++local) {
-      const uint32_t ab = local & 1u, v = local >> 1;
+      const uint32_t ab = kNBuf == 2 ? (local & 1u) : 0u, v = kNBuf == 2 ? (local >> 1) : local;
       // The row and first-chunk column operands are loaded before the accumulator is ready.
       int mb, nb;
       tile_coords(g, t, mb, nb);
@@ -512,19 +527,19 @@ __global__ void __launch_bounds__(kThreads, 1) w8a8_gemm_kernel(const __grid_con
       const bool mrow = m < g.M;
       const float sa = (mrow && g.sa) ? g.sa[m] : 0.0f;   // no scales in int32-accumulator mode
       const int32_t rs = (g.azp && mrow) ? g.rowsum[m] : 0;
-      const int OC = g.act ? BN / 2 : BN;   // output columns of a tile
-      const uint32_t tm = tmem_base + ((uint32_t)(q * 32) << 16) + ab * BN;   // this warp's accumulator
+      const int OC = g.act ? TN / 2 : TN;   // output columns of a tile (gated: NSUB == 1)
+      const uint32_t tm = tmem_base + ((uint32_t)(q * 32) << 16) + ab * TN;   // this warp's accumulator
       ColVals cv0{0.0f, 0.0f, 0.0f, 0.0f}, cv1{0.0f, 0.0f, 0.0f, 0.0f};
       float2 af[4], as[4];                  // gated: the 4 x 32 columns of each operand (OC = 128)
       if (g.act) {
 #pragma unroll
         for (int k = 0; k < 4; ++k) {
-          af[k] = load_sb_bias(g, nb * BN + 32 * k, lane);
-          as[k] = load_sb_bias(g, nb * BN + OC + 32 * k, lane);
+          af[k] = load_sb_bias(g, nb * TN + 32 * k, lane);
+          as[k] = load_sb_bias(g, nb * TN + OC + 32 * k, lane);
         }
       } else {
-        cv0 = load_cols(g, nb * BN + half * CW, lane);
-        if (esize == 2 && half * CW + 32 < BN) cv1 = load_cols(g, nb * BN + half * CW + 32, lane);
+        cv0 = load_cols(g, nb * TN + half * CW, lane);
+        if (esize == 2 && half * CW + 32 < TN) cv1 = load_cols(g, nb * TN + half * CW + 32, lane);
       }
       if (!mbar_wait_bounded(&tmem_full[ab], v & 1u)) break;
       tc_fence_after();
@@ -554,17 +569,17 @@ __global__ void __launch_bounds__(kThreads, 1) w8a8_gemm_kernel(const __grid_con
             pack_out(g, fa, w + 16 * h);    // h > 0 only for 16-bit outputs (16 words per 32 columns)
           }
         } else {
-          const int n0 = nb * BN + c0;
+          const int n0 = nb * TN + c0;
           const ColVals cur0 = cv0, cur1 = cv1;
-          if (c0 + 2 * CW < BN) {           // prefetch this warp's next chunk's column operands
+          if (c0 + 2 * CW < TN) {           // prefetch this warp's next chunk's column operands
             cv0 = load_cols(g, n0 + 2 * CW, lane);
-            if (esize == 2 && c0 + 2 * CW + 32 < BN) cv1 = load_cols(g, n0 + 2 * CW + 32, lane);
+            if (esize == 2 && c0 + 2 * CW + 32 < TN) cv1 = load_cols(g, n0 + 2 * CW + 32, lane);
           }
           uint32_t r[32];
           __syncwarp();                     // tcgen05.ld is .sync.aligned: reconverge first
           tmem_ld32(tm + c0, r);
           epilogue32(g, r, cur0, sa, rs, w);
-          if (esize == 2 && c0 + 32 < BN) {
+          if (esize == 2 && c0 + 32 < TN) {
             __syncwarp();
             tmem_ld32(tm + c0 + 32, r);
             epilogue32(g, r, cur1, sa, rs, w + 16);
@@ -740,7 +755,7 @@ bool tma_store_ok(const GemmArgs& g, void* const* dests, int ndest, int64_t map_
   return true;
 }
 
-template <int BN, int STAGES, bool kTmaStore, bool k2Sm>
+template <int BN, int STAGES, bool kTmaStore, bool k2Sm, int NSUB = 1>
 int launch_gemm(const int8_t* a, const int8_t* b_nk, GemmArgs& g, void* const* dests, int ndest, int64_t map_cols,
                 cudaStream_t st) {
   constexpr int kTileM = k2Sm ? 2 * kBM : kBM;
@@ -751,7 +766,7 @@ int launch_gemm(const int8_t* a, const int8_t* b_nk, GemmArgs& g, void* const* d
   rc = make_map(&mb, b_nk, g.N, g.K, kBRows);
   if (rc) return rc;
   g.m_blocks = (g.M + kTileM - 1) / kTileM;
-  g.n_blocks = (g.N + BN - 1) / BN;
+  g.n_blocks = (g.N + BN * NSUB - 1) / (BN * NSUB);
   g.tiles = g.m_blocks * g.n_blocks;
   OutMaps om;
   memset(&om, 0, sizeof(om));
@@ -762,8 +777,8 @@ int launch_gemm(const int8_t* a, const int8_t* b_nk, GemmArgs& g, void* const* d
     if (rc) return rc;
   }
   constexpr size_t kStaging = kTmaStore ? kEpiWarps * 4096 : 0;   // one [32 rows x 128 B] buffer per epilogue warp
-  const size_t smem = (size_t)STAGES * (kBM * kBK + kBRows * kBK) + kStaging + 1024;
-  auto kern = w8a8_gemm_kernel<BN, STAGES, kTmaStore, k2Sm>;
+  const size_t smem = (size_t)STAGES * (kBM * kBK + NSUB * kBRows * kBK) + kStaging + 1024;
+  auto kern = w8a8_gemm_kernel<BN, STAGES, kTmaStore, k2Sm, NSUB>;
   static int set_dev = -1;
   int dev = 0;
   cudaGetDevice(&dev);
@@ -898,9 +913,13 @@ extern "C" int kvb_w8a8_scaled_mm(const int8_t* a, const int8_t* b, int b_layout
     g.rowsum = rs;
   }
   // M <= 128 streams B from HBM: 208-column tiles make N = 28672 exactly 138 tiles (one wave on
-  // 148 SMs).  Larger M: CTA pairs with 256 x 256 tiles (half the B bytes per SM per k-block).
+  // 148 SMs).  M <= 256: CTA pairs with 256 x 512 tiles (two N = 256 MMAs per k-step sharing A:
+  // 56 tiles for N = 28672, one wave; 58.2 vs 60.0 us at M = 256).  Larger M: CTA pairs with
+  // 256 x 256 tiles and a double-buffered accumulator, so each tile's epilogue overlaps the next
+  // tile's main loop (the single-buffered 512-column tiles lose 5-15 % there).
   void* dests[1] = {out};
   if (M <= 128) return launch_gemm<208, 5, false, false>(a, b_nk, g, dests, 1, N, st);
+  if (M <= 256) return launch_gemm<256, 4, false, true, 2>(a, b_nk, g, dests, 1, N, st);
   return launch_gemm<256, 6, false, true>(a, b_nk, g, dests, 1, N, st);
 }
 
