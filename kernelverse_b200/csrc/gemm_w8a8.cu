@@ -417,6 +417,11 @@ __global__ void __launch_bounds__(kThreads, 1) w8a8_gemm_kernel(const __grid_con
   }
   tc_fence_after();
   const uint32_t tmem_base = tmem_base_s;
+  // Launched as a programmatic dependent of the previous kernel in the stream: everything above
+  // (barriers, TMEM, descriptor prefetch) overlaps that kernel's tail; nothing global is read or
+  // written before it has completed.  Kernels after this one may be scheduled as SMs free up.
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+  asm volatile("griddepcontrol.launch_dependents;");
 
   if (warp == 0) {
     // ------------------------------------------------------------ TMA producer
@@ -790,23 +795,35 @@ int launch_gemm(const int8_t* a, const int8_t* b_nk, GemmArgs& g, void* const* d
   if constexpr (k2Sm) {
     // CTA pairs: a cluster of 2 along x, one pair per two SMs
     cudaLaunchConfig_t cfg = {};
-    cudaLaunchAttribute attr[1];
+    cudaLaunchAttribute attr[2];
     attr[0].id = cudaLaunchAttributeClusterDimension;
     attr[0].val.clusterDim.x = 2;
     attr[0].val.clusterDim.y = 1;
     attr[0].val.clusterDim.z = 1;
+    attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;   // see griddepcontrol in the kernel
+    attr[1].val.programmaticStreamSerializationAllowed = 1;
     cfg.gridDim = dim3(2u * (unsigned)std::min(g.tiles, num_sms() / 2));
+    cfg.blockDim = dim3(kThreads);
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = st;
+    cfg.attrs = attr;
+    cfg.numAttrs = 2;
+    cudaError_t e = cudaLaunchKernelEx(&cfg, kern, ma, mb, g, om);
+    if (e != cudaSuccess) return set_error(KVB_E_LAUNCH, "w8a8_gemm_kernel (pairs): %s", cudaGetErrorString(e));
+    return check_launch("w8a8_gemm_kernel");
+  } else {
+    cudaLaunchConfig_t cfg = {};
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;   // see griddepcontrol in the kernel
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.gridDim = dim3((unsigned)std::min(g.tiles, num_sms()));
     cfg.blockDim = dim3(kThreads);
     cfg.dynamicSmemBytes = smem;
     cfg.stream = st;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
     cudaError_t e = cudaLaunchKernelEx(&cfg, kern, ma, mb, g, om);
-    if (e != cudaSuccess) return set_error(KVB_E_LAUNCH, "w8a8_gemm_kernel (pairs): %s", cudaGetErrorString(e));
-    return check_launch("w8a8_gemm_kernel");
-  } else {
-    const int grid = std::min(g.tiles, num_sms());
-    kern<<<grid, kThreads, smem, st>>>(ma, mb, g, om);
+    if (e != cudaSuccess) return set_error(KVB_E_LAUNCH, "w8a8_gemm_kernel: %s", cudaGetErrorString(e));
     return check_launch("w8a8_gemm_kernel");
   }
 }
