@@ -6,6 +6,7 @@
 #include <cuda_fp16.h>
 #include <cuda_fp8.h>
 #include <stdint.h>
+#include <utility>
 
 #include "../../include/kvb.h"
 
@@ -174,6 +175,29 @@ __device__ __forceinline__ float block_reduce_1bar(float v, float* buf) {
   __syncthreads();
   float r = lane < nwarps ? buf[lane] : 0.0f;
   return kMax ? warp_max_redux(r) : warp_sum(r);
+}
+
+// ------------------------------------------------------------------ programmatic dependent launch
+// A kernel launched with launch_pdl may start (and run its set-up) while the previous kernel in
+// the stream finishes; pdl_wait() returns once that kernel has completed and its memory is
+// visible, so everything global is read or written after it.  pdl_trigger() lets the next such
+// kernel be scheduled as SMs free up.  Both return at once without a dependent launch.
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;"); }
+
+template <typename... KArgs, typename... Args>
+cudaError_t launch_pdl(void (*kern)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t st, Args&&... args) {
+  cudaLaunchConfig_t cfg = {};
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, kern, std::forward<Args>(args)...);
 }
 
 // ------------------------------------------------------------------ quantisation primitives

@@ -179,6 +179,8 @@ __global__ void __launch_bounds__(kMaxThreads, kMinBlocks)
     group_quant_rowblock_kernel(const T* __restrict__ x, int group_vecs, float eps, int8_t* __restrict__ q,
                                 float* __restrict__ scales) {
   __shared__ float scratch[32];
+  pdl_trigger();
+  pdl_wait();            // launched as a programmatic dependent (launch_pdl)
   const int64_t g = blockIdx.x;
   const T* xg = x + g * group_vecs * 8;
   Vec8<T> a[VPT];
@@ -265,10 +267,14 @@ int launch_rowblock(const T* x, int64_t ngroups, int64_t gvec, float eps, int8_t
   int threads = (int)((gvec + VPT - 1) / VPT);
   threads = ((threads + 31) / 32) * 32;
   if (threads > 1024) return set_error(KVB_E_SHAPE, "group too large for the register-resident path");
+  cudaError_t e;
   if (threads <= 128)
-    group_quant_rowblock_kernel<T, VPT, 128, 16><<<(unsigned)ngroups, threads, 0, st>>>(x, (int)gvec, eps, q, scales);
+    e = launch_pdl(group_quant_rowblock_kernel<T, VPT, 128, 16>, dim3((unsigned)ngroups), dim3(threads), 0, st, x,
+                   (int)gvec, eps, q, scales);
   else
-    group_quant_rowblock_kernel<T, VPT, 1024, 1><<<(unsigned)ngroups, threads, 0, st>>>(x, (int)gvec, eps, q, scales);
+    e = launch_pdl(group_quant_rowblock_kernel<T, VPT, 1024, 1>, dim3((unsigned)ngroups), dim3(threads), 0, st, x,
+                   (int)gvec, eps, q, scales);
+  if (e != cudaSuccess) return set_error(KVB_E_LAUNCH, "group_quant_rowblock_kernel: %s", cudaGetErrorString(e));
   return check_launch("group_quant_rowblock_kernel");
 }
 

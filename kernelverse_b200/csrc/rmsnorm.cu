@@ -229,6 +229,8 @@ __global__ void __launch_bounds__(512) add_rmsnorm_pipe_kernel(const T* __restri
     fence_mbar_init();
   }
   __syncthreads();
+  pdl_trigger();
+  pdl_wait();            // launched as a programmatic dependent (launch_pdl): global data from here on
   const uint64_t pol = policy_evict_first();
   if (tid == 0) {
 #pragma unroll
@@ -380,7 +382,9 @@ int launch_pipe(const T* x, const T* r, const T* w, int64_t rows, int64_t nvec, 
   int sms = 0;
   cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
   const int64_t grid = std::min<int64_t>(rows, (int64_t)cached_blocks * sms);
-  kern<<<(unsigned)grid, threads, smem, st>>>(x, r, w, rows, (int)nvec, (float)(nvec * 8), eps, out, codes, scales);
+  cudaError_t e = launch_pdl(kern, dim3((unsigned)grid), dim3(threads), smem, st, x, r, w, rows, (int)nvec,
+                             (float)(nvec * 8), eps, out, codes, scales);
+  if (e != cudaSuccess) return set_error(KVB_E_LAUNCH, "add_rmsnorm_pipe_kernel: %s", cudaGetErrorString(e));
   return check_launch("add_rmsnorm_pipe_kernel");
 }
 
