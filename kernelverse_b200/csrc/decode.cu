@@ -172,13 +172,23 @@ __global__ void __launch_bounds__(MAXT, MAXT <= 288 ? 2 : 1) paged_decode_kernel
   extern __shared__ __align__(128) uint8_t smem[];
   __shared__ uint64_t full[kStagesMax], empty[kStagesMax];
 
-  // The merge grid (a programmatic dependent) may be scheduled once every CTA of this grid has
-  // started; it waits for this grid's completion before reading anything this grid writes.
-  asm volatile("griddepcontrol.launch_dependents;");
   const int p = blockIdx.x, b = blockIdx.y;
   const int h0 = blockIdx.z * a.hc;                  // first KV head of this CTA
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int ncons = a.hc * a.tiles_per_kv;           // consumer warps; warp ncons is the producer
+  const int S = a.stages;
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < S; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], ncons);
+    }
+    fence_mbar_init();
+  }
+  __syncthreads();
+  // Launched as a programmatic dependent: everything above overlaps the previous grid's tail and
+  // nothing global is touched before pdl_wait().  The merge grid may be scheduled from then on.
+  pdl_wait();
+  pdl_trigger();
   const int64_t L = seq_len_of(a, b);
   const int64_t t_begin = (int64_t)p * a.part;
   const int64_t t_end = (L < t_begin + a.part ? L : t_begin + a.part);
@@ -205,18 +215,8 @@ __global__ void __launch_bounds__(MAXT, MAXT <= 288 ? 2 : 1) paged_decode_kernel
   const uint32_t srow = (uint32_t)(a.hc * D * EB);         // its slice of this CTA's heads, as staged
   const uint32_t head_off = (uint32_t)(h0 * D * EB);
   const uint32_t chunk_bytes = kChunk * srow;
-  const int S = a.stages;
   auto kstage = [&](int s) { return smem + (size_t)s * 2 * chunk_bytes; };
   auto vstage = [&](int s) { return smem + (size_t)s * 2 * chunk_bytes + chunk_bytes; };
-
-  if (threadIdx.x == 0) {
-    for (int s = 0; s < S; ++s) {
-      mbar_init(&full[s], 1);
-      mbar_init(&empty[s], ncons);
-    }
-    fence_mbar_init();
-  }
-  __syncthreads();
 
   // ------------------------------------------------------------------ producer warp
   if (warp == ncons) {
@@ -597,12 +597,15 @@ __global__ void __launch_bounds__(128) decode_merge_kernel(const float* __restri
   extern __shared__ float wgt[];        // [pmax]
   __shared__ float red[32];
   const int bh = blockIdx.x, b = bh / hq, sq = b / qtok;
+  // Launched as a programmatic dependent of the decode grid: wait until that grid has
+  // completed and its partials are visible (returns at once without a prerequisite grid).
+  // (Triggering the next grid after the wait rather than at entry measured faster in
+  // back-to-back decode steps.)
+  pdl_wait();
+  pdl_trigger();
   const int64_t L = sl64 ? reinterpret_cast<const int64_t*>(seq_lens)[sq] : (int64_t)reinterpret_cast<const int32_t*>(seq_lens)[sq];
   const int64_t npl = (L + part - 1) / part;
   const int np = (int)(npl < pmax ? npl : pmax);
-  // Launched as a programmatic dependent of the decode grid: wait until that grid has
-  // completed and its partials are visible (returns at once without a prerequisite grid).
-  asm volatile("griddepcontrol.wait;" ::: "memory");
   const float* mp = m_part + (int64_t)bh * pmax;
   const float* lp = l_part + (int64_t)bh * pmax;
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nwarps = blockDim.x >> 5;
@@ -665,7 +668,8 @@ int launch_decode_t(DecodeArgs& a, size_t smem, cudaStream_t st) {
   }
   const int threads = (a.hc * a.tiles_per_kv + 1) * 32;
   dim3 grid(a.pmax, a.batch, a.hkv / a.hc);
-  kern<<<grid, threads, smem, st>>>(a);
+  cudaError_t e = launch_pdl(kern, grid, dim3(threads), smem, st, a);
+  if (e != cudaSuccess) return set_error(KVB_E_LAUNCH, "paged_decode_kernel: %s", cudaGetErrorString(e));
   return check_launch("paged_decode_kernel");
 }
 

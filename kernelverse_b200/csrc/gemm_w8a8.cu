@@ -420,8 +420,8 @@ __global__ void __launch_bounds__(kThreads, 1) w8a8_gemm_kernel(const __grid_con
   // Launched as a programmatic dependent of the previous kernel in the stream: everything above
   // (barriers, TMEM, descriptor prefetch) overlaps that kernel's tail; nothing global is read or
   // written before it has completed.  Kernels after this one may be scheduled as SMs free up.
-  asm volatile("griddepcontrol.wait;" ::: "memory");
-  asm volatile("griddepcontrol.launch_dependents;");
+  pdl_wait();
+  pdl_trigger();
 
   if (warp == 0) {
     // ------------------------------------------------------------ TMA producer

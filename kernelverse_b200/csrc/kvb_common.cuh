@@ -181,7 +181,9 @@ __device__ __forceinline__ float block_reduce_1bar(float v, float* buf) {
 // A kernel launched with launch_pdl may start (and run its set-up) while the previous kernel in
 // the stream finishes; pdl_wait() returns once that kernel has completed and its memory is
 // visible, so everything global is read or written after it.  pdl_trigger() lets the next such
-// kernel be scheduled as SMs free up.  Both return at once without a dependent launch.
+// kernel be scheduled once every CTA of this grid has issued it (or exited); that kernel may then
+// run its own set-up, but it too reads and writes nothing global before its pdl_wait(), which
+// is what makes an early trigger safe.  Both return at once without a dependent launch.
 __device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
 __device__ __forceinline__ void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;"); }
 
