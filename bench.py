@@ -305,7 +305,7 @@ def gemm_benchmarks(torch, ops, hbm_peak):
         nbytes = M * K + N * K + M * N * 2 + M * 4 + N * 4 + N * 2
         entry = {"workload": f"W8A8 GEMM M={M}, N={N}, K={K}, bf16 out (BASELINE config 3)",
                  "kernel": ("w8a8_gemm_kernel 256x256 tiles on CTA pairs (cta_group::2)" if M > 256 else
-                            "w8a8_gemm_kernel 256x512 tiles on CTA pairs (two N=256 MMAs per k-step)" if M > 128
+                            "w8a8_gemm_kernel 256x448 tiles on CTA pairs (two N=224 MMAs per k-step)" if M > 128
                             else "w8a8_gemm_kernel 128x208 tiles, one CTA per SM"), "us_per_call": round(us, 2),
                  "tops": round(ops_ / us / 1e6, 1), "bytes_per_call": nbytes,
                  "achieved_gbs": round(nbytes / us / 1e3, 1), "hbm_frac": round(nbytes / us / 1e3 / hbm_peak, 4)}

@@ -322,6 +322,52 @@ __device__ __forceinline__ void epilogue32(const GemmArgs& g, const uint32_t (&r
   pack_out(g, f, w);
 }
 
+// The plain scale / bias epilogue with the tile's column operands in shared memory: cop[j] =
+// {sb, bias} of column j, read as broadcasts (every lane reads the same address), two columns
+// per 16-byte load -- no shuffles, and no global loads once the accumulator is ready.
+template <bool kBias>
+__device__ __forceinline__ void epi_values_smem_t(const uint32_t (&r)[32], const float2* cop, float sa, float (&f)[32]) {
+#pragma unroll
+  for (int j = 0; j < 32; j += 2) {
+    const float4 c = *reinterpret_cast<const float4*>(cop + j);
+    float y0 = __fmul_rn(__fmul_rn((float)(int32_t)r[j], sa), c.x);
+    float y1 = __fmul_rn(__fmul_rn((float)(int32_t)r[j + 1], sa), c.z);
+    if constexpr (kBias) {
+      y0 = __fadd_rn(y0, c.y);
+      y1 = __fadd_rn(y1, c.w);
+    }
+    f[j] = y0;
+    f[j + 1] = y1;
+  }
+}
+__device__ __forceinline__ void epilogue32_smem(const GemmArgs& g, const uint32_t (&r)[32], const float2* cop, float sa,
+                                                uint32_t* w) {
+  float f[32];
+  if (g.bias) epi_values_smem_t<true>(r, cop, sa, f);
+  else epi_values_smem_t<false>(r, cop, sa, f);
+  pack_out(g, f, w);
+}
+
+// Named barrier 1 over the epilogue warps only (barrier 0 is __syncthreads).
+__device__ __forceinline__ void epi_bar() { asm volatile("bar.sync 1, %0;" ::"n"(kEpiWarps * 32) : "memory"); }
+
+// Dynamic shared memory of one configuration: the stage ring, the TMA-store staging buffers and,
+// when they fit in the 227 KB a CTA may have, one column-operand table per accumulator buffer
+// ({sb, bias} per column, the tile's columns rounded up to 32), plus 1 KB for the 1024-byte
+// alignment of the ring.
+template <int BN, int STAGES, bool kTmaStore, bool k2Sm, int NSUB>
+struct GemmSmem {
+  static constexpr int kBRows = k2Sm ? BN / 2 : BN;
+  static constexpr size_t kStage = (size_t)kBM * kBK + (size_t)NSUB * kBRows * kBK;
+  static constexpr size_t kStaging = kTmaStore ? (size_t)kEpiWarps * 4096 : 0;
+  static constexpr int kNBuf = NSUB == 1 ? 2 : 1;
+  static constexpr int kTabCols = (BN * NSUB + 31) / 32 * 32;
+  static constexpr size_t kTabBytes = (size_t)kNBuf * kTabCols * 8;
+  static constexpr size_t kBase = STAGES * kStage + kStaging;   // offset of the tables
+  static constexpr bool kColSmem = kBase + kTabBytes + 2048 <= 232448;   // + alignment + static smem
+  static constexpr size_t kDynamic = kBase + (kColSmem ? kTabBytes : 0) + 1024;
+};
+
 // The value the unfused GEMM would have stored, back in float32.
 __device__ __forceinline__ float round_out(const GemmArgs& g, float x) {
   if (g.out_dtype == KVB_BF16) return __bfloat162float(__float2bfloat16_rn(x));
@@ -357,8 +403,9 @@ __device__ __forceinline__ void act_values(const GemmArgs& g, const uint32_t (&r
 
 // k2Sm: CTA pairs (cluster of 2) compute 256 x BN tiles with cta_group::2 MMAs; each CTA loads
 // its 128 rows of A and BN/2 rows of B, so a k-block moves 32 KB per SM instead of 48 KB.
-// NSUB = 2: a tile is two N = BN MMA sub-tiles sharing the A tile (2 x 256 = 512 columns, the
-// whole TMEM, so one accumulator buffer); a k-block then moves 48 KB per SM for twice the MACs.
+// NSUB = 2: a tile is two N = BN MMA sub-tiles sharing the A tile (2 x BN > 256 columns, so one
+// accumulator buffer in the 512 TMEM columns); a k-block then moves (16 + BN / 8) KB per SM for
+// twice the MACs.
 template <int BN, int STAGES, bool kTmaStore, bool k2Sm, int NSUB = 1>
 __global__ void __launch_bounds__(kThreads, 1) w8a8_gemm_kernel(const __grid_constant__ CUtensorMap tmap_a,
                                                                  const __grid_constant__ CUtensorMap tmap_b,
@@ -378,6 +425,8 @@ __global__ void __launch_bounds__(kThreads, 1) w8a8_gemm_kernel(const __grid_con
   constexpr uint32_t kTmemCols = kAcc <= 32 ? 32 : kAcc <= 64 ? 64 : kAcc <= 128 ? 128 : kAcc <= 256 ? 256 : 512;
   static_assert(BN % 16 == 0 && BN >= 16 && BN <= 256, "tcgen05 kind::i8 with M=128 needs N % 16 == 0, N <= 256");
   constexpr uint32_t kIdesc = idesc_i8(kTileM, BN);
+  using SL = GemmSmem<BN, STAGES, kTmaStore, k2Sm, NSUB>;
+  static_assert(SL::kStage == kStageBytes && SL::kNBuf == kNBuf, "shared-memory layout");
 
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -521,12 +570,29 @@ __global__ void __launch_bounds__(kThreads, 1) w8a8_gemm_kernel(const __grid_con
     const int esize = (g.out_dtype == KVB_I32 || g.out_dtype == KVB_F32) ? 4 : 2;
     const int CW = 128 / esize;             // columns per 128-byte chunk
     uint8_t* stage_buf = smem + (size_t)STAGES * kStageBytes + (size_t)ew * 4096;
+    // Plain scale / bias epilogue: the eight warps load the tile's column operands into a shared
+    // table while the accumulator is computed (every warp of the CTA runs the same tiles, so all
+    // take part in every epi_bar, also after a timed-out wait).
+    const bool smem_cols = SL::kColSmem && !g.act && !g.azp && !g.azp_adj && g.out_dtype != KVB_I32;
+    bool failed = false;
     uint32_t local = 0;
     for (int t = tile0; t < g.tiles; t += tstride, ++local) {
       const uint32_t ab = kNBuf == 2 ? (local & 1u) : 0u, v = kNBuf == 2 ? (local >> 1) : local;
-      // The row and first-chunk column operands are loaded before the accumulator is ready.
+      // The row and column operands are loaded before the accumulator is ready.
       int mb, nb;
       tile_coords(g, t, mb, nb);
+      float2* const cop = reinterpret_cast<float2*>(smem + SL::kBase) + ab * SL::kTabCols;
+      if (smem_cols) {
+        // With one table, every warp must be done with the previous tile's; with two, the
+        // barrier after the previous fill already ordered this one behind tile t - 2's readers.
+        if constexpr (kNBuf == 1) epi_bar();
+        for (int c = ew * 32 + lane; c < SL::kTabCols; c += kEpiWarps * 32) {
+          const int n = min(nb * TN + c, g.N - 1);
+          cop[c] = make_float2(g.sb[n], g.bias ? load_bias(g.bias, g.bias_dtype, n) : 0.0f);
+        }
+        epi_bar();
+      }
+      if (failed) continue;
       const int row0 = mb * kTileM + (int)crank * kBM + q * 32;   // first output row of this warp
       const int m = row0 + lane;
       const bool mrow = m < g.M;
@@ -542,11 +608,14 @@ __global__ void __launch_bounds__(kThreads, 1) w8a8_gemm_kernel(const __grid_con
           af[k] = load_sb_bias(g, nb * TN + 32 * k, lane);
           as[k] = load_sb_bias(g, nb * TN + OC + 32 * k, lane);
         }
-      } else {
+      } else if (!smem_cols) {
         cv0 = load_cols(g, nb * TN + half * CW, lane);
         if (esize == 2 && half * CW + 32 < TN) cv1 = load_cols(g, nb * TN + half * CW + 32, lane);
       }
-      if (!mbar_wait_bounded(&tmem_full[ab], v & 1u)) break;
+      if (!mbar_wait_bounded(&tmem_full[ab], v & 1u)) {
+        failed = true;   // stop working but keep taking part in the table barriers
+        continue;
+      }
       tc_fence_after();
 #pragma unroll 1
       for (int c0 = half * CW; c0 < OC; c0 += 2 * CW) {
@@ -572,6 +641,16 @@ __global__ void __launch_bounds__(kThreads, 1) w8a8_gemm_kernel(const __grid_con
               fa[j] = g.act == 1 ? __fmul_rn(silu(x), y) : __fmul_rn(x, silu(y));
             }
             pack_out(g, fa, w + 16 * h);    // h > 0 only for 16-bit outputs (16 words per 32 columns)
+          }
+        } else if (smem_cols) {
+          uint32_t r[32];
+          __syncwarp();                     // tcgen05.ld is .sync.aligned: reconverge first
+          tmem_ld32(tm + c0, r);
+          epilogue32_smem(g, r, cop + c0, sa, w);
+          if (esize == 2 && c0 + 32 < TN) {
+            __syncwarp();
+            tmem_ld32(tm + c0 + 32, r);
+            epilogue32_smem(g, r, cop + c0 + 32, sa, w + 16);
           }
         } else {
           const int n0 = nb * TN + c0;
@@ -781,8 +860,7 @@ int launch_gemm(const int8_t* a, const int8_t* b_nk, GemmArgs& g, void* const* d
     rc = make_out_map(&om.m[d], dests[d], g.out_dtype, g.M, map_cols, g.ldo);
     if (rc) return rc;
   }
-  constexpr size_t kStaging = kTmaStore ? kEpiWarps * 4096 : 0;   // one [32 rows x 128 B] buffer per epilogue warp
-  const size_t smem = (size_t)STAGES * (kBM * kBK + NSUB * kBRows * kBK) + kStaging + 1024;
+  const size_t smem = GemmSmem<BN, STAGES, kTmaStore, k2Sm, NSUB>::kDynamic;
   auto kern = w8a8_gemm_kernel<BN, STAGES, kTmaStore, k2Sm, NSUB>;
   static int set_dev = -1;
   int dev = 0;
@@ -930,13 +1008,14 @@ extern "C" int kvb_w8a8_scaled_mm(const int8_t* a, const int8_t* b, int b_layout
     g.rowsum = rs;
   }
   // M <= 128 streams B from HBM: 208-column tiles make N = 28672 exactly 138 tiles (one wave on
-  // 148 SMs).  M <= 256: CTA pairs with 256 x 512 tiles (two N = 256 MMAs per k-step sharing A:
-  // 56 tiles for N = 28672, one wave; 58.2 vs 60.0 us at M = 256).  Larger M: CTA pairs with
+  // 148 SMs).  M <= 256: CTA pairs with 256 x 448 tiles (two N = 224 MMAs per k-step sharing A:
+  // 64 tiles for N = 28672, one wave on 128 SMs; 54.3 us at M = 256 against 57.9 with 256 x 512
+  // tiles on 112 SMs and 60.0 with 256 x 256 tiles in two waves).  Larger M: CTA pairs with
   // 256 x 256 tiles and a double-buffered accumulator, so each tile's epilogue overlaps the next
   // tile's main loop (the single-buffered 512-column tiles lose 5-15 % there).
   void* dests[1] = {out};
   if (M <= 128) return launch_gemm<208, 5, false, false>(a, b_nk, g, dests, 1, N, st);
-  if (M <= 256) return launch_gemm<256, 4, false, true, 2>(a, b_nk, g, dests, 1, N, st);
+  if (M <= 256) return launch_gemm<224, 5, false, true, 2>(a, b_nk, g, dests, 1, N, st);
   return launch_gemm<256, 6, false, true>(a, b_nk, g, dests, 1, N, st);
 }
 
