@@ -60,7 +60,9 @@ KVB_API int kvb_abi_version(void);
  * Diagnostics (no reference counterpart).  kvb_device_status synchronises the
  * current device and returns the OR of the library's device status words:
  * bit 0 = a bounded device-side wait gave up (its kernel drained and exited
- * early; outputs of that launch are invalid).  reset != 0 clears the words.
+ * early; outputs of that launch are invalid); bit 1 = a slot or block-table entry out of
+ * range was skipped; bit 2 = a prefill indptr range out of range was skipped.  reset != 0
+ * clears the words.
  * Returns 0x80000000 if the device itself reports an error.
  */
 KVB_API unsigned int kvb_device_status(int reset);
@@ -309,6 +311,23 @@ KVB_API int kvb_flash_attn_with_kvcache(const void* q, const void* k_cache, cons
                                        int64_t seq_len_k, int num_heads, int num_kv_heads, int head_dim,
                                        float softmax_scale, void* out, float* softmax_lse, void* workspace,
                                        size_t workspace_bytes, void* stream);
+
+/*
+ * Packed variable-length causal prefill.  Replaces
+ * operators/attention/batched_prefill_attention/batched_prefill_attention.py:30-73:
+ * q [total_q, num_q_heads, D]; k / v [total_kv, num_kv_heads, D]; qo_indptr / kv_indptr int32
+ * [batch + 1] (device): request b owns query rows [qo_indptr[b], qo_indptr[b+1]) and keys
+ * [kv_indptr[b], kv_indptr[b+1]); with q_len <= kv_len its query row i is at position
+ * kv_len - q_len + i and attends keys 0..that position (causal), query head h using KV head
+ * h / (num_q_heads / num_kv_heads); logits scaled by softmax_scale; float32 softmax state.
+ * out [total_q, num_q_heads, D] in `dtype` (KVB_F32, KVB_F16 or KVB_BF16, shared by q, k, v).
+ * D a multiple of 8, at most 128.  An indptr range outside [0, total_q] / [0, total_kv] skips
+ * its request and sets bit 2 of kvb_device_status.  No workspace, no host synchronisation.
+ */
+KVB_API int kvb_batched_prefill_attention(const void* q, const void* k, const void* v, int dtype,
+                                          const int32_t* qo_indptr, const int32_t* kv_indptr, int batch,
+                                          int64_t total_q, int64_t total_kv, int num_q_heads, int num_kv_heads,
+                                          int head_dim, float softmax_scale, void* out, void* stream);
 
 /*
  * Allocation-free variant of kvb_paged_attention (no counterpart in the reference).

@@ -14,6 +14,9 @@ namespace kvb {
 
 // ------------------------------------------------------------------ host-side error reporting
 // Sets the thread-local message returned by kvb_last_error() and returns `code`.
+#if defined(__GNUC__)
+__attribute__((format(printf, 2, 3)))
+#endif
 int set_error(int code, const char* fmt, ...);
 // Checks the launch that was just issued (no synchronisation).
 int check_launch(const char* what);

@@ -312,6 +312,33 @@ def flash_attn_with_kvcache(q, k_cache, v_cache, cache_seqlens, softmax_scale: O
     return out, lse
 
 
+def batched_prefill_attention(q, k, v, qo_indptr, kv_indptr, softmax_scale: Optional[float] = None):
+    """operators/attention/batched_prefill_attention/batched_prefill_attention.py:30-73 ->
+    packed output [total_q, Hq, D] in q's dtype.
+
+    q [total_q, Hq, D]; k / v [total_kv, Hkv, D] of q's dtype; qo_indptr / kv_indptr int32
+    [batch + 1] on the device: causal attention inside each request, its query rows being the
+    last q_len positions of its kv_len keys; query head h reads KV head h // (Hq / Hkv)."""
+    dev = _cuda(q, k, v, qo_indptr, kv_indptr)
+    tq, hq, d = q.shape
+    tkv, hkv = k.shape[0], k.shape[1]
+    if k.shape != (tkv, hkv, d) or v.shape != k.shape:
+        raise ValueError("batched_prefill_attention: k and v must be [total_kv, num_kv_heads, head_dim]")
+    if k.dtype != q.dtype or v.dtype != q.dtype:
+        raise ValueError("batched_prefill_attention: q, k and v must share a dtype")
+    if qo_indptr.dtype != torch.int32 or kv_indptr.dtype != torch.int32:
+        raise ValueError("batched_prefill_attention: indptrs must be int32")
+    if qo_indptr.dim() != 1 or kv_indptr.shape != qo_indptr.shape:
+        raise ValueError("batched_prefill_attention: indptrs must be [batch + 1]")
+    scale = d ** -0.5 if softmax_scale is None else softmax_scale
+    q, k, v = q.contiguous(), k.contiguous(), v.contiguous()
+    qo_indptr, kv_indptr = qo_indptr.contiguous(), kv_indptr.contiguous()
+    out = torch.empty((tq, hq, d), dtype=q.dtype, device=dev)
+    call("kvb_batched_prefill_attention", _ptr(q), _ptr(k), _ptr(v), kvb_dtype(q.dtype), _ptr(qo_indptr),
+         _ptr(kv_indptr), qo_indptr.numel() - 1, tq, tkv, hq, hkv, d, float(scale), _ptr(out), _stream(dev))
+    return out
+
+
 _FLASH_DECODE_INDEX = {}
 
 

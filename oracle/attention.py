@@ -22,6 +22,9 @@ The oracle, like the device kernels, takes caches as ``[num_blocks, bs, Hkv, D]`
 * ``flash_attn_with_kvcache``: ``operators/attention/flash_attn_with_kvcache/flash_attn_with_kvcache.py:29-56``
   -- every query token of sequence b attends to its first ``cache_seqlens[b]`` keys of a
   dense ``[B, Sk, H, D]`` cache; also the natural-log sum of exp of the scaled logits.
+* ``batched_prefill_attention``: ``operators/attention/batched_prefill_attention/batched_prefill_attention.py:30-73``
+  -- packed requests delimited by ``qo_indptr`` / ``kv_indptr``; query row i of a request with
+  ``q_len <= kv_len`` sits at position ``kv_len - q_len + i`` and sees keys ``<=`` it (``:66-73``).
 * ``flash_decoding_attention``: ``operators/attention/flash_decoding_attention/flash_decoding_attention.py:30-87``
   over ``[B, H, S, D]`` caches in chunks of ``chunk_size`` keys, with the causal mask of
   ``:89-101`` (query i of Sq sees keys ``<= S - Sq + i``).
@@ -199,3 +202,29 @@ def flash_attn_with_kvcache(q, k_cache, v_cache, cache_seqlens, scale: float):
                 lse[b, h, i] = m + np.log(p.sum())
     return out.astype(np.float32), lse.astype(np.float32)
 
+
+
+def batched_prefill_attention(q, k, v, qo_indptr, kv_indptr, num_q_heads: int, num_kv_heads: int, scale: float):
+    """Packed causal prefill (batched_prefill_attention.py:30-73): ``q [Tq, Hq, D]``,
+    ``k / v [Tkv, Hkv, D]``, indptrs ``[B + 1]`` -> ``out [Tq, Hq, D]``; query head h reads KV
+    head ``h // (Hq / Hkv)``; row i of request b is at ``kv_len - q_len + i`` (:66-73)."""
+    qf = np.asarray(q, np.float64)
+    kf = np.asarray(k, np.float64)
+    vf = np.asarray(v, np.float64)
+    grp = num_q_heads // num_kv_heads
+    out = np.zeros(qf.shape)
+    qo = np.asarray(qo_indptr, np.int64)
+    kvp = np.asarray(kv_indptr, np.int64)
+    for b in range(len(qo) - 1):
+        q0, q1, k0, k1 = qo[b], qo[b + 1], kvp[b], kvp[b + 1]
+        ql, kl = q1 - q0, k1 - k0
+        pos = np.arange(ql) + (kl - ql)
+        masked = np.arange(kl)[None, :] > pos[:, None]
+        for h in range(num_q_heads):
+            kk, vv = kf[k0:k1, h // grp], vf[k0:k1, h // grp]
+            sc = (qf[q0:q1, h] @ kk.T) * scale
+            sc[masked] = -np.inf
+            m = sc.max(axis=1, keepdims=True)
+            p = np.exp(sc - m)
+            out[q0:q1, h] = (p @ vv) / p.sum(axis=1, keepdims=True)
+    return out.astype(np.float32)

@@ -314,6 +314,18 @@ def main():
         save(f"flash_attn_with_kvcache_{i}", shape, q=qq, k_cache=kk, v_cache=vv, cache_seqlens=lens, out=out,
              softmax_lse=lse)
 
+    # --- next rows: batched_prefill_attention (reference op, correctness mode): full and chunked
+    #     prefill, ragged lengths, GQA / MHA / MQA, head dims 64 / 80 / 96 / 128, all three dtypes
+    for i, (ql, kl, hq, hkv, d, dt) in enumerate([([64, 48, 32, 16], [64, 48, 32, 16], 8, 2, 64, "FP32"),
+                                                 ([100, 7], [100, 7], 4, 4, 128, "BF16"),
+                                                 ([33, 70], [160, 70], 8, 1, 80, "FP16"),
+                                                 ([129, 1, 65], [200, 1, 65], 4, 2, 96, "FP32"),
+                                                 ([80, 40], [300, 90], 8, 2, 128, "BF16")]):
+        shape = {"q_lens": ql, "kv_lens": kl, "num_q_heads": hq, "num_kv_heads": hkv, "head_dim": d, "dtype": dt}
+        qq, kk, vv, qo, kvp = gen_inputs("attention", "batched_prefill_attention", shape, 1600 + i)
+        out = run_model("attention", "batched_prefill_attention", shape, (qq, kk, vv, qo, kvp))
+        save(f"batched_prefill_attention_{i}", shape, q=qq, k=kk, v=vv, qo_indptr=qo, kv_indptr=kvp, out=out)
+
     (HERE / "VERSIONS.txt").write_text(f"torch {torch.__version__}\nnumpy {np.__version__}\n")
 
 

@@ -52,6 +52,12 @@ def test_validation_errors_need_no_gpu():
     assert rc == 1
     rc = lib.kvb_add_rmsnorm_quant(None, None, None, _lib.BF16, 2, 8, 1e-6, None, None, _lib.E4M3, None, None)
     assert rc == 1
+    rc = lib.kvb_batched_prefill_attention(None, None, None, _lib.BF16, None, None, 1, 8, 8, 4, 3, 64, 0.125, None,
+                                           None)
+    assert rc == 2 and b"num_q_heads" in lib.kvb_last_error()
+    rc = lib.kvb_batched_prefill_attention(None, None, None, _lib.BF16, None, None, 1, 8, 8, 4, 2, 136, 0.125, None,
+                                           None)
+    assert rc == 2 and b"head_dim" in lib.kvb_last_error()
     with pytest.raises(_lib.KvbError):
         _lib.call("kvb_per_token_group_quant_int8", None, _lib.F32, 1, 10, 3, 1e-6, None, None, None)
 

@@ -179,3 +179,12 @@ def test_flash_attn_with_kvcache(name):
     assert out.dtype == TORCH_DT[meta["dtype"]] and lse.dtype == torch.float32
     _check(out, g["out"][0], "", TOL[meta["dtype"]])
     _check(lse, g["softmax_lse"][0], "", TOL["FP32"] if meta["dtype"] == "FP32" else {"rtol": 2e-3, "atol": 2e-3})
+
+
+@pytest.mark.parametrize("name", golden_names("batched_prefill_attention"))
+def test_batched_prefill_attention(name):
+    meta, g = load_golden(name)
+    out = modelnew("batched_prefill_attention", meta)(*(_as_dev(*g[k]) for k in ("q", "k", "v", "qo_indptr",
+                                                                                 "kv_indptr")))
+    assert out.dtype == TORCH_DT[meta["dtype"]] and tuple(out.shape) == g["out"][0].shape
+    _check(out, g["out"][0], "", TOL[meta["dtype"]])

@@ -169,3 +169,12 @@ def test_flash_attn_with_kvcache(name):
     tol = {"FP32": 2e-5, "FP16": 2e-3, "BF16": 1.6e-2}[meta["dtype"]]
     np.testing.assert_allclose(out, g["out"][0], rtol=tol, atol=tol)
     np.testing.assert_allclose(lse, g["softmax_lse"][0], rtol=2e-5, atol=2e-5)
+
+
+@pytest.mark.parametrize("name", golden_names("batched_prefill_attention"))
+def test_batched_prefill_attention(name):
+    meta, g = load_golden(name)
+    out = attention.batched_prefill_attention(g["q"][0], g["k"][0], g["v"][0], g["qo_indptr"][0], g["kv_indptr"][0],
+                                              meta["num_q_heads"], meta["num_kv_heads"], meta["head_dim"] ** -0.5)
+    tol = {"FP32": 2e-5, "FP16": 2e-3, "BF16": 1.6e-2}[meta["dtype"]]
+    np.testing.assert_allclose(out, g["out"][0], rtol=tol, atol=tol)
