@@ -328,6 +328,17 @@ KVB_API int kvb_batched_prefill_attention(const void* q, const void* k, const vo
                                           const int32_t* qo_indptr, const int32_t* kv_indptr, int batch,
                                           int64_t total_q, int64_t total_kv, int num_q_heads, int num_kv_heads,
                                           int head_dim, float softmax_scale, void* out, void* stream);
+/*
+ * The same with the kernel chosen (test hook, no reference counterpart): variant 0 = automatic
+ * (tcgen05 for f16 / bf16 with head_dim a multiple of 16 in [64, 128], at least 128 query and
+ * key tokens and a 16-byte-aligned out; otherwise the mma.sync kernel), 1 = the mma.sync
+ * kernel, 2 = the tcgen05 kernel (KVB_E_SHAPE where it does not apply).
+ */
+KVB_API int kvb_batched_prefill_attention_variant(const void* q, const void* k, const void* v, int dtype,
+                                                  const int32_t* qo_indptr, const int32_t* kv_indptr, int batch,
+                                                  int64_t total_q, int64_t total_kv, int num_q_heads,
+                                                  int num_kv_heads, int head_dim, float softmax_scale, void* out,
+                                                  int variant, void* stream);
 
 /*
  * Allocation-free variant of kvb_paged_attention (no counterpart in the reference).

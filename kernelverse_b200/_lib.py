@@ -44,6 +44,8 @@ SIGNATURES = {
     "kvb_paged_attention": (_I, [_P, _I, _P, _P, _I, _P, _P, _P, _I, _P, _I64, _I, _I, _I, _I, _I, _I64, _I64, _F,
                                  _P, _P, _I, _I, _P, _I, _P, _P, _P, _I, _P, _SZ, _P]),
     "kvb_batched_prefill_attention": (_I, [_P, _P, _P, _I, _P, _P, _I, _I64, _I64, _I, _I, _I, _F, _P, _P]),
+    "kvb_batched_prefill_attention_variant": (_I, [_P, _P, _P, _I, _P, _P, _I, _I64, _I64, _I, _I, _I, _F, _P, _I,
+                                                   _P]),
     "kvb_paged_attention_noalloc": (_I, [_P, _I, _P, _P, _I, _P, _P, _P, _I, _P, _I64, _I, _I, _I, _I, _I, _I64, _I64,
                                          _F, _P, _P, _I, _I, _P, _I, _P, _P, _P, _I, _P]),
 }

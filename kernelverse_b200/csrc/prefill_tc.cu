@@ -1,0 +1,481 @@
+// Packed causal prefill attention on the 5th-generation tensor cores (16-bit inputs).
+// Same contract as prefill.cu (operators/attention/batched_prefill_attention/batched_prefill_attention.py:30-73);
+// this kernel serves f16 / bf16 with head_dim a multiple of 16 up to 128.
+//
+// One CTA per (128 query rows of one request, one query head), warp-specialised:
+//   warp 0     TMA producer: the Q tile once, then K and V tiles of 128 keys into a 2-deep ring
+//              (3-D tensor maps over [tokens, heads, D], boxes of 64 D-elements x 128 tokens with
+//              the 128-byte swizzle; rows past the tensors are zero-filled);
+//   warp 1     allocates TMEM (S double buffer of 2 x 128 columns + O of D columns) and one lane
+//              issues the MMAs: S_j = Q K_j^T (kind::f16, M = 128, N = 128, both K-major) into
+//              S[j % 2], then O += P_j V_j (M = 128, N = D, K = 128; P K-major from shared memory,
+//              V MN-major), S_{j+1} issued ahead of PV_j so the softmax of tile j+1 overlaps PV_j;
+//   warps 2-5  softmax, one query row per thread (TMEM lane = row): the row max of S_j (scaled to
+//              the log2 domain, causal mask), P = 2^(s - m) rounded to the input type into
+//              shared memory (K-major, 128-byte swizzle), the running sum, and the O rescale; the
+//              max is only moved when it grows by more than 2^8 (the sum and O then scale by
+//              the same factor, so the result is unchanged and most tiles skip the rescale);
+//              finally O / l to global memory.
+// Every mbarrier wait is bounded; on a timeout the roles stop, the producer waits for its own
+// copies, the MMA lane for its MMAs, and the CTA frees its TMEM before exiting.
+#include <cuda.h>
+#include <cudaTypedefs.h>
+
+#include <mutex>
+#include <type_traits>
+
+#include "kvb_common.cuh"
+#include "kvb_async.cuh"
+
+namespace kvb {
+namespace {
+
+constexpr int kTcRows = 128;               // query rows per CTA (TMEM lanes)
+constexpr int kTcKeys = 128;               // keys per K/V tile
+constexpr int kTcThreads = 192;            // producer, MMA, four softmax warps
+constexpr uint32_t kChunkBytes = 16384;    // [128 rows x 64 elements] of a 16-bit operand
+constexpr float kLazyMax = 8.0f;           // log2 growth of the row max that forces a rescale
+constexpr unsigned int kStatusBadIndptrTc = 4u;
+
+struct TcArgs {
+  const int32_t* qo;
+  const int32_t* kvp;
+  void* out;
+  int64_t total_q, total_kv;
+  int batch, hq, hkv, group, D;
+  float scale_log2;
+};
+
+__device__ __forceinline__ void tma_load_3d(uint32_t dst, const CUtensorMap* map, int x, int y, int z, uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.3d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3, %4}], [%5];"
+      ::"r"(dst), "l"(map), "r"(x), "r"(y), "r"(z), "r"(smem_u32(bar))
+      : "memory");
+}
+__device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void mma_commit(uint64_t* bar) {
+  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar))
+               : "memory");
+}
+// K-major operand with the 128-byte swizzle: rows of 128 B, 8-row atoms of 1024 B.
+__device__ __forceinline__ uint64_t desc_kmajor(uint32_t saddr) {
+  uint64_t d = (uint64_t)((saddr >> 4) & 0x3FFFu);
+  d |= (uint64_t)1u << 16;                  // leading byte offset (unused for swizzled K-major)
+  d |= (uint64_t)(1024u >> 4) << 32;        // stride byte offset: 8-row groups
+  d |= (uint64_t)1u << 46;                  // descriptor version (sm_100)
+  d |= (uint64_t)2u << 61;                  // SWIZZLE_128B
+  return d;
+}
+// MN-major operand with the 128-byte swizzle: 64 MN-elements per 128-byte row, one row per K
+// index; 8-row (K) groups 1024 B apart (stride offset), 64-element MN blocks `mn_block` B apart
+// (leading offset).
+__device__ __forceinline__ uint64_t desc_mnmajor(uint32_t saddr, uint32_t mn_block) {
+  uint64_t d = (uint64_t)((saddr >> 4) & 0x3FFFu);
+  d |= (uint64_t)((mn_block >> 4) & 0x3FFFu) << 16;
+  d |= (uint64_t)(1024u >> 4) << 32;
+  d |= (uint64_t)1u << 46;
+  d |= (uint64_t)2u << 61;
+  return d;
+}
+// Instruction descriptor of kind::f16 with float32 accumulation; A K-major, B K-major or MN-major.
+__host__ __device__ constexpr uint32_t idesc_f16(int m, int n, bool bf16, bool b_mn_major) {
+  return (1u << 4) | (bf16 ? (1u << 7) | (1u << 10) : 0u) | (b_mn_major ? (1u << 16) : 0u) |
+         ((uint32_t)(n >> 3) << 17) | ((uint32_t)(m >> 4) << 24);
+}
+__device__ __forceinline__ void mma_f16(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc, uint32_t idesc, uint32_t accum) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, {%5, %6, %7, %8}, p;\n\t}"
+      ::"r"(tmem_d), "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accum), "r"(0), "r"(0), "r"(0), "r"(0)
+      : "memory");
+}
+__device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&r)[32]) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
+      "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]), "=r"(r[8]),
+        "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]), "=r"(r[16]),
+        "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]), "=r"(r[24]),
+        "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+      : "r"(taddr));
+  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void tmem_st32(uint32_t taddr, const uint32_t (&r)[32]) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16,"
+      "%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31,%32};"
+      ::"r"(taddr), "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]),
+        "r"(r[8]), "r"(r[9]), "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]), "r"(r[15]), "r"(r[16]),
+        "r"(r[17]), "r"(r[18]), "r"(r[19]), "r"(r[20]), "r"(r[21]), "r"(r[22]), "r"(r[23]), "r"(r[24]),
+        "r"(r[25]), "r"(r[26]), "r"(r[27]), "r"(r[28]), "r"(r[29]), "r"(r[30]), "r"(r[31])
+      : "memory");
+  asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
+}
+__device__ __forceinline__ float ex2_approx(float x) {   // 2^x (MUFU.EX2; ex2(-inf) = +0)
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+template <bool kBf>
+__device__ __forceinline__ uint32_t pack2h(float lo, float hi) {
+  if constexpr (kBf) {
+    __nv_bfloat162 h = __floats2bfloat162_rn(lo, hi);
+    return *reinterpret_cast<uint32_t*>(&h);
+  } else {
+    __half2 h = __floats2half2_rn(lo, hi);
+    return *reinterpret_cast<uint32_t*>(&h);
+  }
+}
+// Every lane waits; the warp goes on only if all of them saw the phase complete.
+__device__ __forceinline__ bool warp_wait(uint64_t* bar, uint32_t parity) {
+  const bool ok = mbar_wait_bounded(bar, parity);
+  return __all_sync(0xffffffffu, ok);
+}
+
+// DC: 64-element chunks of D (1 or 2).  Shared memory: V ring, K ring, Q, P (each chunk 16 KB).
+template <typename T, int DC>
+__global__ void __launch_bounds__(kTcThreads, 1) prefill_tc_kernel(const __grid_constant__ CUtensorMap tq,
+                                                                   const __grid_constant__ CUtensorMap tk,
+                                                                   const __grid_constant__ CUtensorMap tv,
+                                                                   const __grid_constant__ TcArgs a) {
+  constexpr bool kBf = std::is_same<T, __nv_bfloat16>::value;
+  constexpr uint32_t kOpBytes = DC * kChunkBytes;          // one Q / K / V tile
+  constexpr uint32_t kV0 = 0, kK0 = 2 * kOpBytes, kQ0 = 4 * kOpBytes, kP0 = 5 * kOpBytes;
+  constexpr uint32_t kTmemCols = 512;
+  constexpr uint32_t kO = 2 * kTcKeys;                      // O's first TMEM column
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  const uint32_t sbase = smem_u32(smem);
+  __shared__ uint64_t q_full, k_full[2], v_full[2], kv_empty[2], s_full[2], s_free[2], p_full, pv_done, mma_done;
+  __shared__ uint32_t tmem_base_s;
+  __shared__ volatile int s_abort;
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int h = blockIdx.x;
+  if (threadIdx.x == 0) {
+    mbar_init(&q_full, 1);
+    for (int s = 0; s < 2; ++s) {
+      mbar_init(&k_full[s], 1);
+      mbar_init(&v_full[s], 1);
+      mbar_init(&kv_empty[s], 1);
+      mbar_init(&s_full[s], 1);
+      mbar_init(&s_free[s], 4);
+    }
+    mbar_init(&p_full, 4);
+    mbar_init(&pv_done, 1);
+    mbar_init(&mma_done, 1);
+    s_abort = 0;
+    fence_mbar_init();
+    asm volatile("prefetch.tensormap [%0];" ::"l"(&tq) : "memory");
+    asm volatile("prefetch.tensormap [%0];" ::"l"(&tk) : "memory");
+    asm volatile("prefetch.tensormap [%0];" ::"l"(&tv) : "memory");
+  }
+  pdl_trigger();
+  pdl_wait();            // launched as a programmatic dependent: global data from here on
+
+  // (request, query tile) of this CTA: request b's tiles, last first.
+  int b = -1, tile = 0;
+  {
+    int rem = (int)blockIdx.y;
+    for (int r = 0; r < a.batch; ++r) {
+      const int ql = a.qo[r + 1] - a.qo[r];
+      const int nt = ql > 0 ? (ql + kTcRows - 1) / kTcRows : 0;
+      if (rem < nt) {
+        b = r;
+        tile = nt - 1 - rem;
+        break;
+      }
+      rem -= nt;
+    }
+  }
+  if (b < 0) return;
+  const int q0 = a.qo[b], ql = a.qo[b + 1] - q0;
+  const int k0 = a.kvp[b], kl = a.kvp[b + 1] - k0;
+  if (q0 < 0 || (int64_t)q0 + ql > a.total_q || k0 < 0 || kl < 0 || (int64_t)k0 + kl > a.total_kv) {
+    if (threadIdx.x == 0) atomicOr(&g_tu_status, kStatusBadIndptrTc);
+    return;
+  }
+  const int i0 = tile * kTcRows;
+  const int rows = min(kTcRows, ql - i0);
+  const int off = kl - ql;                                 // position of query row i = off + i
+  const int last = min(off + i0 + rows - 1, kl - 1);       // last key the tile attends
+  const int n = last >= 0 ? last / kTcKeys + 1 : 0;        // key tiles
+  const int kvh = h / a.group;
+  const int D = a.D;
+
+  if (warp == 1) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(&tmem_base_s)),
+                 "r"(kTmemCols)
+                 : "memory");
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = tmem_base_s;
+
+  if (warp == 0) {
+    // ---------------------------------------------------------------- TMA producer
+    if (lane == 0) {
+      mbar_arrive_expect_tx(&q_full, kOpBytes);
+      for (int c = 0; c < DC; ++c) tma_load_3d(sbase + kQ0 + c * kChunkBytes, &tq, c * 64, h, q0 + i0, &q_full);
+      int issued = 0;
+      for (int j = 0; j < n; ++j) {
+        const int s = j & 1;
+        if (j >= 2 && !mbar_wait_bounded(&kv_empty[s], ((j >> 1) - 1) & 1)) {
+          s_abort = 1;
+          break;
+        }
+        if (s_abort) break;
+        const int kt = k0 + j * kTcKeys;
+        mbar_arrive_expect_tx(&k_full[s], kOpBytes);
+        for (int c = 0; c < DC; ++c)
+          tma_load_3d(sbase + kK0 + s * kOpBytes + c * kChunkBytes, &tk, c * 64, kvh, kt, &k_full[s]);
+        mbar_arrive_expect_tx(&v_full[s], kOpBytes);
+        for (int c = 0; c < DC; ++c)
+          tma_load_3d(sbase + kV0 + s * kOpBytes + c * kChunkBytes, &tv, c * 64, kvh, kt, &v_full[s]);
+        issued = j + 1;
+      }
+      // every copy this CTA issued has landed before it exits
+      mbar_wait_bounded(&q_full, 0);
+      for (int j = issued > 2 ? issued - 2 : 0; j < issued; ++j) {
+        mbar_wait_bounded(&k_full[j & 1], (j >> 1) & 1);
+        mbar_wait_bounded(&v_full[j & 1], (j >> 1) & 1);
+      }
+    }
+  } else if (warp == 1) {
+    // ---------------------------------------------------------------- MMA issuer
+    if (lane == 0) {
+      constexpr uint32_t kIdS = idesc_f16(kTcRows, kTcKeys, kBf, false);
+      const uint32_t id_pv = idesc_f16(kTcRows, D, kBf, true);
+      const int ksteps = D / 16;
+      auto issue_s = [&](int j) -> bool {
+        const int s = j & 1;
+        if (!mbar_wait_bounded(&k_full[s], (j >> 1) & 1)) return false;
+        if (j >= 2 && !mbar_wait_bounded(&s_free[s], ((j >> 1) - 1) & 1)) return false;
+        tc_fence_after();
+        for (int ks = 0; ks < ksteps; ++ks) {
+          const uint32_t off_b = (uint32_t)(ks >> 2) * kChunkBytes + (uint32_t)(ks & 3) * 32u;
+          mma_f16(tmem + (uint32_t)s * kTcKeys, desc_kmajor(sbase + kQ0 + off_b),
+                  desc_kmajor(sbase + kK0 + s * kOpBytes + off_b), kIdS, ks > 0);
+        }
+        mma_commit(&s_full[s]);
+        return true;
+      };
+      bool ok = n == 0 || (mbar_wait_bounded(&q_full, 0) && issue_s(0));
+      for (int j = 0; j < n && ok && !s_abort; ++j) {
+        if (j + 1 < n && !issue_s(j + 1)) {
+          ok = false;
+          break;
+        }
+        if (!mbar_wait_bounded(&p_full, j & 1) || !mbar_wait_bounded(&v_full[j & 1], (j >> 1) & 1)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        const uint32_t vs = sbase + kV0 + (j & 1) * kOpBytes;
+#pragma unroll
+        for (int ks = 0; ks < kTcKeys / 16; ++ks) {
+          const uint32_t pa = sbase + kP0 + (uint32_t)(ks >> 2) * kChunkBytes + (uint32_t)(ks & 3) * 32u;
+          mma_f16(tmem + kO, desc_kmajor(pa), desc_mnmajor(vs + (uint32_t)ks * 2048u, kChunkBytes), id_pv,
+                  (j | ks) != 0);
+        }
+        mma_commit(&pv_done);
+        mma_commit(&kv_empty[j & 1]);
+      }
+      if (!ok) s_abort = 1;
+      mma_commit(&mma_done);                 // every MMA issued above has completed before TMEM is freed
+      mbar_wait_bounded(&mma_done, 0);
+    }
+  } else {
+    // ---------------------------------------------------------------- softmax (warps 2-5)
+    const int quarter = warp & 3;                          // TMEM lanes this warp may access
+    const int row = quarter * 32 + lane;                   // query row of the tile = TMEM lane
+    const int pos = off + i0 + row;
+    const uint32_t lane_addr = (uint32_t)(quarter * 32) << 16;
+    uint8_t* prow = smem + kP0 + row * 128;                // this row in each 64-key chunk of P
+    float m_used = -INFINITY, l = 0.0f;
+    bool ok = true;
+    for (int j = 0; j < n; ++j) {
+      if (__shfl_sync(0xffffffffu, s_abort, 0) || !warp_wait(&s_full[j & 1], (j >> 1) & 1)) {   // warp-uniform
+        ok = false;
+        break;
+      }
+      tc_fence_after();
+      const uint32_t sa = tmem + lane_addr + (uint32_t)(j & 1) * kTcKeys;
+      const int kb = j * kTcKeys;
+      const bool mask = kb + kTcKeys - 1 > off + i0 + quarter * 32;   // some key of the tile may pass a row
+      // pass 1: the tile's row max (log2 domain)
+      float mx = -INFINITY;
+#pragma unroll 1
+      for (int c = 0; c < 4; ++c) {
+        uint32_t r[32];
+        tmem_ld32(sa + c * 32, r);
+#pragma unroll
+        for (int i = 0; i < 32; ++i) {
+          float v = __uint_as_float(r[i]) * a.scale_log2;
+          if (mask && kb + c * 32 + i > pos) v = -INFINITY;
+          mx = fmaxf(mx, v);
+        }
+      }
+      const bool grow = mx > m_used + kLazyMax;
+      const float alpha = grow ? ex2_approx(m_used - mx) : 1.0f;
+      if (grow) m_used = mx;
+      l *= alpha;
+      // P may be overwritten and O rescaled once PV_{j-1} has completed
+      if (j > 0) {
+        if (!warp_wait(&pv_done, (j - 1) & 1)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+      }
+      // pass 2: P = 2^(s - m) in the input type, K-major with the 128-byte swizzle
+#pragma unroll 1
+      for (int c = 0; c < 4; ++c) {
+        uint32_t r[32];
+        tmem_ld32(sa + c * 32, r);
+        uint32_t w[16];
+#pragma unroll
+        for (int i = 0; i < 32; i += 2) {
+          float v0 = __uint_as_float(r[i]) * a.scale_log2, v1 = __uint_as_float(r[i + 1]) * a.scale_log2;
+          if (mask && kb + c * 32 + i > pos) v0 = -INFINITY;
+          if (mask && kb + c * 32 + i + 1 > pos) v1 = -INFINITY;
+          const float p0 = ex2_approx(v0 - m_used), p1 = ex2_approx(v1 - m_used);
+          l += p0 + p1;
+          w[i >> 1] = pack2h<kBf>(p0, p1);
+        }
+        uint8_t* chunk = prow + (c >> 1) * kChunkBytes;
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+          const int col16 = (c & 1) * 4 + u;               // 16-byte column within the 128-byte row
+          *reinterpret_cast<uint4*>(chunk + ((col16 ^ (row & 7)) << 4)) =
+              make_uint4(w[4 * u], w[4 * u + 1], w[4 * u + 2], w[4 * u + 3]);
+        }
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&s_free[j & 1]);
+      // O *= alpha where the max moved (whole warp, when any of its rows needs it)
+      if (j > 0 && __any_sync(0xffffffffu, alpha != 1.0f)) {
+        for (int c = 0; c < (D + 31) / 32; ++c) {
+          uint32_t r[32];
+          tmem_ld32(tmem + lane_addr + kO + c * 32, r);
+#pragma unroll
+          for (int i = 0; i < 32; ++i) r[i] = __float_as_uint(__uint_as_float(r[i]) * alpha);
+          tmem_st32(tmem + lane_addr + kO + c * 32, r);
+        }
+      }
+      asm volatile("fence.proxy.async.shared::cta;" ::: "memory");   // P visible to the tensor core
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&p_full);
+    }
+    if (!ok) s_abort = 1;
+    // O / l of the valid rows
+    if (ok && (n == 0 || warp_wait(&pv_done, (n - 1) & 1))) {
+      tc_fence_after();
+      const float inv = 1.0f / l;
+      const bool valid = i0 + row < ql;
+      T* orow = reinterpret_cast<T*>(a.out) + ((int64_t)q0 + i0 + row) * a.hq * D + (int64_t)h * D;
+      for (int c = 0; c < (D + 31) / 32; ++c) {
+        uint32_t r[32];
+        if (n > 0) tmem_ld32(tmem + lane_addr + kO + c * 32, r);
+        else
+#pragma unroll
+          for (int i = 0; i < 32; ++i) r[i] = 0u;
+        uint32_t w[16];
+#pragma unroll
+        for (int i = 0; i < 32; i += 2)
+          w[i >> 1] = pack2h<kBf>(__uint_as_float(r[i]) * inv, __uint_as_float(r[i + 1]) * inv);
+        if (valid) {
+#pragma unroll
+          for (int u = 0; u < 4; ++u)
+            if (c * 32 + u * 8 < D)
+              *reinterpret_cast<uint4*>(orow + c * 32 + u * 8) = make_uint4(w[4 * u], w[4 * u + 1], w[4 * u + 2], w[4 * u + 3]);
+        }
+      }
+    } else {
+      s_abort = 1;
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(kTmemCols) : "memory");
+  }
+}
+
+PFN_cuTensorMapEncodeTiled_v12000 encode_tiled() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    cudaDriverEntryPointQueryResult q;
+    void* p = nullptr;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+  });
+  return fn;
+}
+
+// [tokens, heads, D] 16-bit tensor; box of 64 D-elements x 1 head x 128 tokens, 128-byte swizzle,
+// zero fill out of bounds.
+int make_head_map(CUtensorMap* map, const void* base, bool bf16, int64_t tokens, int heads, int D) {
+  auto fn = encode_tiled();
+  if (!fn) return set_error(KVB_E_LAUNCH, "batched_prefill_attention: cuTensorMapEncodeTiled unavailable");
+  cuuint64_t dims[3] = {(cuuint64_t)D, (cuuint64_t)heads, (cuuint64_t)tokens};
+  cuuint64_t strides[2] = {(cuuint64_t)D * 2, (cuuint64_t)heads * D * 2};
+  cuuint32_t box[3] = {64u, 1u, (cuuint32_t)kTcRows};
+  cuuint32_t estr[3] = {1, 1, 1};
+  CUresult r = fn(map, bf16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 3,
+                  const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                  CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return set_error(KVB_E_LAUNCH, "batched_prefill_attention: tensor map failed (%d)", (int)r);
+  return KVB_OK;
+}
+
+template <typename T, int DC>
+int launch_tc(const CUtensorMap& mq, const CUtensorMap& mk, const CUtensorMap& mv, const TcArgs& a, int tiles_ub,
+              cudaStream_t st) {
+  constexpr size_t smem = 5 * (size_t)DC * kChunkBytes + 2 * kChunkBytes + 1024;
+  auto kern = prefill_tc_kernel<T, DC>;
+  static int set_dev = -1;
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (set_dev != dev) {
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    if (e != cudaSuccess) return set_error(KVB_E_LAUNCH, "batched_prefill_attention: smem attribute: %s", cudaGetErrorString(e));
+    set_dev = dev;
+  }
+  cudaError_t e = launch_pdl(kern, dim3((unsigned)a.hq, (unsigned)tiles_ub), dim3(kTcThreads), smem, st, mq, mk, mv, a);
+  if (e != cudaSuccess) return set_error(KVB_E_LAUNCH, "prefill_tc_kernel: %s", cudaGetErrorString(e));
+  return check_launch("prefill_tc_kernel");
+}
+
+}  // namespace
+
+// Host entry used by prefill.cu for 16-bit inputs with head_dim % 16 == 0 and <= 128.
+int prefill_tcgen05(const void* q, const void* k, const void* v, bool bf16, const int32_t* qo, const int32_t* kvp,
+                    int batch, int64_t total_q, int64_t total_kv, int hq, int hkv, int D, float scale_log2, void* out,
+                    cudaStream_t st) {
+  const int64_t tiles_ub = total_q / kTcRows + batch;
+  if (tiles_ub > 65535) return set_error(KVB_E_SHAPE, "batched_prefill_attention: too many query tiles");
+  CUtensorMap mq, mk, mv;
+  int rc = make_head_map(&mq, q, bf16, total_q, hq, D);
+  if (!rc) rc = make_head_map(&mk, k, bf16, total_kv, hkv, D);
+  if (!rc) rc = make_head_map(&mv, v, bf16, total_kv, hkv, D);
+  if (rc) return rc;
+  TcArgs a{};
+  a.qo = qo; a.kvp = kvp; a.out = out; a.total_q = total_q; a.total_kv = total_kv;
+  a.batch = batch; a.hq = hq; a.hkv = hkv; a.group = hq / hkv; a.D = D; a.scale_log2 = scale_log2;
+  if (D <= 64) return bf16 ? launch_tc<__nv_bfloat16, 1>(mq, mk, mv, a, (int)tiles_ub, st)
+                           : launch_tc<__half, 1>(mq, mk, mv, a, (int)tiles_ub, st);
+  return bf16 ? launch_tc<__nv_bfloat16, 2>(mq, mk, mv, a, (int)tiles_ub, st)
+              : launch_tc<__half, 2>(mq, mk, mv, a, (int)tiles_ub, st);
+}
+
+}  // namespace kvb

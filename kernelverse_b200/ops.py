@@ -312,7 +312,7 @@ def flash_attn_with_kvcache(q, k_cache, v_cache, cache_seqlens, softmax_scale: O
     return out, lse
 
 
-def batched_prefill_attention(q, k, v, qo_indptr, kv_indptr, softmax_scale: Optional[float] = None):
+def batched_prefill_attention(q, k, v, qo_indptr, kv_indptr, softmax_scale: Optional[float] = None, _variant: int = 0):
     """operators/attention/batched_prefill_attention/batched_prefill_attention.py:30-73 ->
     packed output [total_q, Hq, D] in q's dtype.
 
@@ -334,8 +334,10 @@ def batched_prefill_attention(q, k, v, qo_indptr, kv_indptr, softmax_scale: Opti
     q, k, v = q.contiguous(), k.contiguous(), v.contiguous()
     qo_indptr, kv_indptr = qo_indptr.contiguous(), kv_indptr.contiguous()
     out = torch.empty((tq, hq, d), dtype=q.dtype, device=dev)
-    call("kvb_batched_prefill_attention", _ptr(q), _ptr(k), _ptr(v), kvb_dtype(q.dtype), _ptr(qo_indptr),
-         _ptr(kv_indptr), qo_indptr.numel() - 1, tq, tkv, hq, hkv, d, float(scale), _ptr(out), _stream(dev))
+    # _variant (tests): 0 = automatic kernel choice, 1 = the mma.sync kernel, 2 = the tcgen05 kernel
+    call("kvb_batched_prefill_attention_variant", _ptr(q), _ptr(k), _ptr(v), kvb_dtype(q.dtype), _ptr(qo_indptr),
+         _ptr(kv_indptr), qo_indptr.numel() - 1, tq, tkv, hq, hkv, d, float(scale), _ptr(out), int(_variant),
+         _stream(dev))
     return out
 
 

@@ -33,7 +33,7 @@ def _indptr(lens):
     return np.concatenate([[0], np.cumsum(lens)]).astype(np.int32)
 
 
-def _run(q_lens, kv_lens, hq, hkv, d, dt, seed, scale=None):
+def _run(q_lens, kv_lens, hq, hkv, d, dt, seed, scale=None, variant=0):
     rng = seeded(seed)
     tq, tkv = int(sum(q_lens)), int(sum(kv_lens))
     tdt = TORCH_DT[dt]
@@ -41,7 +41,7 @@ def _run(q_lens, kv_lens, hq, hkv, d, dt, seed, scale=None):
     kt = dev(rng.standard_normal((tkv, hkv, d)).astype(np.float32), tdt)
     vt = dev(rng.standard_normal((tkv, hkv, d)).astype(np.float32), tdt)
     qo, kvp = _indptr(q_lens), _indptr(kv_lens)
-    out = _ops().batched_prefill_attention(qt, kt, vt, dev(qo), dev(kvp), scale)
+    out = _ops().batched_prefill_attention(qt, kt, vt, dev(qo), dev(kvp), scale, _variant=variant)
     assert out.dtype == tdt and tuple(out.shape) == (tq, hq, d)
     ref = attention.batched_prefill_attention(host(qt), host(kt), host(vt), qo, kvp, hq, hkv,
                                               d ** -0.5 if scale is None else scale)
@@ -67,7 +67,10 @@ def test_prefill_golden(name):
     np.testing.assert_allclose(host(out), g["out"][0].astype(np.float32), rtol=rtol, atol=atol)
 
 
-@pytest.mark.parametrize("dt", ["FP32", "FP16", "BF16"])
+KERNELS = [("FP32", 1), ("FP16", 1), ("BF16", 1), ("FP16", 2), ("BF16", 2)]   # (dtype, 1 = mma.sync / 2 = tcgen05)
+
+
+@pytest.mark.parametrize("dt,variant", KERNELS)
 @pytest.mark.parametrize("q_lens,kv_lens,hq,hkv,d", [
     ([512, 384, 256, 128], [512, 384, 256, 128], 32, 8, 128),       # the reference's default shape
     ([128, 128, 128, 128], [1024, 768, 512, 256], 8, 2, 128),       # chunked prefill with context
@@ -75,9 +78,19 @@ def test_prefill_golden(name):
     ([300, 65], [300, 65], 16, 1, 96),                               # MQA, head_dim 96
     ([200, 1, 63], [250, 1, 64], 8, 4, 80),                          # head_dim 80, one-row requests
 ])
-def test_prefill_shapes(dt, q_lens, kv_lens, hq, hkv, d):
-    got, ref = _run(q_lens, kv_lens, hq, hkv, d, dt, sum(q_lens) + hq * 7 + d)
+def test_prefill_shapes(dt, variant, q_lens, kv_lens, hq, hkv, d):
+    got, ref = _run(q_lens, kv_lens, hq, hkv, d, dt, sum(q_lens) + hq * 7 + d, variant=variant)
     _check(got, ref, dt)
+
+
+@pytest.mark.parametrize("variant", [1, 2])
+@pytest.mark.parametrize("q_lens,kv_lens", [([130, 1, 255], [130, 1, 400]), ([128, 128], [128, 1000]),
+                                            ([7, 300], [64, 300])])
+def test_prefill_tile_edges(variant, q_lens, kv_lens):
+    """Query and key counts one past / at / below the 128-row tiles, one-token requests, and a
+    request whose queries see far more keys than queries (chunked prefill)."""
+    got, ref = _run(q_lens, kv_lens, 8, 2, 128, "BF16", 901 + sum(kv_lens), variant=variant)
+    _check(got, ref, "BF16")
 
 
 @pytest.mark.parametrize("dt", ["FP32", "BF16"])
@@ -94,10 +107,19 @@ def test_prefill_scale_and_empty_request():
     _check(got, ref, "FP32")
 
 
-def test_prefill_long_sequence():
-    """One 4096-token request (64 query tiles, up to 64 key tiles each) beside short ones."""
-    got, ref = _run([4096, 64], [4096, 64], 4, 1, 128, "BF16", 77)
+@pytest.mark.parametrize("variant", [1, 2])
+def test_prefill_long_sequence(variant):
+    """One 4096-token request (up to 64 key tiles per query tile) beside a short one."""
+    got, ref = _run([4096, 64], [4096, 64], 4, 1, 128, "BF16", 77, variant=variant)
     _check(got, ref, "BF16")
+
+
+def test_prefill_variants_agree_closely():
+    """Both kernels on the same inputs: the same P rounding and float32 accumulation."""
+    a, ref = _run([512, 384, 256, 128], [512, 384, 256, 128], 32, 8, 128, "BF16", 3, variant=1)
+    b, _ = _run([512, 384, 256, 128], [512, 384, 256, 128], 32, 8, 128, "BF16", 3, variant=2)
+    assert np.max(np.abs(a - b)) <= 1.6e-2
+    assert np.mean(np.abs(a - ref)) <= 2e-3 and np.mean(np.abs(b - ref)) <= 2e-3
 
 
 def test_prefill_bad_indptr_is_flagged():
@@ -116,6 +138,19 @@ def test_prefill_bad_indptr_is_flagged():
     np.testing.assert_allclose(host(out)[:16], ref, rtol=1.5e-2, atol=1e-2)
 
 
+def test_prefill_tcgen05_bad_indptr_is_flagged():
+    from kernelverse_b200 import _lib
+    q = torch.randn((256, 2, 64), device="cuda").to(torch.bfloat16)
+    k = torch.randn((256, 1, 64), device="cuda").to(torch.bfloat16)
+    qo = torch.tensor([0, 128, 256], dtype=torch.int32, device="cuda")
+    kvp = torch.tensor([0, 128, 300], dtype=torch.int32, device="cuda")
+    out = _ops().batched_prefill_attention(q, k, k, qo, kvp, _variant=2)
+    assert _lib.lib().kvb_device_status(1) & 4
+    ref = attention.batched_prefill_attention(host(q)[:128], host(k)[:128], host(k)[:128], np.array([0, 128]),
+                                              np.array([0, 128]), 2, 1, 64 ** -0.5)
+    np.testing.assert_allclose(host(out)[:128], ref, rtol=1.5e-2, atol=1e-2)
+
+
 def test_prefill_rejects_bad_arguments():
     ops = _ops()
     q = torch.randn((8, 4, 64), device="cuda")
@@ -130,3 +165,5 @@ def test_prefill_rejects_bad_arguments():
     k2 = torch.randn((8, 2, 136), device="cuda")
     with pytest.raises(RuntimeError, match="head_dim"):
         ops.batched_prefill_attention(q2, k2, k2, ind, ind)
+    with pytest.raises(RuntimeError, match="tcgen05"):
+        ops.batched_prefill_attention(q, k, k, ind, ind, _variant=2)   # float32 has no tcgen05 kernel
