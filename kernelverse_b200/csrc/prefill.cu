@@ -442,7 +442,7 @@ extern "C" int kvb_batched_prefill_attention_variant(const void* q, const void* 
   // boxes of 64 head elements x 128 tokens, and it stores 16-byte vectors); the rest on the
   // mma.sync kernel.
   const bool tc_ok = (dtype == KVB_BF16 || dtype == KVB_F16) && head_dim % 16 == 0 && head_dim >= 64 &&
-                     total_q >= 128 && total_kv >= 128 && aligned16(out);
+                     total_q >= 128 && total_kv >= 128 && aligned16(out) && softmax_scale != 0.0f;
   if (variant == 2 && !tc_ok) return set_error(KVB_E_SHAPE, "batched_prefill_attention: no tcgen05 kernel for this case");
   if (tc_ok && variant != 1)
     return prefill_tcgen05(q, k, v, dtype == KVB_BF16, qo_indptr, kv_indptr, batch, total_q, total_kv, num_q_heads,

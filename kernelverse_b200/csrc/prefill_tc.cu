@@ -12,7 +12,8 @@
 //              V MN-major), S_{j+1} issued ahead of PV_j so the softmax of tile j+1 overlaps PV_j;
 //   warps 2-5  softmax, one query row per thread (TMEM lane = row): the row max of S_j (scaled to
 //              the log2 domain, causal mask), P = 2^(s - m) rounded to the input type into
-//              shared memory (K-major, 128-byte swizzle), the running sum, and the O rescale; the
+//              shared memory (K-major, 128-byte swizzle, double-buffered so tile j+1's P is
+//              written while PV_j runs), the running sum, and the O rescale; the
 //              max is only moved when it grows by more than 2^8 (the sum and O then scale by
 //              the same factor, so the result is unchanged and most tiles skip the rescale);
 //              finally O / l to global memory.
@@ -102,6 +103,37 @@ __device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&r)[32]) {
       : "r"(taddr));
   asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
 }
+// 32 lanes x 128 consecutive 32-bit columns in one load (one round trip): this thread gets its
+// lane's 128 columns.
+__device__ __forceinline__ void tmem_ld128(uint32_t taddr, uint32_t (&r)[128]) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x128.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16,%17,%18,"
+      "%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31,%32,%33,%34,%35,%36,%37,%38,%39,%40,%41,%42,%43,%44,%45,"
+      "%46,%47,%48,%49,%50,%51,%52,%53,%54,%55,%56,%57,%58,%59,%60,%61,%62,%63,%64,%65,%66,%67,%68,%69,%70,%71,%72,"
+      "%73,%74,%75,%76,%77,%78,%79,%80,%81,%82,%83,%84,%85,%86,%87,%88,%89,%90,%91,%92,%93,%94,%95,%96,%97,%98,%99,"
+      "%100,%101,%102,%103,%104,%105,%106,%107,%108,%109,%110,%111,%112,%113,%114,%115,%116,%117,%118,%119,%120,"
+      "%121,%122,%123,%124,%125,%126,%127}, [%128];\n\t"
+      "tcgen05.wait::ld.sync.aligned;"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]), "=r"(r[8]),
+        "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]), "=r"(r[16]),
+        "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]), "=r"(r[24]),
+        "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31]), "=r"(r[32]),
+        "=r"(r[33]), "=r"(r[34]), "=r"(r[35]), "=r"(r[36]), "=r"(r[37]), "=r"(r[38]), "=r"(r[39]), "=r"(r[40]),
+        "=r"(r[41]), "=r"(r[42]), "=r"(r[43]), "=r"(r[44]), "=r"(r[45]), "=r"(r[46]), "=r"(r[47]), "=r"(r[48]),
+        "=r"(r[49]), "=r"(r[50]), "=r"(r[51]), "=r"(r[52]), "=r"(r[53]), "=r"(r[54]), "=r"(r[55]), "=r"(r[56]),
+        "=r"(r[57]), "=r"(r[58]), "=r"(r[59]), "=r"(r[60]), "=r"(r[61]), "=r"(r[62]), "=r"(r[63]), "=r"(r[64]),
+        "=r"(r[65]), "=r"(r[66]), "=r"(r[67]), "=r"(r[68]), "=r"(r[69]), "=r"(r[70]), "=r"(r[71]), "=r"(r[72]),
+        "=r"(r[73]), "=r"(r[74]), "=r"(r[75]), "=r"(r[76]), "=r"(r[77]), "=r"(r[78]), "=r"(r[79]), "=r"(r[80]),
+        "=r"(r[81]), "=r"(r[82]), "=r"(r[83]), "=r"(r[84]), "=r"(r[85]), "=r"(r[86]), "=r"(r[87]), "=r"(r[88]),
+        "=r"(r[89]), "=r"(r[90]), "=r"(r[91]), "=r"(r[92]), "=r"(r[93]), "=r"(r[94]), "=r"(r[95]), "=r"(r[96]),
+        "=r"(r[97]), "=r"(r[98]), "=r"(r[99]), "=r"(r[100]), "=r"(r[101]), "=r"(r[102]), "=r"(r[103]), "=r"(r[104]),
+        "=r"(r[105]), "=r"(r[106]), "=r"(r[107]), "=r"(r[108]), "=r"(r[109]), "=r"(r[110]), "=r"(r[111]),
+        "=r"(r[112]), "=r"(r[113]), "=r"(r[114]), "=r"(r[115]), "=r"(r[116]), "=r"(r[117]), "=r"(r[118]),
+        "=r"(r[119]), "=r"(r[120]), "=r"(r[121]), "=r"(r[122]), "=r"(r[123]), "=r"(r[124]), "=r"(r[125]),
+        "=r"(r[126]), "=r"(r[127])
+      : "r"(taddr)
+      : "memory");
+}
 __device__ __forceinline__ void tmem_st32(uint32_t taddr, const uint32_t (&r)[32]) {
   asm volatile(
       "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16,"
@@ -134,7 +166,8 @@ __device__ __forceinline__ bool warp_wait(uint64_t* bar, uint32_t parity) {
   return __all_sync(0xffffffffu, ok);
 }
 
-// DC: 64-element chunks of D (1 or 2).  Shared memory: V ring, K ring, Q, P (each chunk 16 KB).
+// DC: 64-element chunks of D (1 or 2).  Shared memory: V ring, K ring, Q, P double buffer (each
+// operand DC chunks of 16 KB, each P buffer two).
 template <typename T, int DC>
 __global__ void __launch_bounds__(kTcThreads, 1) prefill_tc_kernel(const __grid_constant__ CUtensorMap tq,
                                                                    const __grid_constant__ CUtensorMap tk,
@@ -148,7 +181,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) prefill_tc_kernel(const __grid_
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   const uint32_t sbase = smem_u32(smem);
-  __shared__ uint64_t q_full, k_full[2], v_full[2], kv_empty[2], s_full[2], s_free[2], p_full, pv_done, mma_done;
+  __shared__ uint64_t q_full, k_full[2], v_full[2], kv_empty[2], s_full[2], s_free[2], p_full, pv_done[2], mma_done;
   __shared__ uint32_t tmem_base_s;
   __shared__ volatile int s_abort;
 
@@ -164,7 +197,8 @@ __global__ void __launch_bounds__(kTcThreads, 1) prefill_tc_kernel(const __grid_
       mbar_init(&s_free[s], 4);
     }
     mbar_init(&p_full, 4);
-    mbar_init(&pv_done, 1);
+    mbar_init(&pv_done[0], 1);
+    mbar_init(&pv_done[1], 1);
     mbar_init(&mma_done, 1);
     s_abort = 0;
     fence_mbar_init();
@@ -278,11 +312,12 @@ __global__ void __launch_bounds__(kTcThreads, 1) prefill_tc_kernel(const __grid_
         const uint32_t vs = sbase + kV0 + (j & 1) * kOpBytes;
 #pragma unroll
         for (int ks = 0; ks < kTcKeys / 16; ++ks) {
-          const uint32_t pa = sbase + kP0 + (uint32_t)(ks >> 2) * kChunkBytes + (uint32_t)(ks & 3) * 32u;
+          const uint32_t pa = sbase + kP0 + (uint32_t)(j & 1) * 2 * kChunkBytes + (uint32_t)(ks >> 2) * kChunkBytes +
+                              (uint32_t)(ks & 3) * 32u;
           mma_f16(tmem + kO, desc_kmajor(pa), desc_mnmajor(vs + (uint32_t)ks * 2048u, kChunkBytes), id_pv,
                   (j | ks) != 0);
         }
-        mma_commit(&pv_done);
+        mma_commit(&pv_done[j & 1]);
         mma_commit(&kv_empty[j & 1]);
       }
       if (!ok) s_abort = 1;
@@ -295,7 +330,8 @@ __global__ void __launch_bounds__(kTcThreads, 1) prefill_tc_kernel(const __grid_
     const int row = quarter * 32 + lane;                   // query row of the tile = TMEM lane
     const int pos = off + i0 + row;
     const uint32_t lane_addr = (uint32_t)(quarter * 32) << 16;
-    uint8_t* prow = smem + kP0 + row * 128;                // this row in each 64-key chunk of P
+    uint8_t* prow = smem + kP0 + row * 128;                // this row in each 64-key chunk of P buffer 0
+    const float sc = a.scale_log2;
     float m_used = -INFINITY, l = 0.0f;
     bool ok = true;
     for (int j = 0; j < n; ++j) {
@@ -307,59 +343,69 @@ __global__ void __launch_bounds__(kTcThreads, 1) prefill_tc_kernel(const __grid_
       const uint32_t sa = tmem + lane_addr + (uint32_t)(j & 1) * kTcKeys;
       const int kb = j * kTcKeys;
       const bool mask = kb + kTcKeys - 1 > off + i0 + quarter * 32;   // some key of the tile may pass a row
-      // pass 1: the tile's row max (log2 domain)
-      float mx = -INFINITY;
-#pragma unroll 1
-      for (int c = 0; c < 4; ++c) {
-        uint32_t r[32];
-        tmem_ld32(sa + c * 32, r);
+      // the row's 128 scores in one load; S[j % 2] is then free for S_{j+2}
+      uint32_t r[128];
+      tmem_ld128(sa, r);
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&s_free[j & 1]);
+      if (mask) {
 #pragma unroll
-        for (int i = 0; i < 32; ++i) {
-          float v = __uint_as_float(r[i]) * a.scale_log2;
-          if (mask && kb + c * 32 + i > pos) v = -INFINITY;
-          mx = fmaxf(mx, v);
-        }
+        for (int i = 0; i < 128; ++i)
+          if (kb + i > pos) r[i] = __float_as_uint(sc >= 0.0f ? -INFINITY : INFINITY);
       }
+      // the tile's row max in the log2 domain (the raw extreme times the scale)
+      float mx;
+      if (sc >= 0.0f) {
+        float m4[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
+#pragma unroll
+        for (int i = 0; i < 128; ++i) m4[i & 3] = fmaxf(m4[i & 3], __uint_as_float(r[i]));
+        mx = fmaxf(fmaxf(m4[0], m4[1]), fmaxf(m4[2], m4[3]));
+      } else {
+        float m4[4] = {INFINITY, INFINITY, INFINITY, INFINITY};
+#pragma unroll
+        for (int i = 0; i < 128; ++i) m4[i & 3] = fminf(m4[i & 3], __uint_as_float(r[i]));
+        mx = fminf(fminf(m4[0], m4[1]), fminf(m4[2], m4[3]));
+      }
+      mx *= sc;
       const bool grow = mx > m_used + kLazyMax;
       const float alpha = grow ? ex2_approx(m_used - mx) : 1.0f;
       if (grow) m_used = mx;
       l *= alpha;
-      // P may be overwritten and O rescaled once PV_{j-1} has completed
-      if (j > 0) {
-        if (!warp_wait(&pv_done, (j - 1) & 1)) {
+      // P buffer j % 2 is free once PV_{j-2} has completed
+      if (j >= 2) {
+        if (!warp_wait(&pv_done[j & 1], ((j - 2) >> 1) & 1)) {
           ok = false;
           break;
         }
         tc_fence_after();
       }
-      // pass 2: P = 2^(s - m) in the input type, K-major with the 128-byte swizzle
-#pragma unroll 1
-      for (int c = 0; c < 4; ++c) {
-        uint32_t r[32];
-        tmem_ld32(sa + c * 32, r);
-        uint32_t w[16];
+      // P = 2^(s * scale - m) in the input type (masked scores give 2^-inf = 0), K-major with the
+      // 128-byte swizzle
+      const float neg_m = -m_used;
+      float l4[4] = {0.0f, 0.0f, 0.0f, 0.0f};
 #pragma unroll
-        for (int i = 0; i < 32; i += 2) {
-          float v0 = __uint_as_float(r[i]) * a.scale_log2, v1 = __uint_as_float(r[i + 1]) * a.scale_log2;
-          if (mask && kb + c * 32 + i > pos) v0 = -INFINITY;
-          if (mask && kb + c * 32 + i + 1 > pos) v1 = -INFINITY;
-          const float p0 = ex2_approx(v0 - m_used), p1 = ex2_approx(v1 - m_used);
-          l += p0 + p1;
-          w[i >> 1] = pack2h<kBf>(p0, p1);
-        }
-        uint8_t* chunk = prow + (c >> 1) * kChunkBytes;
+      for (int c = 0; c < 16; ++c) {                       // 16-byte column c of the 256-byte P row
+        uint32_t w[4];
 #pragma unroll
         for (int u = 0; u < 4; ++u) {
-          const int col16 = (c & 1) * 4 + u;               // 16-byte column within the 128-byte row
-          *reinterpret_cast<uint4*>(chunk + ((col16 ^ (row & 7)) << 4)) =
-              make_uint4(w[4 * u], w[4 * u + 1], w[4 * u + 2], w[4 * u + 3]);
+          const float p0 = ex2_approx(fmaf(__uint_as_float(r[8 * c + 2 * u]), sc, neg_m));
+          const float p1 = ex2_approx(fmaf(__uint_as_float(r[8 * c + 2 * u + 1]), sc, neg_m));
+          l4[u] += p0 + p1;
+          w[u] = pack2h<kBf>(p0, p1);
         }
+        uint8_t* chunk = prow + (j & 1) * 2 * kChunkBytes + (c >> 3) * kChunkBytes;
+        *reinterpret_cast<uint4*>(chunk + (((c & 7) ^ (row & 7)) << 4)) = make_uint4(w[0], w[1], w[2], w[3]);
       }
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&s_free[j & 1]);
-      // O *= alpha where the max moved (whole warp, when any of its rows needs it)
+      l += (l4[0] + l4[1]) + (l4[2] + l4[3]);
+      // O *= alpha where the max moved (whole warp, when any of its rows needs it), once PV_{j-1}
+      // has completed
       if (j > 0 && __any_sync(0xffffffffu, alpha != 1.0f)) {
+        if (!warp_wait(&pv_done[(j - 1) & 1], ((j - 1) >> 1) & 1)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
         for (int c = 0; c < (D + 31) / 32; ++c) {
           uint32_t r[32];
           tmem_ld32(tmem + lane_addr + kO + c * 32, r);
@@ -375,7 +421,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) prefill_tc_kernel(const __grid_
     }
     if (!ok) s_abort = 1;
     // O / l of the valid rows
-    if (ok && (n == 0 || warp_wait(&pv_done, (n - 1) & 1))) {
+    if (ok && (n == 0 || warp_wait(&pv_done[(n - 1) & 1], ((n - 1) >> 1) & 1))) {
       tc_fence_after();
       const float inv = 1.0f / l;
       const bool valid = i0 + row < ql;
@@ -441,7 +487,7 @@ int make_head_map(CUtensorMap* map, const void* base, bool bf16, int64_t tokens,
 template <typename T, int DC>
 int launch_tc(const CUtensorMap& mq, const CUtensorMap& mk, const CUtensorMap& mv, const TcArgs& a, int tiles_ub,
               cudaStream_t st) {
-  constexpr size_t smem = 5 * (size_t)DC * kChunkBytes + 2 * kChunkBytes + 1024;
+  constexpr size_t smem = 5 * (size_t)DC * kChunkBytes + 4 * kChunkBytes + 1024;
   auto kern = prefill_tc_kernel<T, DC>;
   static int set_dev = -1;
   int dev = 0;
