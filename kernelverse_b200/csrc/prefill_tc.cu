@@ -3,20 +3,21 @@
 // this kernel serves f16 / bf16 with head_dim a multiple of 16 up to 128.
 //
 // One CTA per (128 query rows of one request, one query head), warp-specialised:
-//   warp 0     TMA producer: the Q tile once, then K and V tiles of 128 keys into a 2-deep ring
+//   warp 0     TMA producer: the Q tile once, then K and V tiles of 128 keys into a 3-deep ring
 //              (3-D tensor maps over [tokens, heads, D], boxes of 64 D-elements x 128 tokens with
 //              the 128-byte swizzle; rows past the tensors are zero-filled);
-//   warp 1     allocates TMEM (S double buffer of 2 x 128 columns + O of D columns) and one lane
+//   warp 1     allocates TMEM (three S buffers of 128 columns + O of D columns) and one lane
 //              issues the MMAs: S_j = Q K_j^T (kind::f16, M = 128, N = 128, both K-major) into
-//              S[j % 2], then O += P_j V_j (M = 128, N = D, K = 128; P K-major from shared memory,
-//              V MN-major), S_{j+1} issued ahead of PV_j so the softmax of tile j+1 overlaps PV_j;
-//   warps 2-5  softmax, one query row per thread (TMEM lane = row): the row max of S_j (scaled to
-//              the log2 domain, causal mask), P = 2^(s - m) rounded to the input type into
-//              shared memory (K-major, 128-byte swizzle, double-buffered so tile j+1's P is
-//              written while PV_j runs), the running sum, and the O rescale; the
-//              max is only moved when it grows by more than 2^8 (the sum and O then scale by
-//              the same factor, so the result is unchanged and most tiles skip the rescale);
-//              finally O / l to global memory.
+//              S[j % 3], then O += P_j V_j (M = 128, N = D, K = 128; P read from tensor memory,
+//              where the softmax wrote it over S_j; V MN-major).  S_{j+1} is issued ahead of PV_j,
+//              so the softmax of tile j+1 overlaps PV_j, and with three buffers S_{j+1} never
+//              waits for a PV that is still running;
+//   warps 2-5  softmax, one query row per thread (TMEM lane = row): the row's 128 scores in one
+//              load, the row max (log2 domain, causal mask), P = 2^(s - m) rounded to the input
+//              type and packed two keys per column over the scores, the running sum, and the O
+//              rescale; the max is only moved when it grows by more than 2^8 (the sum and O then
+//              scale by the same factor, so the result is unchanged and most tiles skip the
+//              rescale); finally O / l to global memory.
 // Every mbarrier wait is bounded; on a timeout the roles stop, the producer waits for its own
 // copies, the MMA lane for its MMAs, and the CTA frees its TMEM before exiting.
 #include <cuda.h>
@@ -34,6 +35,7 @@ namespace {
 constexpr int kTcRows = 128;               // query rows per CTA (TMEM lanes)
 constexpr int kTcKeys = 128;               // keys per K/V tile
 constexpr int kTcThreads = 192;            // producer, MMA, four softmax warps
+constexpr int kRing = 3;                   // K / V stages = S / P buffers in TMEM
 constexpr uint32_t kChunkBytes = 16384;    // [128 rows x 64 elements] of a 16-bit operand
 constexpr float kLazyMax = 8.0f;           // log2 growth of the row max that forces a rescale
 constexpr unsigned int kStatusBadIndptrTc = 4u;
@@ -145,6 +147,33 @@ __device__ __forceinline__ void tmem_st32(uint32_t taddr, const uint32_t (&r)[32
       : "memory");
   asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
 }
+// 32 lanes x 64 consecutive 32-bit columns stored in one instruction.
+__device__ __forceinline__ void tmem_st64(uint32_t taddr, const uint32_t (&r)[64]) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x64.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16,%17,%18,"
+      "%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31,%32,%33,%34,%35,%36,%37,%38,%39,%40,%41,%42,%43,%44,%45,"
+      "%46,%47,%48,%49,%50,%51,%52,%53,%54,%55,%56,%57,%58,%59,%60,%61,%62,%63,%64};\n\t"
+      "tcgen05.wait::st.sync.aligned;"
+      ::"r"(taddr), "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]),
+        "r"(r[8]), "r"(r[9]), "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]), "r"(r[15]), "r"(r[16]),
+        "r"(r[17]), "r"(r[18]), "r"(r[19]), "r"(r[20]), "r"(r[21]), "r"(r[22]), "r"(r[23]), "r"(r[24]), "r"(r[25]),
+        "r"(r[26]), "r"(r[27]), "r"(r[28]), "r"(r[29]), "r"(r[30]), "r"(r[31]), "r"(r[32]), "r"(r[33]), "r"(r[34]),
+        "r"(r[35]), "r"(r[36]), "r"(r[37]), "r"(r[38]), "r"(r[39]), "r"(r[40]), "r"(r[41]), "r"(r[42]), "r"(r[43]),
+        "r"(r[44]), "r"(r[45]), "r"(r[46]), "r"(r[47]), "r"(r[48]), "r"(r[49]), "r"(r[50]), "r"(r[51]), "r"(r[52]),
+        "r"(r[53]), "r"(r[54]), "r"(r[55]), "r"(r[56]), "r"(r[57]), "r"(r[58]), "r"(r[59]), "r"(r[60]), "r"(r[61]),
+        "r"(r[62]), "r"(r[63])
+      : "memory");
+}
+// tcgen05.mma kind::f16 with A (M = 128 lanes x 16 K-elements, two 16-bit elements per 32-bit
+// column, the lower K index in the low half) read from tensor memory.
+__device__ __forceinline__ void mma_f16_ts(uint32_t tmem_d, uint32_t tmem_a, uint64_t bdesc, uint32_t idesc, uint32_t accum) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, {%5, %6, %7, %8}, p;\n\t}"
+      ::"r"(tmem_d), "r"(tmem_a), "l"(bdesc), "r"(idesc), "r"(accum), "r"(0), "r"(0), "r"(0), "r"(0)
+      : "memory");
+}
 __device__ __forceinline__ float ex2_approx(float x) {   // 2^x (MUFU.EX2; ex2(-inf) = +0)
   float y;
   asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
@@ -166,8 +195,8 @@ __device__ __forceinline__ bool warp_wait(uint64_t* bar, uint32_t parity) {
   return __all_sync(0xffffffffu, ok);
 }
 
-// DC: 64-element chunks of D (1 or 2).  Shared memory: V ring, K ring, Q, P double buffer (each
-// operand DC chunks of 16 KB, each P buffer two).
+// DC: 64-element chunks of D (1 or 2).  Shared memory: V ring, K ring and Q, each stage DC
+// chunks of 16 KB.
 template <typename T, int DC>
 __global__ void __launch_bounds__(kTcThreads, 1) prefill_tc_kernel(const __grid_constant__ CUtensorMap tq,
                                                                    const __grid_constant__ CUtensorMap tk,
@@ -175,13 +204,14 @@ __global__ void __launch_bounds__(kTcThreads, 1) prefill_tc_kernel(const __grid_
                                                                    const __grid_constant__ TcArgs a) {
   constexpr bool kBf = std::is_same<T, __nv_bfloat16>::value;
   constexpr uint32_t kOpBytes = DC * kChunkBytes;          // one Q / K / V tile
-  constexpr uint32_t kV0 = 0, kK0 = 2 * kOpBytes, kQ0 = 4 * kOpBytes, kP0 = 5 * kOpBytes;
+  constexpr uint32_t kV0 = 0, kK0 = kRing * kOpBytes, kQ0 = 2 * kRing * kOpBytes;
   constexpr uint32_t kTmemCols = 512;
-  constexpr uint32_t kO = 2 * kTcKeys;                      // O's first TMEM column
+  constexpr uint32_t kO = kRing * kTcKeys;                  // O's first TMEM column (after the S buffers)
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   const uint32_t sbase = smem_u32(smem);
-  __shared__ uint64_t q_full, k_full[2], v_full[2], kv_empty[2], s_full[2], s_free[2], p_full, pv_done[2], mma_done;
+  __shared__ uint64_t q_full, k_full[kRing], v_full[kRing], kv_empty[kRing], s_full[kRing], pv_done[kRing], p_full,
+      mma_done;
   __shared__ uint32_t tmem_base_s;
   __shared__ volatile int s_abort;
 
@@ -189,16 +219,14 @@ __global__ void __launch_bounds__(kTcThreads, 1) prefill_tc_kernel(const __grid_
   const int h = blockIdx.x;
   if (threadIdx.x == 0) {
     mbar_init(&q_full, 1);
-    for (int s = 0; s < 2; ++s) {
+    for (int s = 0; s < kRing; ++s) {
       mbar_init(&k_full[s], 1);
       mbar_init(&v_full[s], 1);
       mbar_init(&kv_empty[s], 1);
       mbar_init(&s_full[s], 1);
-      mbar_init(&s_free[s], 4);
+      mbar_init(&pv_done[s], 1);
     }
     mbar_init(&p_full, 4);
-    mbar_init(&pv_done[0], 1);
-    mbar_init(&pv_done[1], 1);
     mbar_init(&mma_done, 1);
     s_abort = 0;
     fence_mbar_init();
@@ -256,9 +284,8 @@ __global__ void __launch_bounds__(kTcThreads, 1) prefill_tc_kernel(const __grid_
       mbar_arrive_expect_tx(&q_full, kOpBytes);
       for (int c = 0; c < DC; ++c) tma_load_3d(sbase + kQ0 + c * kChunkBytes, &tq, c * 64, h, q0 + i0, &q_full);
       int issued = 0;
-      for (int j = 0; j < n; ++j) {
-        const int s = j & 1;
-        if (j >= 2 && !mbar_wait_bounded(&kv_empty[s], ((j >> 1) - 1) & 1)) {
+      for (int j = 0, s = 0, ph = 0; j < n; ++j) {            // stage s = j % kRing, ph = (j / kRing) & 1
+        if (j >= kRing && !mbar_wait_bounded(&kv_empty[s], ph ^ 1)) {
           s_abort = 1;
           break;
         }
@@ -271,12 +298,16 @@ __global__ void __launch_bounds__(kTcThreads, 1) prefill_tc_kernel(const __grid_
         for (int c = 0; c < DC; ++c)
           tma_load_3d(sbase + kV0 + s * kOpBytes + c * kChunkBytes, &tv, c * 64, kvh, kt, &v_full[s]);
         issued = j + 1;
+        if (++s == kRing) {
+          s = 0;
+          ph ^= 1;
+        }
       }
       // every copy this CTA issued has landed before it exits
       mbar_wait_bounded(&q_full, 0);
-      for (int j = issued > 2 ? issued - 2 : 0; j < issued; ++j) {
-        mbar_wait_bounded(&k_full[j & 1], (j >> 1) & 1);
-        mbar_wait_bounded(&v_full[j & 1], (j >> 1) & 1);
+      for (int j = issued > kRing ? issued - kRing : 0; j < issued; ++j) {
+        mbar_wait_bounded(&k_full[j % kRing], (j / kRing) & 1);
+        mbar_wait_bounded(&v_full[j % kRing], (j / kRing) & 1);
       }
     }
   } else if (warp == 1) {
@@ -285,10 +316,13 @@ __global__ void __launch_bounds__(kTcThreads, 1) prefill_tc_kernel(const __grid_
       constexpr uint32_t kIdS = idesc_f16(kTcRows, kTcKeys, kBf, false);
       const uint32_t id_pv = idesc_f16(kTcRows, D, kBf, true);
       const int ksteps = D / 16;
+      // S_j into S buffer j % kRing once K_j has landed and PV_{j-kRing} has consumed the P that
+      // buffer held
       auto issue_s = [&](int j) -> bool {
-        const int s = j & 1;
-        if (!mbar_wait_bounded(&k_full[s], (j >> 1) & 1)) return false;
-        if (j >= 2 && !mbar_wait_bounded(&s_free[s], ((j >> 1) - 1) & 1)) return false;
+        const int s = j % kRing;
+        const uint32_t ph = (uint32_t)(j / kRing) & 1u;
+        if (!mbar_wait_bounded(&k_full[s], ph)) return false;
+        if (j >= kRing && !mbar_wait_bounded(&pv_done[s], ph ^ 1u)) return false;
         tc_fence_after();
         for (int ks = 0; ks < ksteps; ++ks) {
           const uint32_t off_b = (uint32_t)(ks >> 2) * kChunkBytes + (uint32_t)(ks & 3) * 32u;
@@ -304,21 +338,19 @@ __global__ void __launch_bounds__(kTcThreads, 1) prefill_tc_kernel(const __grid_
           ok = false;
           break;
         }
-        if (!mbar_wait_bounded(&p_full, j & 1) || !mbar_wait_bounded(&v_full[j & 1], (j >> 1) & 1)) {
+        const int s = j % kRing;
+        if (!mbar_wait_bounded(&p_full, j & 1) || !mbar_wait_bounded(&v_full[s], (j / kRing) & 1)) {
           ok = false;
           break;
         }
         tc_fence_after();
-        const uint32_t vs = sbase + kV0 + (j & 1) * kOpBytes;
+        const uint32_t vs = sbase + kV0 + s * kOpBytes;
 #pragma unroll
-        for (int ks = 0; ks < kTcKeys / 16; ++ks) {
-          const uint32_t pa = sbase + kP0 + (uint32_t)(j & 1) * 2 * kChunkBytes + (uint32_t)(ks >> 2) * kChunkBytes +
-                              (uint32_t)(ks & 3) * 32u;
-          mma_f16(tmem + kO, desc_kmajor(pa), desc_mnmajor(vs + (uint32_t)ks * 2048u, kChunkBytes), id_pv,
-                  (j | ks) != 0);
-        }
-        mma_commit(&pv_done[j & 1]);
-        mma_commit(&kv_empty[j & 1]);
+        for (int ks = 0; ks < kTcKeys / 16; ++ks)   // P_j: 16 keys = 8 packed columns of S buffer s
+          mma_f16_ts(tmem + kO, tmem + (uint32_t)s * kTcKeys + (uint32_t)ks * 8u,
+                     desc_mnmajor(vs + (uint32_t)ks * 2048u, kChunkBytes), id_pv, (j | ks) != 0);
+        mma_commit(&pv_done[s]);
+        mma_commit(&kv_empty[s]);
       }
       if (!ok) s_abort = 1;
       mma_commit(&mma_done);                 // every MMA issued above has completed before TMEM is freed
@@ -330,25 +362,22 @@ __global__ void __launch_bounds__(kTcThreads, 1) prefill_tc_kernel(const __grid_
     const int row = quarter * 32 + lane;                   // query row of the tile = TMEM lane
     const int pos = off + i0 + row;
     const uint32_t lane_addr = (uint32_t)(quarter * 32) << 16;
-    uint8_t* prow = smem + kP0 + row * 128;                // this row in each 64-key chunk of P buffer 0
     const float sc = a.scale_log2;
     float m_used = -INFINITY, l = 0.0f;
     bool ok = true;
     for (int j = 0; j < n; ++j) {
-      if (__shfl_sync(0xffffffffu, s_abort, 0) || !warp_wait(&s_full[j & 1], (j >> 1) & 1)) {   // warp-uniform
+      const int sb = j % kRing;                            // S / P buffer of tile j
+      if (__shfl_sync(0xffffffffu, s_abort, 0) || !warp_wait(&s_full[sb], (j / kRing) & 1)) {   // warp-uniform
         ok = false;
         break;
       }
       tc_fence_after();
-      const uint32_t sa = tmem + lane_addr + (uint32_t)(j & 1) * kTcKeys;
+      const uint32_t sa = tmem + lane_addr + (uint32_t)sb * kTcKeys;
       const int kb = j * kTcKeys;
       const bool mask = kb + kTcKeys - 1 > off + i0 + quarter * 32;   // some key of the tile may pass a row
-      // the row's 128 scores in one load; S[j % 2] is then free for S_{j+2}
+      // the row's 128 scores in one load
       uint32_t r[128];
       tmem_ld128(sa, r);
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&s_free[j & 1]);
       if (mask) {
 #pragma unroll
         for (int i = 0; i < 128; ++i)
@@ -372,36 +401,24 @@ __global__ void __launch_bounds__(kTcThreads, 1) prefill_tc_kernel(const __grid_
       const float alpha = grow ? ex2_approx(m_used - mx) : 1.0f;
       if (grow) m_used = mx;
       l *= alpha;
-      // P buffer j % 2 is free once PV_{j-2} has completed
-      if (j >= 2) {
-        if (!warp_wait(&pv_done[j & 1], ((j - 2) >> 1) & 1)) {
-          ok = false;
-          break;
-        }
-        tc_fence_after();
-      }
-      // P = 2^(s * scale - m) in the input type (masked scores give 2^-inf = 0), K-major with the
-      // 128-byte swizzle
+      // P = 2^(s * scale - m) in the input type (masked scores give 2^-inf = 0), two keys per
+      // 32-bit column over the first 64 columns of the row's scores: the A operand of PV_j
       const float neg_m = -m_used;
       float l4[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+      uint32_t w[64];
 #pragma unroll
-      for (int c = 0; c < 16; ++c) {                       // 16-byte column c of the 256-byte P row
-        uint32_t w[4];
-#pragma unroll
-        for (int u = 0; u < 4; ++u) {
-          const float p0 = ex2_approx(fmaf(__uint_as_float(r[8 * c + 2 * u]), sc, neg_m));
-          const float p1 = ex2_approx(fmaf(__uint_as_float(r[8 * c + 2 * u + 1]), sc, neg_m));
-          l4[u] += p0 + p1;
-          w[u] = pack2h<kBf>(p0, p1);
-        }
-        uint8_t* chunk = prow + (j & 1) * 2 * kChunkBytes + (c >> 3) * kChunkBytes;
-        *reinterpret_cast<uint4*>(chunk + (((c & 7) ^ (row & 7)) << 4)) = make_uint4(w[0], w[1], w[2], w[3]);
+      for (int i = 0; i < 128; i += 2) {
+        const float p0 = ex2_approx(fmaf(__uint_as_float(r[i]), sc, neg_m));
+        const float p1 = ex2_approx(fmaf(__uint_as_float(r[i + 1]), sc, neg_m));
+        l4[(i >> 1) & 3] += p0 + p1;
+        w[i >> 1] = pack2h<kBf>(p0, p1);
       }
+      tmem_st64(sa, w);
       l += (l4[0] + l4[1]) + (l4[2] + l4[3]);
       // O *= alpha where the max moved (whole warp, when any of its rows needs it), once PV_{j-1}
       // has completed
       if (j > 0 && __any_sync(0xffffffffu, alpha != 1.0f)) {
-        if (!warp_wait(&pv_done[(j - 1) & 1], ((j - 1) >> 1) & 1)) {
+        if (!warp_wait(&pv_done[(j - 1) % kRing], ((j - 1) / kRing) & 1)) {
           ok = false;
           break;
         }
@@ -414,14 +431,13 @@ __global__ void __launch_bounds__(kTcThreads, 1) prefill_tc_kernel(const __grid_
           tmem_st32(tmem + lane_addr + kO + c * 32, r);
         }
       }
-      asm volatile("fence.proxy.async.shared::cta;" ::: "memory");   // P visible to the tensor core
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&p_full);
     }
     if (!ok) s_abort = 1;
     // O / l of the valid rows
-    if (ok && (n == 0 || warp_wait(&pv_done[(n - 1) & 1], ((n - 1) >> 1) & 1))) {
+    if (ok && (n == 0 || warp_wait(&pv_done[(n - 1) % kRing], ((n - 1) / kRing) & 1))) {
       tc_fence_after();
       const float inv = 1.0f / l;
       const bool valid = i0 + row < ql;
@@ -487,7 +503,7 @@ int make_head_map(CUtensorMap* map, const void* base, bool bf16, int64_t tokens,
 template <typename T, int DC>
 int launch_tc(const CUtensorMap& mq, const CUtensorMap& mk, const CUtensorMap& mv, const TcArgs& a, int tiles_ub,
               cudaStream_t st) {
-  constexpr size_t smem = 5 * (size_t)DC * kChunkBytes + 4 * kChunkBytes + 1024;
+  constexpr size_t smem = (2 * kRing + 1) * (size_t)DC * kChunkBytes + 1024;
   auto kern = prefill_tc_kernel<T, DC>;
   static int set_dev = -1;
   int dev = 0;
