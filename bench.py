@@ -494,6 +494,33 @@ def secondary_benchmarks(torch, ops, hbm_peak):
     return out
 
 
+def prefill_benchmarks(torch, ops, bf16_peak):
+    """Packed causal prefill (batched_prefill_attention) at the reference's default shape and
+    its long full-prefill sweep point; FLOPs count the causal (q, k) pairs only."""
+    dev = torch.device("cuda")
+    out = []
+    for ql, dt in (([512, 384, 256, 128], torch.bfloat16), ([2048, 1536, 1024, 512], torch.bfloat16),
+                   ([512, 384, 256, 128], torch.float32)):
+        hq, hkv, d = 32, 8, 128
+        g = torch.Generator(device=dev).manual_seed(31)
+        tq = sum(ql)
+        q = torch.randn((tq, hq, d), generator=g, device=dev).to(dt)
+        k = torch.randn((tq, hkv, d), generator=g, device=dev).to(dt)
+        v = torch.randn((tq, hkv, d), generator=g, device=dev).to(dt)
+        ind = torch.tensor([0] + [sum(ql[:i + 1]) for i in range(len(ql))], dtype=torch.int32, device=dev)
+        us = time_fn(torch, lambda: ops.batched_prefill_attention(q, k, v, ind, ind), 20)
+        flops = 4 * sum(n * (n + 1) // 2 for n in ql) * hq * d
+        e = {"workload": f"batched_prefill_attention q_lens=kv_lens={ql}, 32/8 heads, D=128, "
+                         f"{'bf16' if dt == torch.bfloat16 else 'fp32'}",
+             "kernel": "prefill_kernel (mma.sync m16n8k16 bf16" + (")" if dt == torch.bfloat16 else "; 3xTF32 m16n8k8)"),
+             "us_per_call": round(us, 2), "tflops": round(flops / us / 1e6, 1), "flops_per_call": flops}
+        if dt == torch.bfloat16:
+            e["frac_of_bf16_peak"] = round(flops / us / 1e6 / bf16_peak, 4)
+        out.append(e)
+        del q, k, v
+    return out
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -504,7 +531,8 @@ def main():
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--profile-only", action="store_true",
                     help="run W warm-up + K steps of the headline kernel and exit (for ncu captures)")
-    ap.add_argument("--profile-workload", choices=["c1", "c2", "c4", "c3m16", "c3m256", "c3m4096"], default="c2",
+    ap.add_argument("--profile-workload", choices=["c1", "c2", "c4", "c3m16", "c3m256", "c3m4096", "prefill"],
+                    default="c2",
                     help="workload that --profile-only runs")
     args = ap.parse_args()
     if args.warmup < 3:
@@ -513,7 +541,7 @@ def main():
     rank = int(os.environ.get("RANK", "0"))
     world = int(os.environ.get("WORLD_SIZE", "1"))
     local = int(os.environ.get("LOCAL_RANK", "0"))
-    hbm_peak, _, peak_kind = peaks()
+    hbm_peak, bf16_peak, peak_kind = peaks()
     config = {"workload": "fused residual add + RMSNorm + per-token e4m3 quant, bf16 [8192, 8192] per GPU "
                           "(BASELINE config 2)",
               "rows_per_gpu": M_ROWS, "hidden": HIDDEN, "eps": EPS, "global_rows": M_ROWS * world,
@@ -561,6 +589,17 @@ def main():
                                              c["bt"], k_new=c["k_new"], v_new=c["v_new"], max_seq_len=c["max_len"])
         for _ in range(args.warmup + args.steps):
             step4()
+        torch.cuda.synchronize()
+        return
+    if args.profile_only and args.profile_workload == "prefill":
+        ql = [2048, 1536, 1024, 512]
+        g5 = torch.Generator(device=dev).manual_seed(31)
+        q5 = torch.randn((sum(ql), 32, 128), generator=g5, device=dev).to(torch.bfloat16)
+        k5 = torch.randn((sum(ql), 8, 128), generator=g5, device=dev).to(torch.bfloat16)
+        v5 = torch.randn((sum(ql), 8, 128), generator=g5, device=dev).to(torch.bfloat16)
+        ind = torch.tensor([0, 2048, 3584, 4608, 5120], dtype=torch.int32, device=dev)
+        for _ in range(args.warmup + args.steps):
+            ops.batched_prefill_attention(q5, k5, v5, ind, ind)
         torch.cuda.synchronize()
         return
     if args.profile_only and args.profile_workload.startswith("c3m"):
@@ -626,7 +665,8 @@ def main():
 
     secondary = None
     if world == 1 and not args.no_secondary:
-        secondary = secondary_benchmarks(torch, ops, hbm_peak) + gemm_benchmarks(torch, ops, hbm_peak)
+        secondary = (secondary_benchmarks(torch, ops, hbm_peak) + gemm_benchmarks(torch, ops, hbm_peak) +
+                     prefill_benchmarks(torch, ops, bf16_peak))
     elif world > 1 and not args.no_secondary:
         secondary = multi_gpu_benchmarks(torch, ops, dist, world, rank, hbm_peak)
 
