@@ -180,7 +180,7 @@ KVB_API int kvb_w8a8_scaled_mm_allgather(const int8_t* a, const int8_t* b_shard,
 
 /*
  * W8A8 GEMM with a gated-activation epilogue: the gate+up projection of an MLP followed by
- * SwiGLU in one kernel (SURVEY "next" row: operators/activation/swiglu/swiglu.py:24-28 and
+ * SwiGLU in one kernel (operators/activation/swiglu/swiglu.py:24-28 and
  * operators/activation/mul_and_silu/mul_and_silu.py:24-29 applied to this GEMM's output).
  * b_nk [N, K] holds the two operand weights with their rows interleaved in blocks of 128:
  * rows [256 j, 256 j + 128) are rows [128 j, 128 j + 128) of the first operand's weight and

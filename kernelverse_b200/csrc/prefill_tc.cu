@@ -210,7 +210,10 @@ __global__ void __launch_bounds__(kTcThreads, 1) prefill_tc_kernel(const __grid_
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   const uint32_t sbase = smem_u32(smem);
-  __shared__ uint64_t q_full, k_full[kRing], v_full[kRing], kv_empty[kRing], s_full[kRing], pv_done[kRing], p_full,
+  // One P-ready barrier per buffer (like S and PV): with a single one, a softmax that finished
+  // tile j+1 before the MMA lane had seen tile j would complete two phases and the MMA lane
+  // would wait for a third.
+  __shared__ uint64_t q_full, k_full[kRing], v_full[kRing], kv_empty[kRing], s_full[kRing], pv_done[kRing], p_full[kRing],
       mma_done;
   __shared__ uint32_t tmem_base_s;
   __shared__ volatile int s_abort;
@@ -226,7 +229,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) prefill_tc_kernel(const __grid_
       mbar_init(&s_full[s], 1);
       mbar_init(&pv_done[s], 1);
     }
-    mbar_init(&p_full, 4);
+    for (int s = 0; s < kRing; ++s) mbar_init(&p_full[s], 4);
     mbar_init(&mma_done, 1);
     s_abort = 0;
     fence_mbar_init();
@@ -339,7 +342,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) prefill_tc_kernel(const __grid_
           break;
         }
         const int s = j % kRing;
-        if (!mbar_wait_bounded(&p_full, j & 1) || !mbar_wait_bounded(&v_full[s], (j / kRing) & 1)) {
+        if (!mbar_wait_bounded(&p_full[s], (j / kRing) & 1) || !mbar_wait_bounded(&v_full[s], (j / kRing) & 1)) {
           ok = false;
           break;
         }
@@ -433,7 +436,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) prefill_tc_kernel(const __grid_
       }
       tc_fence_before();
       __syncwarp();
-      if (lane == 0) mbar_arrive(&p_full);
+      if (lane == 0) mbar_arrive(&p_full[sb]);
     }
     if (!ok) s_abort = 1;
     // O / l of the valid rows
