@@ -19,12 +19,17 @@ sharded across GPUs with no collective on the data path: weak scaling).
 * ``roofline``: the fused kernel's achieved GB/s against the measured HBM copy
   bandwidth; ``traffic`` is the DRAM bytes of one launch from the committed ncu
   summary.
-* ``cpu_baseline``: the numpy oracle (a port of the reference's CPU algorithm)
-  timed on this host's cores on a bounded row sample.
+* ``cpu_baseline``: the reference's own CPU code for the step -- its ``add_rmsnorm``
+  ``Model.forward`` (performance mode) plus the per-row e4m3 quantisation, CPU torch on all
+  host threads -- imported from ``baseline/_ref`` (``baseline/install_ref.py``); the numpy
+  port in ``oracle/`` when that install is absent.  Rank 0 at N=1 only.
 * ``secondary``: the other hot-path kernels at their BASELINE configs (N=1 only).
+* ``sharded_config5``: the fifth config at every N, including N=1: the column-sharded TP
+  GEMM (fused all-gather, GEMM + NCCL, shard GEMM) and the batch-512 decode, each with the
+  single-GPU time T1 measured in the same run and the efficiency T1 / (N T_N).
 
-``--impl reference`` times the reference algorithm's CPU port on the host cores
-(rank 0 only) for the same metric and prints it with ``"impl": "reference"``.
+``--impl reference`` runs the same reference CPU code on the host cores (rank 0 only) for
+``--warmup`` + ``--steps`` steps and prints the same metric with ``"impl": "reference"``.
 """
 from __future__ import annotations
 
@@ -137,6 +142,97 @@ class ClockSampler:
 
 
 # ------------------------------------------------------------------------------------------ CPU leg
+REF_DIR = ROOT / "baseline" / "_ref"          # the reference, installed by baseline/install_ref.py
+MIN_SCALING_FACTOR = 1.0 / (448.0 * 512.0)    # operators/quantization/dynamic_scaled_int8_quant/helpers.py:8
+
+
+def host_threads() -> int:
+    return len(os.sched_getaffinity(0)) if hasattr(os, "sched_getaffinity") else (os.cpu_count() or 1)
+
+
+def cpu_model() -> str:
+    try:
+        for line in Path("/proc/cpuinfo").read_text().splitlines():
+            if line.startswith("model name"):
+                return line.split(":", 1)[1].strip()
+    except OSError:
+        pass
+    return "unknown"
+
+
+def reference_cpu_step(rows: int):
+    """One step of the headline workload through the reference's own CPU code, or None.
+
+    The reference's ``add_rmsnorm.Model.forward``
+    (operators/normalization/add_rmsnorm/add_rmsnorm.py:24-35) in its performance compute mode
+    (native bf16, :17-22) on CPU torch with all host threads, composed with the updated residual
+    (``x + residual`` in bf16) and the per-row e4m3 quantisation of the BASELINE second config
+    (scale = max(amax / 448, 1/(448*512)); codes = e4m3fn(clamp(y / scale, +-448))).  Returns
+    (step function, description) over ``rows`` rows of the [8192, 8192] workload.
+    """
+    if not (REF_DIR / "operators" / "registry.py").exists():
+        return None
+    import torch
+    torch.set_num_threads(host_threads())
+    if str(REF_DIR) not in sys.path:
+        sys.path.insert(0, str(REF_DIR))
+    from operators.normalization.add_rmsnorm.add_rmsnorm import Model
+    model = Model({"shape": [rows, HIDDEN], "eps": EPS, "dtype": "BF16", "_baseline_compute_mode": "performance"})
+    g = torch.Generator().manual_seed(1234)
+    x = torch.randn((rows, HIDDEN), generator=g).to(torch.bfloat16)
+    r = torch.randn((rows, HIDDEN), generator=g).to(torch.bfloat16)
+    w = (1.0 + 0.02 * torch.randn((HIDDEN,), generator=g)).to(torch.bfloat16)
+
+    def step():
+        with torch.no_grad():
+            r_out = x + r
+            y = model(x, r, w).float()
+            scale = (y.abs().amax(dim=-1, keepdim=True) / 448.0).clamp_min(MIN_SCALING_FACTOR)
+            codes = (y / scale).clamp(-448.0, 448.0).to(torch.float8_e4m3fn)
+        return r_out, codes, scale
+
+    return step, ("reference add_rmsnorm.Model.forward (performance mode, bf16) + x+residual + per-row "
+                  f"e4m3 quant, CPU torch {torch.__version__}, {torch.get_num_threads()} threads")
+
+
+def reference_cpu_run(warmup: int, steps: int, step_budget_s: float = 1.5):
+    """Time ``warmup`` + ``steps`` steps of the reference's CPU path (numpy port if absent).
+
+    A step is one pass over the full [8192, 8192] batch when that takes under ``step_budget_s``
+    on this host; otherwise over the largest power-of-two row sample that does, so that the
+    whole run stays within a few minutes.  Returns a dict with the throughput and what was run.
+    """
+    threads = host_threads()
+    rows = M_ROWS
+    leg = reference_cpu_step(rows)
+    if leg is None:                      # the reference is not installed: time the numpy port
+        tbs, cores, sample = cpu_port_throughput(budget_s=max(3.0, step_budget_s * (warmup + steps)))
+        return {"tbs": tbs, "cores": cores, "kind": "port", "sample": sample, "steps_run": 1, "rows": M_ROWS,
+                "ms_per_step": c2_bytes(M_ROWS, HIDDEN) / (tbs * 1e12) * 1e3}
+    step, desc = leg
+    step()                               # first call: allocator and thread-pool start-up
+    t0 = time.perf_counter()
+    step()
+    one = time.perf_counter() - t0
+    while one > step_budget_s and rows > 64:
+        rows //= 2
+        one /= 2
+    if rows != M_ROWS:
+        step, desc = reference_cpu_step(rows)
+    for _ in range(max(warmup - 2, 0)):
+        step()
+    t0 = time.perf_counter()
+    for _ in range(steps):
+        step()
+    dt = time.perf_counter() - t0
+    ms = dt / steps * 1e3
+    tbs = c2_bytes(rows, HIDDEN) / (dt / steps) / 1e12
+    sample = (f"{steps} timed steps (+{warmup} warm-up) of {rows} of {M_ROWS} rows x {HIDDEN} each, "
+              f"{dt:.2f} s timed; {desc}; host CPU: {cpu_model()}")
+    return {"tbs": tbs, "cores": threads, "kind": "reference", "sample": sample, "steps_run": steps, "rows": rows,
+            "ms_per_step": ms}
+
+
 def cpu_port_throughput(budget_s: float = 12.0, rows_per_task: int = 64):
     """Time the oracle (numpy port of the reference algorithm) on a bounded row sample.
 
@@ -334,26 +430,29 @@ def gemm_benchmarks(torch, ops, hbm_peak):
     return res
 
 
-def multi_gpu_benchmarks(torch, ops, dist, world: int, rank: int, hbm_peak: float):
-    """N > 1: TP W8A8 GEMM (fused all-gather vs GEMM + NCCL all-gather) and balanced batch-sharded decode.
+PEER_COPY_GBS = 770.0      # measured NVLink peer-copy bandwidth per direction on this pool's B200s
 
-    BASELINE fifth config: M = 4096, K = 8192, N = 57344 split by columns; decode at batch 512 with
-    the fourth config's head layout and context distribution, sequences balanced by context length.
-    Times are device times (CUDA events), max over ranks.
+
+def sharded_benchmarks(torch, ops, dist, world: int, rank: int, hbm_peak: float):
+    """BASELINE fifth config at every N, including N = 1.
+
+    (a) Column-sharded TP W8A8 GEMM, M = 4096, K = 8192, N = 57344 (the gate+up projection):
+        T1 = the whole GEMM on one GPU (every rank runs it on its own GPU at the same time; max
+        over ranks); at N > 1 the fused GEMM + all-gather (kvb_w8a8_scaled_mm_allgather), the
+        GEMM + NCCL all_gather_into_tensor, and the shard GEMM alone.  Efficiency = T1 / (N T_N)
+        (strong scaling: the total work is fixed).  The limiter of the fused kernel is NVLink
+        ingress: each rank receives (N - 1) / N of the 470 MB output.
+    (b) The same with SwiGLU in the epilogue (half the gathered bytes).
+    (c) Paged FP8 decode at batch 512, the fourth config's head layout and context
+        distribution; T1 = all 512 sequences on one GPU; at N > 1 each rank its share balanced
+        by context length.  The limiter is the heaviest rank's KV bytes (max / mean of the
+        per-rank context sums).
+    All times are device times (CUDA events), max over ranks.
     """
     from kernelverse_b200.sharding import TPW8A8, balance_sequences, column_shard
     dev = torch.device("cuda", torch.cuda.current_device())
     res = []
     M, N, K = 4096, 57344, 8192
-    g = torch.Generator(device=dev).manual_seed(5)
-    a = torch.randint(-127, 128, (M, K), generator=g, device=dev, dtype=torch.int8)
-    sa = torch.rand((M,), generator=g, device=dev) * 9e-3 + 1e-3
-    n0, nw = column_shard(N, world, rank)
-    gr = torch.Generator(device=dev).manual_seed(100 + rank)
-    b = torch.randint(-127, 128, (nw, K), generator=gr, device=dev, dtype=torch.int8)
-    sb = torch.rand((nw,), generator=gr, device=dev) * 9e-3 + 1e-3
-    bias = (0.1 * torch.randn((nw,), generator=gr, device=dev)).to(torch.bfloat16)
-    tp = TPW8A8(dist.group.WORLD, M, b, sb, bias)
 
     def timed(fn, iters):
         for _ in range(3):
@@ -361,50 +460,89 @@ def multi_gpu_benchmarks(torch, ops, dist, world: int, rank: int, hbm_peak: floa
         ms, _, _ = time_region(torch, fn, iters, dist, world)
         return ms / iters * 1e3
 
-    us_fused = timed(lambda: tp(a, sa), 10)
-    gathered = torch.empty((world, M, nw), dtype=torch.bfloat16, device=dev)
+    def eff(t1, tn):
+        return round(t1 / (world * tn), 4)
 
-    def nccl_step():
-        local = ops.w8a8_scaled_mm(a, b, sa, sb, bias)
-        dist.all_gather_into_tensor(gathered, local)
-    us_nccl = timed(nccl_step, 10)
-    us_gemm = timed(lambda: ops.w8a8_scaled_mm(a, b, sa, sb, bias), 10)
+    g = torch.Generator(device=dev).manual_seed(5)       # identical tensors on every rank
+    a = torch.randint(-127, 128, (M, K), generator=g, device=dev, dtype=torch.int8)
+    sa = torch.rand((M,), generator=g, device=dev) * 9e-3 + 1e-3
+    b_full = torch.randint(-127, 128, (N, K), generator=g, device=dev, dtype=torch.int8)
+    sb_full = torch.rand((N,), generator=g, device=dev) * 9e-3 + 1e-3
+    bias_full = (0.1 * torch.randn((N,), generator=g, device=dev)).to(torch.bfloat16)
+    t1 = timed(lambda: ops.w8a8_scaled_mm(a, b_full, sa, sb_full, bias_full), 10)
+    t1_act = timed(lambda: ops.w8a8_scaled_mm_act(a, b_full, sa, sb_full, bias_full, "swiglu"), 10)
     ops_total = 2 * M * N * K
-    recv = (world - 1) * M * nw * 2
-    res.append({"workload": f"TP W8A8 GEMM M={M}, N={N} (x{world} column shards of {nw}), K={K}, bf16 out "
-                            "(BASELINE config 5a)",
-                "us_fused_gemm_allgather": round(us_fused, 1), "us_gemm_then_nccl_allgather": round(us_nccl, 1),
-                "us_gemm_only": round(us_gemm, 1), "tops_fused": round(ops_total / us_fused / 1e6, 1),
-                "bytes_received_per_rank": recv,
-                "nvlink_gbs_per_rank_fused": round(recv / us_fused / 1e3, 1),
-                "note": "fused = kvb_w8a8_scaled_mm_allgather (peer stores from the epilogue into symmetric memory)"})
-    del tp, gathered, b
+    e = {"workload": f"TP W8A8 GEMM M={M}, N={N} over {world} GPU(s) (column shards of {N // world}), K={K}, "
+                     "bf16 out (BASELINE config 5a)",
+         "us_single_gpu_full_gemm": round(t1, 1), "tops_single_gpu": round(ops_total / t1 / 1e6, 1)}
+    if world > 1:
+        n0, nw = column_shard(N, world, rank)
+        b, sb, bias = b_full[n0:n0 + nw].contiguous(), sb_full[n0:n0 + nw].contiguous(), bias_full[n0:n0 + nw]
+        tp = TPW8A8(dist.group.WORLD, M, b, sb, bias)
+        us_fused = timed(lambda: tp(a, sa), 10)
+        gathered = torch.empty((world, M, nw), dtype=torch.bfloat16, device=dev)
+
+        def nccl_step():
+            local = ops.w8a8_scaled_mm(a, b, sa, sb, bias)
+            dist.all_gather_into_tensor(gathered, local)
+        us_nccl = timed(nccl_step, 10)
+        us_gemm = timed(lambda: ops.w8a8_scaled_mm(a, b, sa, sb, bias), 10)
+        recv = (world - 1) * M * nw * 2
+        e.update({"us_fused_gemm_allgather": round(us_fused, 1), "us_gemm_then_nccl_allgather": round(us_nccl, 1),
+                  "us_shard_gemm_only": round(us_gemm, 1), "tops_fused": round(ops_total / us_fused / 1e6, 1),
+                  "efficiency_fused": eff(t1, us_fused), "efficiency_gemm_then_nccl": eff(t1, us_nccl),
+                  "efficiency_gemm_phase": eff(t1, us_gemm), "bytes_received_per_rank": recv,
+                  "limiter": "NVLink ingress of the peer stores",
+                  "nvlink_ingress_gbs_per_rank": round(recv / us_fused / 1e3, 1),
+                  "nvlink_bound_us": round(recv / PEER_COPY_GBS / 1e3, 1),
+                  "frac_of_nvlink_bound": round(recv / PEER_COPY_GBS / 1e3 / us_fused, 4),
+                  "note": "fused = kvb_w8a8_scaled_mm_allgather: epilogue TMA stores into every rank's "
+                          "symmetric buffer, double-buffered, one 1-element NCCL all-reduce per call"})
+        del tp, gathered, b
+    res.append(e)
     # gate+up with SwiGLU in the epilogue: each rank gathers half the bytes
-    ib = torch.randint(-127, 128, (nw, K), generator=gr, device=dev, dtype=torch.int8)   # interleaved shard
-    tpa = TPW8A8(dist.group.WORLD, M, ib, sb, bias, act="swiglu")
-    us_act = timed(lambda: tpa(a, sa), 10)
-    recv_act = (world - 1) * M * (nw // 2) * 2
-    res.append({"workload": f"TP W8A8 gate+up GEMM + SwiGLU, M={M}, N={N} (x{world} shards of {nw}) -> {N // 2} "
-                            "outputs, K={K}, bf16 out".replace("{K}", str(K)),
-                "us_fused_gemm_swiglu_allgather": round(us_act, 1), "bytes_received_per_rank": recv_act,
-                "nvlink_gbs_per_rank": round(recv_act / us_act / 1e3, 1),
-                "note": "kvb_w8a8_scaled_mm_act_allgather: activation in the epilogue, then peer stores"})
-    del tpa, ib, a
+    e = {"workload": f"TP W8A8 gate+up GEMM + SwiGLU, M={M}, N={N} -> {N // 2} outputs over {world} GPU(s), "
+                     f"K={K}, bf16 out", "us_single_gpu_full": round(t1_act, 1)}
+    if world > 1:
+        n0, nw = column_shard(N, world, rank)
+        tpa = TPW8A8(dist.group.WORLD, M, b_full[n0:n0 + nw].contiguous(), sb_full[n0:n0 + nw].contiguous(),
+                     bias_full[n0:n0 + nw], act="swiglu")
+        us_act = timed(lambda: tpa(a, sa), 10)
+        recv_act = (world - 1) * M * (nw // 2) * 2
+        e.update({"us_fused_gemm_swiglu_allgather": round(us_act, 1), "efficiency_fused": eff(t1_act, us_act),
+                  "bytes_received_per_rank": recv_act, "nvlink_ingress_gbs_per_rank": round(recv_act / us_act / 1e3, 1),
+                  "frac_of_nvlink_bound": round(recv_act / PEER_COPY_GBS / 1e3 / us_act, 4),
+                  "note": "kvb_w8a8_scaled_mm_act_allgather: activation in the epilogue, then peer stores"})
+        del tpa
+    res.append(e)
+    del a, b_full
     torch.cuda.empty_cache()
     # batch-sharded decode, batch 512 balanced by context length
     gl = torch.Generator(device="cpu").manual_seed(77)
     lens_all = torch.randint(512, 8193, (512,), generator=gl, dtype=torch.int32)
-    mine = balance_sequences(lens_all.tolist(), world)[rank]
-    c = make_c4_sharded(torch, dev, lens_all[torch.from_numpy(mine)], 300 + rank)
-    step = lambda: ops.paged_fp8_decode(c["q"], c["kc"], c["vc"], c["ks"], c["vs"], c["lens"], c["bt"],  # noqa: E731
-                                        k_new=c["k_new"], v_new=c["v_new"], max_seq_len=c["max_len"])
-    us = timed(step, 10)
-    tot = torch.tensor([float(c4_bytes(c))], device=dev, dtype=torch.float64)
-    dist.all_reduce(tot)
-    res.append({"workload": f"batch-sharded paged FP8 decode, batch 512 over {world} GPUs, balanced by context "
-                            "(BASELINE config 5b)", "us_per_step": round(us, 1),
-                "bytes_all_ranks": int(tot.item()), "achieved_gbs_all_ranks": round(tot.item() / us / 1e3, 1),
-                "frac_of_world_hbm": round(tot.item() / us / 1e3 / (hbm_peak * world), 4)})
+
+    def decode_step(c):
+        return lambda: ops.paged_fp8_decode(c["q"], c["kc"], c["vc"], c["ks"], c["vs"], c["lens"], c["bt"],
+                                            k_new=c["k_new"], v_new=c["v_new"], max_seq_len=c["max_len"])
+    c = make_c4_sharded(torch, dev, lens_all, 300)
+    t1_dec = timed(decode_step(c), 10)
+    bytes_all = c4_bytes(c)
+    del c
+    torch.cuda.empty_cache()
+    e = {"workload": f"batch-sharded paged FP8 decode, batch 512 over {world} GPU(s), balanced by context "
+                     "(BASELINE config 5b)", "us_single_gpu_batch512": round(t1_dec, 1), "bytes_all_ranks": bytes_all,
+         "single_gpu_frac_of_hbm": round(bytes_all / t1_dec / 1e3 / hbm_peak, 4)}
+    if world > 1:
+        parts = balance_sequences(lens_all.tolist(), world)
+        loads = [int(lens_all[torch.from_numpy(p)].sum()) for p in parts]
+        c = make_c4_sharded(torch, dev, lens_all[torch.from_numpy(parts[rank])], 300 + rank)
+        us = timed(decode_step(c), 10)
+        e.update({"us_per_step": round(us, 1), "achieved_gbs_all_ranks": round(bytes_all / us / 1e3, 1),
+                  "frac_of_world_hbm": round(bytes_all / us / 1e3 / (hbm_peak * world), 4),
+                  "efficiency": eff(t1_dec, us), "limiter": "per-GPU HBM of the heaviest rank",
+                  "ctx_imbalance_max_over_mean": round(max(loads) / (sum(loads) / world), 4)})
+        del c
+    res.append(e)
     return res
 
 
@@ -512,7 +650,8 @@ def prefill_benchmarks(torch, ops, bf16_peak):
         flops = 4 * sum(n * (n + 1) // 2 for n in ql) * hq * d
         e = {"workload": f"batched_prefill_attention q_lens=kv_lens={ql}, 32/8 heads, D=128, "
                          f"{'bf16' if dt == torch.bfloat16 else 'fp32'}",
-             "kernel": "prefill_kernel (mma.sync m16n8k16 bf16" + (")" if dt == torch.bfloat16 else "; 3xTF32 m16n8k8)"),
+             "kernel": ("prefill_tc_kernel (tcgen05 kind::f16, S and O in TMEM)" if dt == torch.bfloat16
+                        else "prefill_kernel (3xTF32 mma.sync m16n8k8)"),
              "us_per_call": round(us, 2), "tflops": round(flops / us / 1e6, 1), "flops_per_call": flops}
         if dt == torch.bfloat16:
             e["frac_of_bf16_peak"] = round(flops / us / 1e6 / bf16_peak, 4)
@@ -552,15 +691,15 @@ def main():
     if args.impl == "reference":
         if rank != 0:
             return
-        tbs, cores, sample = cpu_port_throughput()
-        ms = per_step_bytes / (tbs * 1e12) * 1e3
+        run = reference_cpu_run(args.warmup, args.steps)
+        tbs = run["tbs"]
         print(json.dumps({"impl": "reference", "metric": METRIC, "value": round(tbs, 6), "unit": "TB/s",
-                          "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
-                          "ms_per_step": round(ms, 3), "higher_is_better": True, "scaling": "weak",
+                          "n_gpus": args.gpus, "steps": run["steps_run"], "warmup": args.warmup,
+                          "ms_per_step": round(run["ms_per_step"], 3), "higher_is_better": True, "scaling": "weak",
                           "vs_baseline": None, "dtype": "bf16->e4m3", "data": "synthetic (seeded N(0,1))",
-                          "config": config,
-                          "cpu_baseline": {"value": round(tbs, 6), "unit": "TB/s", "cores": cores, "kind": "port",
-                                           "sample": sample},
+                          "config": dict(config, rows_per_step=run["rows"]),
+                          "cpu_baseline": {"value": round(tbs, 6), "unit": "TB/s", "cores": run["cores"],
+                                           "kind": run["kind"], "sample": run["sample"]},
                           "e2e": {"value": round(tbs, 6), "unit": "TB/s", "h2d_bytes_per_step": 0,
                                   "d2h_bytes_per_step": 0}}))
         return
@@ -667,13 +806,15 @@ def main():
     if world == 1 and not args.no_secondary:
         secondary = (secondary_benchmarks(torch, ops, hbm_peak) + gemm_benchmarks(torch, ops, hbm_peak) +
                      prefill_benchmarks(torch, ops, bf16_peak))
-    elif world > 1 and not args.no_secondary:
-        secondary = multi_gpu_benchmarks(torch, ops, dist, world, rank, hbm_peak)
+    sharded = None
+    if not args.no_secondary:
+        sharded = sharded_benchmarks(torch, ops, dist, world, rank, hbm_peak)
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu:
-        tbs, cores, sample = cpu_port_throughput()
-        cpu = {"value": round(tbs, 6), "unit": "TB/s", "cores": cores, "kind": "port", "sample": sample}
+        run = reference_cpu_run(2, 20)
+        cpu = {"value": round(run["tbs"], 6), "unit": "TB/s", "cores": run["cores"], "kind": run["kind"],
+               "sample": run["sample"]}
 
     if world > 1:
         dist.barrier()
@@ -699,6 +840,8 @@ def main():
         }
         if secondary:
             line["secondary"] = secondary
+        if sharded:
+            line["sharded_config5"] = sharded
         print(json.dumps(line))
     if world > 1:
         dist.destroy_process_group()

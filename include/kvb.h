@@ -40,6 +40,7 @@ extern "C" {
 #define KVB_E_TIMEOUT 6    /* a bounded device-side wait gave up */
 #define KVB_E_WORKSPACE 7  /* workspace missing or too small */
 #define KVB_E_DEVICE 8     /* device is not sm_100 */
+#define KVB_E_INDEX 9      /* an out-of-range index was skipped on the device */
 
 /* element types */
 #define KVB_F32 0
@@ -66,6 +67,29 @@ KVB_API int kvb_abi_version(void);
  * Returns 0x80000000 if the device itself reports an error.
  */
 KVB_API unsigned int kvb_device_status(int reset);
+/*
+ * kvb_device_status as a status code (no reference counterpart): synchronises the current
+ * device and returns KVB_E_TIMEOUT when bit 0 is set, KVB_E_INDEX when bit 1 or 2 is set,
+ * KVB_E_LAUNCH when the device reports an error, else KVB_OK; the message is in
+ * kvb_last_error().  Entry points never synchronise, so a wait that gives up inside a launch
+ * surfaces here, not in the entry point's return value.  reset != 0 clears the words.
+ */
+KVB_API int kvb_check_device(int reset);
+/*
+ * Sets the bound of every device-side wait, in nanoseconds of %globaltimer (0 restores the
+ * default, 2 s), on the current device (no reference counterpart).  Not stream-ordered: call
+ * it while none of the library's kernels run.
+ */
+KVB_API int kvb_set_wait_limit_ns(uint64_t limit_ns);
+/*
+ * Test hook of the bounded wait (no reference counterpart): one thread bulk-copies 16 bytes from
+ * src16 (device, 16-byte aligned) into shared memory, then waits on an mbarrier on which nothing
+ * ever arrives.  The wait gives up after the current limit and sets bit 0 of
+ * kvb_device_status; the kernel then drains its copy and returns.  out[3] (device int32):
+ * out[0] = the first copied int32, out[1] = 1 if the wait gave up, out[2] = 1 if the copy
+ * completed.
+ */
+KVB_API int kvb_selftest_wait_timeout(const void* src16, int* out, void* stream);
 /* out[i] = a[i] / b[i] through the kernels' FMA-corrected division (test hook). */
 KVB_API int kvb_selftest_div_rn(const float* a, const float* b, float* out, int64_t n, void* stream);
 

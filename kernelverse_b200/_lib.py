@@ -23,6 +23,9 @@ SIGNATURES = {
     "kvb_last_error": (ctypes.c_char_p, []),
     "kvb_abi_version": (_I, []),
     "kvb_device_status": (ctypes.c_uint, [_I]),
+    "kvb_check_device": (_I, [_I]),
+    "kvb_set_wait_limit_ns": (_I, [ctypes.c_uint64]),
+    "kvb_selftest_wait_timeout": (_I, [_P, _P, _P]),
     "kvb_selftest_div_rn": (_I, [_P, _P, _P, _I64, _P]),
     "kvb_dynamic_scaled_int8_quant_workspace_size": (_SZ, []),
     "kvb_dynamic_scaled_int8_quant": (_I, [_P, _I, _I64, _P, _P, _P, _P, _SZ, _P]),
@@ -80,3 +83,9 @@ def call(name: str, *args) -> None:
     rc = getattr(lib(), name)(*args)
     if rc != OK:
         raise KvbError(name, rc, lib().kvb_last_error().decode(errors="replace"))
+
+
+def check_device(reset: bool = True) -> None:
+    """Synchronise the current device and raise KvbError if a bounded device-side wait gave up
+    (KVB_E_TIMEOUT) or an out-of-range index was skipped (KVB_E_INDEX) since the last reset."""
+    call("kvb_check_device", 1 if reset else 0)

@@ -931,6 +931,10 @@ extern "C" int kvb_w8a8_scaled_mm_allgather(const int8_t* a, const int8_t* b_sha
   for (int r = 0; r < world; ++r)
     if (!out_ptrs[r]) return set_error(KVB_E_ARG, "w8a8_allgather: null output pointer of rank %d", r);
   if (M < 0 || N_shard < 0 || K <= 0) return set_error(KVB_E_ARG, "w8a8_allgather: bad sizes");
+  if (M > 0x7fffffff || N_shard > 0x7fffffff || K > 0x7fffffff)
+    return set_error(KVB_E_SHAPE, "w8a8_allgather: size too large");
+  if (bias_shard && bias_dtype != KVB_BF16 && bias_dtype != KVB_F16 && bias_dtype != KVB_F32)
+    return set_error(KVB_E_DTYPE, "w8a8_allgather: bias dtype %d", bias_dtype);
   if (M == 0 || N_shard == 0) return KVB_OK;
   if (ldo < (int64_t)world * N_shard) return set_error(KVB_E_SHAPE, "w8a8_allgather: ldo < world * N_shard");
   if (!a || !b_shard || (out_dtype != KVB_I32 && (!a_scales || !b_scales_shard)))

@@ -15,7 +15,12 @@ namespace kvb {
 static __device__ unsigned int g_tu_status = 0;
 
 constexpr unsigned int kStatusWaitTimeout = 1u;     // an mbarrier wait ran out of time
-constexpr uint64_t kWaitLimitNs = 2000000000ull;    // 2 s
+constexpr uint64_t kWaitLimitNs = 2000000000ull;    // 2 s: the default bound of every wait
+
+// The bound itself, per translation unit; kvb_set_wait_limit_ns() changes it in all of them
+// (a test lowers it to make a wait run out quickly).  Read only once a wait has not
+// completed at its first try.
+static __device__ uint64_t g_wait_limit_ns = kWaitLimitNs;
 
 __device__ __forceinline__ uint64_t globaltimer_ns() {
   uint64_t t;
@@ -57,13 +62,14 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
   return ok != 0;
 }
 
-// Waits for phase `parity` of `bar` to complete; gives up after kWaitLimitNs.
+// Waits for phase `parity` of `bar` to complete; gives up after g_wait_limit_ns.
 __device__ __forceinline__ bool mbar_wait_bounded(uint64_t* bar, uint32_t parity) {
   if (mbar_try_wait(bar, parity)) return true;
   const uint64_t t0 = globaltimer_ns();
+  const uint64_t limit = *(volatile uint64_t*)&g_wait_limit_ns;
   for (uint32_t it = 0;; ++it) {
     if (mbar_try_wait(bar, parity)) return true;
-    if ((it & 255u) == 255u && globaltimer_ns() - t0 > kWaitLimitNs) {
+    if ((it & 255u) == 255u && globaltimer_ns() - t0 > limit) {
       atomicOr(&g_tu_status, kStatusWaitTimeout);
       return false;
     }
@@ -91,7 +97,8 @@ __device__ __forceinline__ uint64_t policy_evict_first() {
 // status word, so kvb_device_status() can report and reset all of them.
 namespace kvb {
 using StatusReader = unsigned int (*)(bool reset);
-void register_status_reader(StatusReader fn);
+using WaitLimitSetter = int (*)(uint64_t ns);
+void register_status_reader(StatusReader fn, WaitLimitSetter set_limit);
 namespace {
 unsigned int read_tu_status(bool reset) {
   unsigned int v = 0;
@@ -102,8 +109,11 @@ unsigned int read_tu_status(bool reset) {
   }
   return v;
 }
+int set_tu_wait_limit(uint64_t ns) {
+  return cudaMemcpyToSymbol(g_wait_limit_ns, &ns, sizeof(ns)) == cudaSuccess ? 0 : 1;
+}
 struct StatusRegistrar {
-  StatusRegistrar() { register_status_reader(&read_tu_status); }
+  StatusRegistrar() { register_status_reader(&read_tu_status, &set_tu_wait_limit); }
 };
 static StatusRegistrar g_status_registrar;
 }  // namespace

@@ -1,11 +1,11 @@
 """Make KernelVerse's operator registry discover this repository's operator packages.
 
 KernelVerse discovers operators only under its own ``operators/`` directory
-(operators/registry.py:137-139, 194-215) and caches the result with ``lru_cache``.
-``install()`` wraps ``discover_operator_specs`` so that the packages under
+(``discover_operator_specs``, operators/registry.py:79-100) and caches the result with
+``lru_cache``.  ``install()`` wraps ``discover_operator_specs`` so that the packages under
 ``kernelverse_b200/operators/<category>/<op>/`` are merged in (reference packages win on a
-name clash); ``get_operator_spec`` looks the function up at call time (:218-226), and
-``load_object`` loads files outside the reference root by path (:287-309).
+name clash); ``get_operator_spec`` (:103-111) looks the function up at call time, and
+``load_module`` / ``load_object`` (:172-203) load files outside the reference root by path.
 
 Evaluations run in spawned processes (runner/generated_correctness_runner.py:1089-1121),
 so the overlay must be active in every interpreter: put ``kernelverse_b200/overlay_site``

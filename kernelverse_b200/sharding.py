@@ -8,7 +8,8 @@
   [r*N/g, (r+1)*N/g) and produces those output columns.  ``TPW8A8`` fuses the all-gather into
   the GEMM: the epilogue stores every output tile into all ranks' symmetric-memory output
   buffers over NVLink (``kvb_w8a8_scaled_mm_allgather``), and a one-element NCCL all-reduce on
-  the same stream orders every rank's kernel before the result is read.
+  the same stream orders every rank's kernel before the result is read; two output buffers
+  alternate so that a call never overwrites a buffer that a slower rank may still read.
 """
 from __future__ import annotations
 
@@ -53,13 +54,27 @@ class TPW8A8:
     """Column-sharded W8A8 GEMM whose all-gather is fused into the epilogue.
 
     ``b_shard`` [N/g, K] int8, ``b_scales_shard`` [N/g] float32 and ``bias_shard`` [N/g] bf16 are
-    this rank's slices; ``__call__(a, a_scales)`` returns the full bf16 output [M, N] (a view of
-    this rank's symmetric-memory buffer, valid until the next call).
+    this rank's slices; ``__call__(a, a_scales)`` returns the full bf16 output [M, N], a view of
+    one of two symmetric-memory buffers that successive calls alternate between.
+
+    Reuse protocol.  Every rank's kernel stores into every rank's buffer, so a call must not
+    start writing a buffer while any rank may still read it.  Call k writes buffer k % 2 and
+    ends with a one-element all-reduce on the calling stream, which completes only after every
+    rank's kernel of call k has finished its stores (they are fenced at system scope).  Call
+    k + 1 writes the other buffer, and call k + 2 -- the next writer of buffer k % 2 -- starts on
+    each rank only after that rank has passed the all-reduce of call k + 1, which in turn waits
+    for every rank to have issued call k + 1.  Hence the result of call k stays intact for all
+    work a rank orders on the calling stream before its next call (the usual "use the output,
+    then call again" pattern); work on other streams must be ordered before that call as well.
+    No extra barrier is needed: the all-reduce that publishes call k also guards the buffer
+    that call k + 1 overwrites.  With ``sync=False`` the caller takes over both duties.
 
     With ``act`` ("swiglu" or "mul_and_silu") the shard is this rank's rows of both operand
     weights in the interleaved order of ``ops.gated_weight_layout`` (N/g a multiple of 256),
     the gated activation runs in the epilogue, and the gathered output is [M, N/2].
     """
+
+    BUFFERS = 2          # call k writes buffer k % BUFFERS
 
     def __init__(self, group, M: int, b_shard, b_scales_shard, bias_shard=None, act=None):
         import torch
@@ -75,11 +90,15 @@ class TPW8A8:
         self.act = act
         self.N = self.n_shard * self.world // (2 if act else 1)   # gathered output columns
         dev = self.b.device
-        self.out = symm_mem.empty((M, self.N), dtype=torch.bfloat16, device=dev)
-        self.handle = symm_mem.rendezvous(self.out, group)
-        ptrs = list(self.handle.buffer_ptrs)
-        self._ptrs = (ctypes.c_void_p * self.world)(*ptrs)
+        # two [M, N] output buffers in one symmetric allocation; M * N * 2 bytes is a multiple of
+        # 16 (N is a multiple of 16), so the second buffer keeps the TMA stores' alignment
+        self.bufs = symm_mem.empty((self.BUFFERS, M, self.N), dtype=torch.bfloat16, device=dev)
+        self.handle = symm_mem.rendezvous(self.bufs, group)
+        base = list(self.handle.buffer_ptrs)
+        step = M * self.N * 2
+        self._ptrs = [(ctypes.c_void_p * self.world)(*[p + i * step for p in base]) for i in range(self.BUFFERS)]
         self._flag = torch.zeros(1, dtype=torch.float32, device=dev)
+        self.calls = 0
 
     def __call__(self, a, a_scales, sync: bool = True):
         import torch
@@ -91,17 +110,22 @@ class TPW8A8:
         a = a.contiguous()
         sa = a_scales.float().contiguous()
         stream = torch.cuda.current_stream(a.device).cuda_stream
+        idx = self.calls % self.BUFFERS
+        ptrs = self._ptrs[idx]
         bias_ptr = self.bias.data_ptr() if self.bias is not None else None
         bias_dt = _lib.BF16 if self.bias is not None else 0
         if self.act:
             from .ops import _ACT
             _lib.call("kvb_w8a8_scaled_mm_act_allgather", a.data_ptr(), self.b.data_ptr(), sa.data_ptr(),
-                      self.sb.data_ptr(), bias_ptr, bias_dt, self.M, self.n_shard, self.k, _ACT[self.act], self._ptrs,
+                      self.sb.data_ptr(), bias_ptr, bias_dt, self.M, self.n_shard, self.k, _ACT[self.act], ptrs,
                       self.world, self.rank, self.N, _lib.BF16, stream)
         else:
             _lib.call("kvb_w8a8_scaled_mm_allgather", a.data_ptr(), self.b.data_ptr(), sa.data_ptr(),
-                      self.sb.data_ptr(), bias_ptr, bias_dt, self.M, self.n_shard, self.k, self._ptrs, self.world,
+                      self.sb.data_ptr(), bias_ptr, bias_dt, self.M, self.n_shard, self.k, ptrs, self.world,
                       self.rank, self.N, _lib.BF16, stream)
+        self.calls += 1
         if sync:
-            dist.all_reduce(self._flag, group=self.group)   # every rank's stores have landed after this
-        return self.out
+            # every rank's stores of this call have landed after this, and every rank has issued
+            # its consumers of the previous call's buffer (which the next call overwrites)
+            dist.all_reduce(self._flag, group=self.group)
+        return self.bufs[idx]

@@ -12,7 +12,9 @@ from kernelverse_b200 import drop_in
 from kernelverse_b200.registry_overlay import local_packages
 from oracle import numerics, quant, rmsnorm
 
-REF = Path(os.environ.get("KV_REFERENCE_ROOT", "/root/reference"))
+# The reference tree: KV_REFERENCE_ROOT, else the install made by baseline/install_ref.py.
+_REF_ENV = os.environ.get("KV_REFERENCE_ROOT")
+REF = Path(_REF_ENV) if _REF_ENV else Path(__file__).resolve().parents[1] / "baseline" / "_ref"
 HAVE_REF = (REF / "operators" / "registry.py").exists()
 # runner/generated_code_checker.py:101-112 (matched case-insensitively anywhere in the file)
 BANNED = ("at::matmul", "at::softmax", "cublas", "cudnn", "cutlass", "hipblas", "miopen", "rocblas",

@@ -112,3 +112,61 @@ def test_column_and_row_shards():
         column_shard(100, 8, 0)
     spans = [row_shard(10, 4, r) for r in range(4)]
     assert spans == [(0, 3), (3, 6), (6, 8), (8, 10)]
+
+
+# ---------------------------------------------------------------------------------------------
+# The reuse protocol of TPW8A8 emulated on CPU: processes stand for GPUs, shared-memory tensors
+# for the symmetric output buffers, program order for stream order and a gloo all-reduce for the
+# one-element NCCL all-reduce that ends every call.  Call k of every rank writes its column
+# slice of value k into ALL ranks' buffer k % depth, then joins the all-reduce; the last rank
+# reads its result only after a delay, while the others go straight on to their next call.
+
+def _reuse_worker(rank, world, port, bufs, depth, calls, results):
+    import time
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    from datetime import timedelta
+    dist.init_process_group("gloo", rank=rank, world_size=world, timeout=timedelta(seconds=60))
+    try:
+        cols = bufs.shape[-1] // world
+        flag = torch.zeros(1)
+        seen = []
+        for k in range(calls):
+            idx = k % depth
+            for dest in range(world):                         # the fused epilogue's peer stores
+                bufs[dest, idx, :, rank * cols:(rank + 1) * cols] = float(k)
+            dist.all_reduce(flag)                             # ends the call
+            if rank == world - 1:
+                time.sleep(0.05)                              # a slow consumer
+            seen.append(bool(torch.all(bufs[rank, idx] == float(k))))
+        results.put((rank, seen))
+    finally:
+        dist.destroy_process_group()
+
+
+def _run_reuse(depth, world=2, calls=6):
+    ctx = mp.get_context("spawn")
+    bufs = torch.zeros((world, depth, 4, 8 * world)).share_memory_()
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_reuse_worker, args=(r, world, port, bufs, depth, calls, q)) for r in range(world)]
+    for p in procs:
+        p.start()
+    for p in procs:
+        p.join(timeout=100)
+    assert all(p.exitcode == 0 for p in procs)
+    return dict(q.get(timeout=5) for _ in range(world))
+
+
+@pytest.mark.timeout(240)
+def test_tp_output_reuse_protocol_survives_a_slow_consumer():
+    from kernelverse_b200.sharding import TPW8A8
+    seen = _run_reuse(TPW8A8.BUFFERS)
+    assert all(all(v) for v in seen.values()), seen
+
+
+@pytest.mark.timeout(240)
+def test_single_output_buffer_is_overwritten_under_a_slow_consumer():
+    # the planted mistake (one buffer, as before the protocol): the slow rank reads a later call
+    seen = _run_reuse(1)
+    assert all(seen[0])
+    assert not all(seen[1]), seen
