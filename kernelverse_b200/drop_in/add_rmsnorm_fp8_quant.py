@@ -1,4 +1,5 @@
 # ModelNew for add_rmsnorm_fp8_quant (B200 kernels).
+import torch
 import torch.nn as nn
 
 from kernelverse_b200 import ops
@@ -10,4 +11,5 @@ class ModelNew(nn.Module):
         self.eps = float(shape["eps"])
 
     def forward(self, x, residual, weight):
-        return ops.add_rmsnorm_quant(x, residual, weight, self.eps)
+        residual_out, codes, scales = ops.add_rmsnorm_quant(x, residual, weight, self.eps)
+        return residual_out, codes.view(torch.uint8), scales

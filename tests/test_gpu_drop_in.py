@@ -128,7 +128,7 @@ def test_baseline_packages_model_vs_modelnew(op, shape):
     gots = got if isinstance(got, tuple) else (got,)
     for r, o in zip(refs, gots):
         assert r.dtype == o.dtype and r.shape == o.shape
-        if r.dtype == torch.float8_e4m3fn:
+        if r.dtype == torch.float8_e4m3fn or (op == "add_rmsnorm_fp8_quant" and r.dtype == torch.uint8):
             from oracle import numerics
             d = np.abs(numerics.e4m3_ordinal(host(o)) - numerics.e4m3_ordinal(host(r)))
             assert d.max() <= 1
