@@ -65,10 +65,19 @@ __global__ void selftest_wait_kernel(const int4* src, int* out) {
   out[2] = drained ? 1 : 0;
 }
 
-// Self-test of div_rn (Markstein division): out[i] = a[i] / b[i] through a Divisor.
+// Self-test of div_rn (Markstein division): out[i] = a[i] / b[i] through a Divisor.  Elements
+// with i % 4 in {2, 3} whose dividend is in the fast domain go through the packed path
+// (div2_rn_fast, the dividend and its negation in one register), the others through div_rn.
 __global__ void selftest_div_kernel(const float* a, const float* b, float* out, int64_t n) {
-  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x)
-    out[i] = div_rn(a[i], make_divisor(b[i]));
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x) {
+    const Divisor d = make_divisor(b[i]);
+    if ((i & 2) && fabsf(a[i]) >= d.thresh) {
+      const float2 q = f2_unpack(div2_rn_fast(f2_pack(a[i], -a[i]), d));
+      out[i] = (q.y == -q.x) ? q.x : __int_as_float(0x7fc00000);   // lanes must agree (NaN otherwise)
+    } else {
+      out[i] = div_rn(a[i], d);
+    }
+  }
 }
 }  // namespace
 

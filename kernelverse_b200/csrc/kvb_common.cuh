@@ -239,6 +239,30 @@ __device__ __forceinline__ float div_rn(float a, const Divisor& d) {
   return div_rn_fast(a, d);
 }
 
+// ------------------------------------------------------------------ packed float32 (sm_100a)
+// Two float32 lanes in one 64-bit register for the packed FMUL2 / FFMA2 / FADD2 instructions
+// (PTX mul/fma/add .rn.f32x2): each lane is rounded exactly as the scalar .rn instruction.
+__device__ __forceinline__ uint64_t f2_pack(float lo, float hi) {
+  uint64_t r;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(lo), "f"(hi));
+  return r;
+}
+__device__ __forceinline__ float2 f2_unpack(uint64_t v) {
+  float2 r;
+  asm("mov.b64 {%0, %1}, %2;" : "=f"(r.x), "=f"(r.y) : "l"(v));
+  return r;
+}
+
+// div_rn_fast on two dividends at once: the same three correctly rounded steps per lane.
+__device__ __forceinline__ uint64_t div2_rn_fast(uint64_t a, const Divisor& d) {
+  const uint64_t y = f2_pack(d.y, d.y), nb = f2_pack(-d.b, -d.b);
+  uint64_t q0, r, q1;
+  asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(q0) : "l"(a), "l"(y));
+  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(r) : "l"(nb), "l"(q0), "l"(a));
+  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(q1) : "l"(r), "l"(y), "l"(q0));
+  return q1;
+}
+
 // int8 code: round-half-even of the IEEE float32 quotient x / scale, clamped to +-127.
 // kChecked = false: the caller has verified |x| >= d.thresh for the values passed.
 template <bool kChecked = true>
@@ -267,6 +291,17 @@ __device__ __forceinline__ uint32_t quant4_fast(float a0, float a1, float a2, fl
   const uint32_t b1 = __float_as_uint(__fadd_rn(div_rn_fast(a1, d), kRound));
   const uint32_t b2 = __float_as_uint(__fadd_rn(div_rn_fast(a2, d), kRound));
   const uint32_t b3 = __float_as_uint(__fadd_rn(div_rn_fast(a3, d), kRound));
+  return __byte_perm(__byte_perm(b0, b1, 0x0040), __byte_perm(b2, b3, 0x0040), 0x5410);
+}
+
+// quant4_fast with packed arithmetic: the four codes of (a0, a1) and (a2, a3), each pair given
+// as one packed register; identical results.
+__device__ __forceinline__ uint32_t quant4_fast_x2(uint64_t a01, uint64_t a23, const Divisor& d) {
+  const uint64_t k = f2_pack(12582912.0f, 12582912.0f);   // 1.5 * 2^23 in both lanes
+  uint64_t r01, r23;
+  asm("add.rn.f32x2 %0, %1, %2;" : "=l"(r01) : "l"(div2_rn_fast(a01, d)), "l"(k));
+  asm("add.rn.f32x2 %0, %1, %2;" : "=l"(r23) : "l"(div2_rn_fast(a23, d)), "l"(k));
+  const uint32_t b0 = (uint32_t)r01, b1 = (uint32_t)(r01 >> 32), b2 = (uint32_t)r23, b3 = (uint32_t)(r23 >> 32);
   return __byte_perm(__byte_perm(b0, b1, 0x0040), __byte_perm(b2, b3, 0x0040), 0x5410);
 }
 

@@ -213,6 +213,84 @@ __global__ void __launch_bounds__(kMaxThreads, kMinBlocks)
   if (threadIdx.x == 0) scales[g] = scale;
 }
 
+// ---------------------------------------------------------------- per-group, long groups, teams
+// CTAs of 512 threads form 16 / WG teams of WG warps; each team quantises one group (a token
+// row for per-token quantisation), so a CTA covers several groups and the launch needs 4-16x
+// fewer CTAs than one CTA per group (a dependent launch of 2048 CTAs costs ~1.7 us more than
+// one of a few hundred on a B200).  Every thread loads its VPT vectors of the group with
+// 128-bit streaming loads before any arithmetic.  At BASELINE sizes the kernel is bound by
+// issue as much as by DRAM, so the instruction count shapes it: the elements are converted to
+// float32 once (shared by the amax and the codes), the amax is one team reduction (a named
+// barrier), amax / 127 uses the FMA-corrected division with the divisor 127, and the codes use
+// packed float32 arithmetic (two lanes per instruction): about four instructions per element
+// plus a fixed cost per warp, which four warps of four vectors a thread keep small.
+constexpr int kTeamThreads = 512;
+
+__device__ __forceinline__ uint2 quant8_fast_x2(const float (&f)[8], const Divisor& d) {
+  return make_uint2(quant4_fast_x2(f2_pack(f[0], f[1]), f2_pack(f[2], f[3]), d),
+                    quant4_fast_x2(f2_pack(f[4], f[5]), f2_pack(f[6], f[7]), d));
+}
+
+__device__ __forceinline__ void named_bar_sync(int id, int count) {
+  asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(count) : "memory");
+}
+
+template <typename T, int VPT, int WG, int kMinBlocks>
+__global__ void __launch_bounds__(kTeamThreads, kMinBlocks)
+    group_quant_teams_kernel(const T* __restrict__ x, int64_t ngroups, int gvec, float eps, int8_t* __restrict__ q,
+                             float* __restrict__ scales) {
+  constexpr int kTeams = kTeamThreads / 32 / WG;
+  constexpr int kThreads = WG * 32;           // threads of a team
+  __shared__ float red[kTeams][WG];
+  const int tid = threadIdx.x, lane = tid & 31;
+  const int team = tid / kThreads, ttid = tid % kThreads;
+  const int64_t g = (int64_t)blockIdx.x * kTeams + team;
+  const bool live = g < ngroups;              // team-uniform
+  pdl_trigger();
+  pdl_wait();            // launched as a programmatic dependent (launch_pdl)
+  Vec8<T> a[VPT];
+  const T* xg = x + g * gvec * 8;
+#pragma unroll
+  for (int j = 0; j < VPT; ++j) {
+    const int v = ttid + j * kThreads;
+    if (live && v < gvec) a[j].load_stream(xg + (int64_t)v * 8);
+  }
+  float f[VPT][8];
+  float m = 0.0f;
+#pragma unroll
+  for (int j = 0; j < VPT; ++j) {
+    a[j].unpack(f[j]);
+    if (live && ttid + j * kThreads < gvec) {
+#pragma unroll
+      for (int e = 0; e < 8; ++e) m = fmaxf(m, fabsf(f[j][e]));
+    }
+  }
+  m = warp_max_redux(m);
+  if (WG > 1) {
+    if (lane == 0) red[team][ttid >> 5] = m;
+    named_bar_sync(1 + team, kThreads);      // one reduction per team and launch: one buffer suffices
+    m = warp_max_redux(lane < WG ? red[team][lane] : 0.0f);
+  }
+  if (!live) return;
+  const float scale = fmaxf(div_rn(m, make_divisor(kInt8Max)), eps);   // == IEEE m / 127
+  const Divisor d = make_divisor(scale);
+  uint2* qg = reinterpret_cast<uint2*>(q + g * gvec * 8);
+  if (fast_divisor(d)) {
+#pragma unroll
+    for (int j = 0; j < VPT; ++j) {
+      const int v = ttid + j * kThreads;
+      if (v < gvec) qg[v] = quant8_fast_x2(f[j], d);
+    }
+  } else {
+#pragma unroll
+    for (int j = 0; j < VPT; ++j) {
+      const int v = ttid + j * kThreads;
+      if (v < gvec) qg[v] = quant8_checked(a[j], d);
+    }
+  }
+  if (ttid == 0) scales[g] = scale;
+}
+
 // ---------------------------------------------------------------- any shape / alignment
 // One warp per group, two passes over global memory (correctness path for odd sizes).
 template <typename T>
@@ -278,6 +356,29 @@ int launch_rowblock(const T* x, int64_t ngroups, int64_t gvec, float eps, int8_t
   return check_launch("group_quant_rowblock_kernel");
 }
 
+// Team path (group_quant_teams_kernel) for groups of 64 to 512 * VPT vectors: WG = the warps
+// that cover a group with at most VPT vectors a thread (a power of two, at most 16).
+template <typename T, int VPT, int WG, int kMinBlocks>
+int launch_teams(const T* x, int64_t ngroups, int64_t gvec, float eps, int8_t* q, float* scales, cudaStream_t st) {
+  constexpr int kTeams = kTeamThreads / 32 / WG;
+  const int64_t grid = (ngroups + kTeams - 1) / kTeams;
+  if (grid > 0x7fffffff) return set_error(KVB_E_SHAPE, "per_token_group_quant_int8: too many groups");
+  cudaError_t e = launch_pdl(group_quant_teams_kernel<T, VPT, WG, kMinBlocks>, dim3((unsigned)grid),
+                             dim3(kTeamThreads), 0, st, x, ngroups, (int)gvec, eps, q, scales);
+  if (e != cudaSuccess) return set_error(KVB_E_LAUNCH, "group_quant_teams_kernel: %s", cudaGetErrorString(e));
+  return check_launch("group_quant_teams_kernel");
+}
+
+template <typename T>
+int launch_teams_any(const T* x, int64_t ngroups, int64_t gvec, float eps, int8_t* q, float* scales, cudaStream_t st) {
+  constexpr int V = sizeof(T) == 4 ? 2 : 4;   // vectors a thread (float vectors are twice as wide)
+  if (gvec <= 32 * V) return launch_teams<T, V, 1, 2>(x, ngroups, gvec, eps, q, scales, st);
+  if (gvec <= 64 * V) return launch_teams<T, V, 2, 2>(x, ngroups, gvec, eps, q, scales, st);
+  if (gvec <= 128 * V) return launch_teams<T, V, 4, 2>(x, ngroups, gvec, eps, q, scales, st);
+  if (gvec <= 256 * V) return launch_teams<T, V, 8, 2>(x, ngroups, gvec, eps, q, scales, st);
+  return launch_teams<T, V, 16, 2>(x, ngroups, gvec, eps, q, scales, st);
+}
+
 template <typename T>
 int launch_group_quant(const void* xv, int64_t tokens, int64_t hidden, int64_t G, float eps, int8_t* q,
                        float* scales, cudaStream_t st) {
@@ -293,6 +394,8 @@ int launch_group_quant(const void* xv, int64_t tokens, int64_t hidden, int64_t G
       group_quant_subwarp_kernel<T><<<blocks, 256, 0, st>>>(x, nvec, (int)lanes, eps, q, scales);
       return check_launch("group_quant_subwarp_kernel");
     }
+    if (lanes >= 64 && lanes <= 512 * (sizeof(T) == 4 ? 2 : 4))
+      return launch_teams_any<T>(x, ngroups, lanes, eps, q, scales, st);
     if (ngroups <= 0x7fffffff) {
       if (lanes <= 4 * 1024) return launch_rowblock<T, 4>(x, ngroups, lanes, eps, q, scales, st);
       if (lanes <= 8 * 1024) return launch_rowblock<T, 8>(x, ngroups, lanes, eps, q, scales, st);

@@ -60,7 +60,10 @@ def test_per_token_quant_baseline_config_full_size():
 @pytest.mark.parametrize("t,h,g", [(64, 4096, 128), (33, 256, 32), (5, 11008, 64), (7, 96, 96), (3, 100, 100),
                                    (4, 8192, 8192), (2, 40, 8), (3, 96, 48), (1, 70000, 70000),
                                    # many per-token rows: 1, 2 and 4 vectors per thread of the row-block kernel
-                                   (320, 1024, 1024), (297, 4096, 4096), (600, 8192, 8192), (1000, 2048, 2048)])
+                                   (320, 1024, 1024), (297, 4096, 4096), (600, 8192, 8192), (1000, 2048, 2048),
+                                   # team kernel: 1, 2, 4, 8 and 16 warps a group, partial last CTA
+                                   (149, 4096, 4096), (5000, 4096, 4096), (3000, 8192, 8192), (40, 512, 512),
+                                   (50, 16384, 16384), (7, 4096, 2048), (33, 1536, 768)])
 def test_group_quant_shapes(dt, t, h, g):
     rng = seeded(t * 7 + h)
     x = (rng.standard_normal((t, h)) * 3).astype(np.float32)
