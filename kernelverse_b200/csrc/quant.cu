@@ -231,6 +231,16 @@ __device__ __forceinline__ uint2 quant8_fast_x2(const float (&f)[8], const Divis
                     quant4_fast_x2(f2_pack(f[4], f[5]), f2_pack(f[6], f[7]), d));
 }
 
+// The general path from float32 values: correctly rounded quotient for any divisor, clamped.
+__device__ __forceinline__ uint2 quant8_checked_f(const float (&f)[8], const Divisor& d) {
+  uint32_t lo = 0, hi = 0;
+#pragma unroll
+  for (int i = 0; i < 4; ++i) lo |= (uint32_t)(uint8_t)quant_int8<true>(f[i], d) << (8 * i);
+#pragma unroll
+  for (int i = 0; i < 4; ++i) hi |= (uint32_t)(uint8_t)quant_int8<true>(f[4 + i], d) << (8 * i);
+  return make_uint2(lo, hi);
+}
+
 __device__ __forceinline__ void named_bar_sync(int id, int count) {
   asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(count) : "memory");
 }
@@ -289,6 +299,87 @@ __global__ void __launch_bounds__(kTeamThreads, kMinBlocks)
     }
   }
   if (ttid == 0) scales[g] = scale;
+}
+
+// ---------------------------------------------------------------- per-group, 16-bit, rolling
+// The team kernel's work as a persistent loop with a one-group prefetch: CTAs of 512 threads
+// (two resident per SM, grid = 2 x SMs) form 16 / WG teams; a team walks the groups
+// g, g + (all teams), ... and issues the loads of its next group as soon as the current group's
+// data has arrived (right after its amax), so while the team reduces, divides and stores one
+// group the next one is in flight.  Keeping one group in flight per team rather than all of
+// them lets early groups land early: with every group requested at once the DRAM interleaves
+// them and all land near the end, after which the arithmetic is a serial tail.  For 16-bit
+// inputs with two vectors a thread (the data of two groups fits the 64 registers a thread has).
+// kFull: every group is exactly VPT x (team threads) vectors (power-of-two rows such as the
+// BASELINE first config), so no per-vector bounds predicate is needed.
+template <typename T, int VPT, int WG, bool kFull>
+__global__ void __launch_bounds__(kTeamThreads, 2)
+    group_quant_rolling_kernel(const T* __restrict__ x, int64_t ngroups, int gvec_arg, float eps,
+                               int8_t* __restrict__ q, float* __restrict__ scales) {
+  constexpr int kTeams = kTeamThreads / 32 / WG;
+  constexpr int kThreads = WG * 32;
+  const int gvec = kFull ? VPT * kThreads : gvec_arg;
+  __shared__ float red[kTeams][2][WG];        // per team, alternating buffers of consecutive reductions
+  const int tid = threadIdx.x, lane = tid & 31;
+  const int team = tid / kThreads, ttid = tid % kThreads;
+  const int64_t stride = (int64_t)gridDim.x * kTeams;
+  pdl_trigger();
+  pdl_wait();            // launched as a programmatic dependent (launch_pdl)
+  int64_t g = (int64_t)blockIdx.x * kTeams + team;   // team-uniform from here on
+  Vec8<T> cur[VPT], nxt[VPT];
+  if (g < ngroups) {
+#pragma unroll
+    for (int j = 0; j < VPT; ++j) {
+      const int v = ttid + j * kThreads;
+      if (v < gvec) cur[j].load_stream(x + g * gvec * 8 + (int64_t)v * 8);
+    }
+  }
+  for (int it = 0; g < ngroups; g += stride, ++it) {
+    float f[VPT][8];
+    float m = 0.0f;
+#pragma unroll
+    for (int j = 0; j < VPT; ++j) {
+      cur[j].unpack(f[j]);
+      if (ttid + j * kThreads < gvec) {
+#pragma unroll
+        for (int e = 0; e < 8; ++e) m = fmaxf(m, fabsf(f[j][e]));
+      }
+    }
+    const int64_t gn = g + stride;       // prefetch: this group's data has arrived (used above)
+    if (gn < ngroups) {
+#pragma unroll
+      for (int j = 0; j < VPT; ++j) {
+        const int v = ttid + j * kThreads;
+        if (v < gvec) nxt[j].load_stream(x + gn * gvec * 8 + (int64_t)v * 8);
+      }
+    }
+    m = warp_max_redux(m);
+    if (WG > 1) {
+      float* buf = red[team][it & 1];
+      if (lane == 0) buf[ttid >> 5] = m;
+      named_bar_sync(1 + team, kThreads);
+      m = warp_max_redux(lane < WG ? buf[lane] : 0.0f);
+    }
+    const float scale = fmaxf(div_rn(m, make_divisor(kInt8Max)), eps);   // == IEEE m / 127
+    const Divisor d = make_divisor(scale);
+    uint2* qg = reinterpret_cast<uint2*>(q + g * gvec * 8);
+    if (fast_divisor(d)) {
+#pragma unroll
+      for (int j = 0; j < VPT; ++j) {
+        const int v = ttid + j * kThreads;
+        if (v < gvec) qg[v] = quant8_fast_x2(f[j], d);
+      }
+    } else {
+#pragma unroll
+      for (int j = 0; j < VPT; ++j) {
+        const int v = ttid + j * kThreads;
+        if (v < gvec) qg[v] = quant8_checked_f(f[j], d);
+      }
+    }
+    if (ttid == 0) scales[g] = scale;
+#pragma unroll
+    for (int j = 0; j < VPT; ++j) cur[j] = nxt[j];
+  }
 }
 
 // ---------------------------------------------------------------- any shape / alignment
@@ -379,6 +470,31 @@ int launch_teams_any(const T* x, int64_t ngroups, int64_t gvec, float eps, int8_
   return launch_teams<T, V, 16, 2>(x, ngroups, gvec, eps, q, scales, st);
 }
 
+// Rolling path (group_quant_rolling_kernel) for 16-bit inputs with 64 to 1024 vectors a group:
+// two vectors a thread, WG = gvec / 64 rounded up to a power of two.
+template <typename T, int WG>
+int launch_rolling(const T* x, int64_t ngroups, int64_t gvec, float eps, int8_t* q, float* scales, cudaStream_t st) {
+  constexpr int kTeams = kTeamThreads / 32 / WG;
+  const int64_t grid = std::min<int64_t>((ngroups + kTeams - 1) / kTeams, 2 * (int64_t)sm_count());
+  const bool full = gvec == 2 * WG * 32;
+  cudaError_t e = full ? launch_pdl(group_quant_rolling_kernel<T, 2, WG, true>, dim3((unsigned)grid),
+                                    dim3(kTeamThreads), 0, st, x, ngroups, (int)gvec, eps, q, scales)
+                       : launch_pdl(group_quant_rolling_kernel<T, 2, WG, false>, dim3((unsigned)grid),
+                                    dim3(kTeamThreads), 0, st, x, ngroups, (int)gvec, eps, q, scales);
+  if (e != cudaSuccess) return set_error(KVB_E_LAUNCH, "group_quant_rolling_kernel: %s", cudaGetErrorString(e));
+  return check_launch("group_quant_rolling_kernel");
+}
+
+template <typename T>
+int launch_rolling_any(const T* x, int64_t ngroups, int64_t gvec, float eps, int8_t* q, float* scales,
+                       cudaStream_t st) {
+  if (gvec <= 64) return launch_rolling<T, 1>(x, ngroups, gvec, eps, q, scales, st);
+  if (gvec <= 128) return launch_rolling<T, 2>(x, ngroups, gvec, eps, q, scales, st);
+  if (gvec <= 256) return launch_rolling<T, 4>(x, ngroups, gvec, eps, q, scales, st);
+  if (gvec <= 512) return launch_rolling<T, 8>(x, ngroups, gvec, eps, q, scales, st);
+  return launch_rolling<T, 16>(x, ngroups, gvec, eps, q, scales, st);
+}
+
 template <typename T>
 int launch_group_quant(const void* xv, int64_t tokens, int64_t hidden, int64_t G, float eps, int8_t* q,
                        float* scales, cudaStream_t st) {
@@ -394,6 +510,8 @@ int launch_group_quant(const void* xv, int64_t tokens, int64_t hidden, int64_t G
       group_quant_subwarp_kernel<T><<<blocks, 256, 0, st>>>(x, nvec, (int)lanes, eps, q, scales);
       return check_launch("group_quant_subwarp_kernel");
     }
+    if (sizeof(T) == 2 && lanes >= 64 && lanes <= 1024)
+      return launch_rolling_any<T>(x, ngroups, lanes, eps, q, scales, st);
     if (lanes >= 64 && lanes <= 512 * (sizeof(T) == 4 ? 2 : 4))
       return launch_teams_any<T>(x, ngroups, lanes, eps, q, scales, st);
     if (ngroups <= 0x7fffffff) {
