@@ -584,71 +584,115 @@ __global__ void __launch_bounds__(128) paged_decode_f32_kernel(const __grid_cons
   }
 }
 
-// out[b, h, :] = sum_p 2^(m_p - M) o_p / (sum_p 2^(m_p - M) l_p + eps)   (paged_attention_v2.py:163-173)
-// Combines the partitions of one (sequence, query head): out = sum_p o_p 2^(m_p - M) /
-// (sum_p l_p 2^(m_p - M) + eps).  The partition weights are computed once into shared memory
-// (dynamic, pmax floats) and every thread then sums one output dimension with independent loads.
+// Combines the split-KV partials of one (query row b, query head h) per warp: the lanes take the
+// partitions' log2-domain maxima 32 at a time for the global max M, weigh the partition sums
+// by 2^(m_p - M) for the total, and accumulate the weighted unnormalised outputs four
+// dimensions a lane (float4 loads of the partial rows, which the decode grid has just written
+// and which are still in L2), with the weights of each batch of 32 partitions broadcast by
+// shuffles (paged_attention_v2.py:163-173; eps = 1e-6 for the v2 normalisation, else 0).  No
+// shared memory and no block barrier: a row is one warp's dependent chain.
 // With lse, the natural-log sum of exp of the scaled logits of query row b (= sequence b / qtok,
 // query token b % qtok) and head h goes to lse[((b / qtok) * hq + h) * qtok + b % qtok].
-__global__ void __launch_bounds__(128) decode_merge_kernel(const float* __restrict__ m_part, const float* __restrict__ l_part,
-                                                           const float* __restrict__ o_part, const void* seq_lens, int sl64,
-                                                           int hq, int D, int part, int pmax, float eps, void* out,
-                                                           int out_dtype, int qtok, float* __restrict__ lse) {
-  extern __shared__ float wgt[];        // [pmax]
-  __shared__ float red[32];
-  const int bh = blockIdx.x, b = bh / hq, sq = b / qtok;
+constexpr int kMergeWarps = 8;
+template <int NK>   // float4 columns a lane: head dims up to 128 * NK
+__global__ void __launch_bounds__(kMergeWarps * 32) decode_merge_kernel(
+    const float* __restrict__ m_part, const float* __restrict__ l_part, const float* __restrict__ o_part,
+    const void* seq_lens, int sl64, int rows, int hq, int D, int part, int pmax, float eps, void* out, int out_dtype,
+    int qtok, float* __restrict__ lse) {
   // Launched as a programmatic dependent of the decode grid: wait until that grid has
   // completed and its partials are visible (returns at once without a prerequisite grid).
   // (Triggering the next grid after the wait rather than at entry measured faster in
   // back-to-back decode steps.)
   pdl_wait();
   pdl_trigger();
+  const int lane = threadIdx.x & 31;
+  const int bh = blockIdx.x * kMergeWarps + (threadIdx.x >> 5);
+  if (bh >= rows) return;
+  const int b = bh / hq, sq = b / qtok;
   const int64_t L = sl64 ? reinterpret_cast<const int64_t*>(seq_lens)[sq] : (int64_t)reinterpret_cast<const int32_t*>(seq_lens)[sq];
   const int64_t npl = (L + part - 1) / part;
   const int np = (int)(npl < pmax ? npl : pmax);
   const float* mp = m_part + (int64_t)bh * pmax;
   const float* lp = l_part + (int64_t)bh * pmax;
-  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nwarps = blockDim.x >> 5;
-  // block max of the (possibly negative) log2-domain maxima; idle lanes contribute -inf
-  float M = -INFINITY;
-  for (int p = threadIdx.x; p < np; p += blockDim.x) M = fmaxf(M, mp[p]);
+  const float* op = o_part + (int64_t)bh * pmax * D;
+  float4 acc[NK];                         // dimensions 4 * lane + 128 * k
 #pragma unroll
-  for (int off = 16; off > 0; off >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, off));
-  if (lane == 0) red[warp] = M;
-  __syncthreads();
-  M = lane < nwarps ? red[lane] : -INFINITY;
+  for (int k = 0; k < NK; ++k) acc[k] = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+  // Weighted sum of the partial rows [i0, i1) of the 32-partition chunk at p0; lane i of wl
+  // holds the weight of partition p0 + i (0 past np).  Eight rows' loads are in flight before
+  // their FMAs.
+  auto fma_rows = [&](int k, const float4 (&v)[8], int i0, float wl) {
 #pragma unroll
-  for (int off = 16; off > 0; off >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, off));
-  const float Mu = M == -INFINITY ? 0.0f : M;
-  float ls = 0.0f;
-  for (int p = threadIdx.x; p < np; p += blockDim.x) {
-    const float w = exp2f(mp[p] - Mu);
-    wgt[p] = w;
-    ls += lp[p] * w;
+    for (int u = 0; u < 8; ++u) {
+      const float w = __shfl_sync(0xffffffffu, wl, (i0 + u) & 31);
+      acc[k].x = fmaf(v[u].x, w, acc[k].x);
+      acc[k].y = fmaf(v[u].y, w, acc[k].y);
+      acc[k].z = fmaf(v[u].z, w, acc[k].z);
+      acc[k].w = fmaf(v[u].w, w, acc[k].w);
+    }
+  };
+  auto load_rows = [&](int k, float4 (&v)[8], int p0, int i0, int i1) {
+    const int d = 4 * lane + 128 * k;
+#pragma unroll
+    for (int u = 0; u < 8; ++u)
+      v[u] = (i0 + u < i1 && d < D) ? *reinterpret_cast<const float4*>(op + (int64_t)(p0 + i0 + u) * D + d)
+                                    : make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+  };
+  auto accumulate = [&](int p0, int i0, int i1, float wl) {
+    for (; i0 < i1; i0 += 8) {
+#pragma unroll
+      for (int k = 0; k < NK; ++k) {
+        float4 v[8];
+        load_rows(k, v, p0, i0, i1);
+        fma_rows(k, v, i0, wl);
+      }
+    }
+  };
+  float M = -INFINITY, Mu, ls = 0.0f;
+  if (NK == 1 && np <= 32) {
+    // One chunk: the maxima, the sums and the first eight partial rows are requested together
+    // (none depends on another), so the row costs one memory round trip, not three.
+    const float ml = lane < np ? mp[lane] : -INFINITY;
+    const float ll = lane < np ? lp[lane] : 0.0f;
+    float4 v0[NK][8];
+#pragma unroll
+    for (int k = 0; k < NK; ++k) load_rows(k, v0[k], 0, 0, np);
+    M = ml;
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, off));
+    Mu = M == -INFINITY ? 0.0f : M;
+    const float wl = lane < np ? exp2f(ml - Mu) : 0.0f;
+    ls = ll * wl;
+#pragma unroll
+    for (int k = 0; k < NK; ++k) fma_rows(k, v0[k], 0, wl);
+    accumulate(0, 8, np, wl);
+  } else {
+    for (int p = lane; p < np; p += 32) M = fmaxf(M, mp[p]);
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, off));
+    Mu = M == -INFINITY ? 0.0f : M;
+    for (int p0 = 0; p0 < np; p0 += 32) {
+      const int p = p0 + lane;
+      const float wl = p < np ? exp2f(mp[p] - Mu) : 0.0f;
+      ls += p < np ? lp[p] * wl : 0.0f;
+      accumulate(p0, 0, min(32, np - p0), wl);
+    }
   }
 #pragma unroll
   for (int off = 16; off > 0; off >>= 1) ls += __shfl_xor_sync(0xffffffffu, ls, off);
-  __syncthreads();                       // every warp has read red; wgt is complete
-  if (lane == 0) red[warp] = ls;
-  __syncthreads();
-  ls = lane < nwarps ? red[lane] : 0.0f;
-#pragma unroll
-  for (int off = 16; off > 0; off >>= 1) ls += __shfl_xor_sync(0xffffffffu, ls, off);
   const float inv = np > 0 ? 1.0f / (ls + eps) : 0.0f;
-  if (lse && threadIdx.x == 0)   // M, in log2 units, plus log2 of the rescaled sum, to natural log
+  if (lse && lane == 0)   // M, in log2 units, plus log2 of the rescaled sum, to natural log
     lse[((int64_t)sq * hq + bh % hq) * qtok + b % qtok] = np > 0 ? (Mu + log2f(ls)) * kLn2 : -INFINITY;
-  const float* op = o_part + (int64_t)bh * pmax * D;
-  for (int d = threadIdx.x; d < D; d += blockDim.x) {
-    float acc0 = 0.0f, acc1 = 0.0f, acc2 = 0.0f, acc3 = 0.0f;
-    int p = 0;
-    for (; p + 4 <= np; p += 4) {
-      acc0 += op[(int64_t)p * D + d] * wgt[p];
-      acc1 += op[(int64_t)(p + 1) * D + d] * wgt[p + 1];
-      acc2 += op[(int64_t)(p + 2) * D + d] * wgt[p + 2];
-      acc3 += op[(int64_t)(p + 3) * D + d] * wgt[p + 3];
+#pragma unroll
+  for (int k = 0; k < NK; ++k) {
+    const int d = 4 * lane + 128 * k;
+    if (d < D) {
+      const int64_t o = (int64_t)bh * D + d;
+      store_any(out, out_dtype, o, acc[k].x * inv);
+      store_any(out, out_dtype, o + 1, acc[k].y * inv);
+      store_any(out, out_dtype, o + 2, acc[k].z * inv);
+      store_any(out, out_dtype, o + 3, acc[k].w * inv);
     }
-    for (; p < np; ++p) acc0 += op[(int64_t)p * D + d] * wgt[p];
-    store_any(out, out_dtype, (int64_t)bh * D + d, ((acc0 + acc1) + (acc2 + acc3)) * inv);
   }
 }
 
@@ -805,9 +849,9 @@ static int paged_attention_impl(const void* query, int q_dtype, const void* key_
   // (every decode CTA allows it as it starts) and waits on the device for its partials, which
   // hides the launch gap between the two kernels.
   cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3((unsigned)(batch * num_q_heads));
-  cfg.blockDim = dim3(128);
-  cfg.dynamicSmemBytes = (size_t)pmax * sizeof(float);   // partition weights
+  const int rows = batch * num_q_heads;
+  cfg.gridDim = dim3((unsigned)((rows + kMergeWarps - 1) / kMergeWarps));
+  cfg.blockDim = dim3(kMergeWarps * 32);
   cfg.stream = st;
   cudaLaunchAttribute attr[1];
   attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
@@ -818,8 +862,9 @@ static int paged_attention_impl(const void* query, int q_dtype, const void* key_
   const float* lp = a.l_part;
   const float* op = a.o_part;
   const int sl64 = a.sl64;
-  cudaError_t e = cudaLaunchKernelEx(&cfg, decode_merge_kernel, mp, lp, op, seq_lens, sl64, num_q_heads, head_dim, part,
-                                     pmax, eps, out, out_dtype, qtok, lse);
+  cudaError_t e = cudaLaunchKernelEx(&cfg, head_dim <= 128 ? decode_merge_kernel<1> : decode_merge_kernel<8>, mp, lp, op,
+                                     seq_lens, sl64, rows, num_q_heads, head_dim, part, pmax, eps, out, out_dtype, qtok,
+                                     lse);
   if (e != cudaSuccess) return set_error(KVB_E_LAUNCH, "decode_merge_kernel: %s", cudaGetErrorString(e));
   return check_launch("decode_merge_kernel");
 }
