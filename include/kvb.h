@@ -156,6 +156,12 @@ KVB_API int kvb_add_rmsnorm(const void* x, const void* residual, const void* wei
  *   scales[r] = max(amax|y_r| / Q, 1/(448*512)),  Q = 448 (KVB_E4M3) or 127 (KVB_I8)
  *   codes = e4m3fn(clamp(y / scale, +-448))  or  clamp(round_half_even(y / scale), +-127)
  * residual_out may be NULL (not written).  codes: [rows, hidden] bytes; scales: [rows].
+ * Exactness: residual_out is bit-exact.  y is a float32 computation whose sum of squares is
+ * reduced in the kernel's own order, so y (and with it the scale and the codes) can differ
+ * from a float64- or differently-ordered reference by about one float32 rounding: codes are
+ * within one step (one e4m3 ulp, or +-1 for int8) of the reference's, >= 99.9 % of them
+ * identical, and scales within a relative 1e-6.  The standalone quantisers
+ * (kvb_per_token_group_quant_int8 etc.) take their scale from the input and are bit-exact.
  */
 KVB_API int kvb_add_rmsnorm_quant(const void* x, const void* residual, const void* weight, int dtype,
                           int64_t rows, int64_t hidden, float eps, void* residual_out,
