@@ -660,7 +660,24 @@ def prefill_benchmarks(torch, ops, bf16_peak):
     return out
 
 
+_JSON_OUT = None
+
+
+def emit(record: dict) -> None:
+    """Write the result line to the original standard output."""
+    out = _JSON_OUT or sys.stdout
+    out.write(json.dumps(record) + "\n")
+    out.flush()
+
+
 def main():
+    # The JSON line is the only thing this program writes to standard output: libraries that
+    # print there (NCCL announces its version on some set-ups) are pointed at stderr instead.
+    global _JSON_OUT
+    sys.stdout.flush()
+    _JSON_OUT = os.fdopen(os.dup(1), "w")
+    os.dup2(2, 1)
+
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=200)
@@ -693,7 +710,7 @@ def main():
             return
         run = reference_cpu_run(args.warmup, args.steps)
         tbs = run["tbs"]
-        print(json.dumps({"impl": "reference", "metric": METRIC, "value": round(tbs, 6), "unit": "TB/s",
+        emit({"impl": "reference", "metric": METRIC, "value": round(tbs, 6), "unit": "TB/s",
                           "n_gpus": args.gpus, "steps": run["steps_run"], "warmup": args.warmup,
                           "ms_per_step": round(run["ms_per_step"], 3), "higher_is_better": True, "scaling": "weak",
                           "vs_baseline": None, "dtype": "bf16->e4m3", "data": "synthetic (seeded N(0,1))",
@@ -701,7 +718,7 @@ def main():
                           "cpu_baseline": {"value": round(tbs, 6), "unit": "TB/s", "cores": run["cores"],
                                            "kind": run["kind"], "sample": run["sample"]},
                           "e2e": {"value": round(tbs, 6), "unit": "TB/s", "h2d_bytes_per_step": 0,
-                                  "d2h_bytes_per_step": 0}}))
+                                  "d2h_bytes_per_step": 0}})
         return
 
     import torch
@@ -842,7 +859,7 @@ def main():
             line["secondary"] = secondary
         if sharded:
             line["sharded_config5"] = sharded
-        print(json.dumps(line))
+        emit(line)
     if world > 1:
         dist.destroy_process_group()
 
