@@ -56,7 +56,9 @@ def test_int8_scaled_mm_azp_golden(name):
 
 
 @pytest.mark.parametrize("M,N,K", [(1, 64, 16), (16, 256, 128), (129, 300, 48), (200, 128, 8208), (256, 1000, 256),
-                                   (300, 512, 1024), (5, 17, 32), (1024, 2048, 4096)])
+                                   (300, 512, 1024), (5, 17, 32), (1024, 2048, 4096),
+                                   # 128 < M <= 256 on CTA pairs with 256 x 448 tiles, N not a multiple of 448
+                                   (256, 28672, 256), (129, 20480, 512), (200, 24576, 128), (256, 28416, 64)])
 def test_w8a8_shapes_exact(M, N, K):
     rng = seeded(M * 7 + N + K)
     a, b = _i8(rng, (M, K)), _i8(rng, (N, K))
