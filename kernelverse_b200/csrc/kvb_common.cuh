@@ -253,6 +253,22 @@ __device__ __forceinline__ float2 f2_unpack(uint64_t v) {
   return r;
 }
 
+__device__ __forceinline__ uint64_t f2_add(uint64_t a, uint64_t b) {
+  uint64_t r;
+  asm("add.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
+  return r;
+}
+__device__ __forceinline__ uint64_t f2_mul(uint64_t a, uint64_t b) {
+  uint64_t r;
+  asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
+  return r;
+}
+__device__ __forceinline__ uint64_t f2_fma(uint64_t a, uint64_t b, uint64_t c) {
+  uint64_t r;
+  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(r) : "l"(a), "l"(b), "l"(c));
+  return r;
+}
+
 // div_rn_fast on two dividends at once: the same three correctly rounded steps per lane.
 __device__ __forceinline__ uint64_t div2_rn_fast(uint64_t a, const Divisor& d) {
   const uint64_t y = f2_pack(d.y, d.y), nb = f2_pack(-d.b, -d.b);
@@ -303,6 +319,13 @@ __device__ __forceinline__ uint32_t quant4_fast_x2(uint64_t a01, uint64_t a23, c
   asm("add.rn.f32x2 %0, %1, %2;" : "=l"(r23) : "l"(div2_rn_fast(a23, d)), "l"(k));
   const uint32_t b0 = (uint32_t)r01, b1 = (uint32_t)(r01 >> 32), b2 = (uint32_t)r23, b3 = (uint32_t)(r23 >> 32);
   return __byte_perm(__byte_perm(b0, b1, 0x0040), __byte_perm(b2, b3, 0x0040), 0x5410);
+}
+
+// quant_e4m3x2<false> on a packed pair (low lane in the low byte), the quotients computed with
+// packed arithmetic; identical results.
+__device__ __forceinline__ uint16_t quant_e4m3x2_fast_x2(uint64_t ab, const Divisor& d) {
+  const float2 q = f2_unpack(div2_rn_fast(ab, d));
+  return static_cast<uint16_t>(__nv_cvt_float2_to_fp8x2(q, __NV_SATFINITE, __NV_E4M3));
 }
 
 // e4m3fn codes of clamp(x / scale, +-448) for two values (a in the low byte).  The

@@ -183,6 +183,7 @@ __device__ __forceinline__ void issue_row(const T* x, const T* res, int64_t row,
 }
 
 // Codes of one thread's VPT vectors of a row (y already in s), packed 8 per 64-bit store.
+// Unchecked divisors take the packed-float32 quotients (two lanes per instruction).
 template <int VPT, int MODE, bool kChecked>
 __device__ __forceinline__ void store_codes(const float (&s)[VPT][8], const Divisor& dv, uint2* crow, int tid,
                                             int stride, int nvec) {
@@ -191,12 +192,17 @@ __device__ __forceinline__ void store_codes(const float (&s)[VPT][8], const Divi
     const int v = tid + j * stride;
     if (v < nvec) {
       uint32_t lo, hi;
-      if (MODE == kQuantE4m3) {
+      if (MODE == kQuantE4m3 && !kChecked) {
+        lo = quant_e4m3x2_fast_x2(f2_pack(s[j][0], s[j][1]), dv) |
+             ((uint32_t)quant_e4m3x2_fast_x2(f2_pack(s[j][2], s[j][3]), dv) << 16);
+        hi = quant_e4m3x2_fast_x2(f2_pack(s[j][4], s[j][5]), dv) |
+             ((uint32_t)quant_e4m3x2_fast_x2(f2_pack(s[j][6], s[j][7]), dv) << 16);
+      } else if (MODE == kQuantE4m3) {
         lo = quant_e4m3x2<kChecked>(s[j][0], s[j][1], dv) | ((uint32_t)quant_e4m3x2<kChecked>(s[j][2], s[j][3], dv) << 16);
         hi = quant_e4m3x2<kChecked>(s[j][4], s[j][5], dv) | ((uint32_t)quant_e4m3x2<kChecked>(s[j][6], s[j][7], dv) << 16);
       } else if (!kChecked) {
-        lo = quant4_fast(s[j][0], s[j][1], s[j][2], s[j][3], dv);
-        hi = quant4_fast(s[j][4], s[j][5], s[j][6], s[j][7], dv);
+        lo = quant4_fast_x2(f2_pack(s[j][0], s[j][1]), f2_pack(s[j][2], s[j][3]), dv);
+        hi = quant4_fast_x2(f2_pack(s[j][4], s[j][5]), f2_pack(s[j][6], s[j][7]), dv);
       } else {
         lo = hi = 0;
 #pragma unroll
@@ -266,7 +272,7 @@ __global__ void __launch_bounds__(512) add_rmsnorm_pipe_kernel(const T* __restri
     const uint4* sx = reinterpret_cast<const uint4*>(smem + st * 2 * row_bytes);
     const uint4* sr = reinterpret_cast<const uint4*>(smem + st * 2 * row_bytes + row_bytes);
     float s[VPT][8];
-    float ss = 0.0f;
+    uint64_t ss2 = f2_pack(0.0f, 0.0f);
 #pragma unroll
     for (int j = 0; j < VPT; ++j) {
       const int v = tid + j * nthr;
@@ -280,17 +286,22 @@ __global__ void __launch_bounds__(512) add_rmsnorm_pipe_kernel(const T* __restri
         float fb[8];
         a.unpack(s[j]);
         b.unpack(fb);
+        // s = x + r and the sum of squares on packed pairs (two partial sums)
 #pragma unroll
-        for (int e = 0; e < 8; ++e) {
-          s[j][e] += fb[e];
-          ss = fmaf(s[j][e], s[j][e], ss);
+        for (int e = 0; e < 8; e += 2) {
+          const uint64_t p = f2_add(f2_pack(s[j][e], s[j][e + 1]), f2_pack(fb[e], fb[e + 1]));
+          ss2 = f2_fma(p, p, ss2);
+          const float2 u = f2_unpack(p);
+          s[j][e] = u.x;
+          s[j][e + 1] = u.y;
         }
       } else {
 #pragma unroll
         for (int e = 0; e < 8; ++e) s[j][e] = 0.0f;
       }
     }
-    ss = block_reduce_1bar<false>(ss, red_sum);   // after this every thread has finished reading stage st
+    const float2 ssp = f2_unpack(ss2);
+    const float ss = block_reduce_1bar<false>(ssp.x + ssp.y, red_sum);   // after this every thread has read stage st
     if (tid == 0) {
       const int64_t next = row + kStages * G;
       if (next < rows) issue_row(x, res, next, nvec, smem + st * 2 * row_bytes, row_bytes, &full[st], pol);
@@ -323,10 +334,13 @@ __global__ void __launch_bounds__(512) add_rmsnorm_pipe_kernel(const T* __restri
           o.pack(s[j]);
           o.store(orow + (int64_t)v * 8);
         }
+        const uint64_t r2 = f2_pack(rinv, rinv);
 #pragma unroll
-        for (int e = 0; e < 8; ++e) {
-          s[j][e] = __fmul_rn(__fmul_rn(s[j][e], rinv), wf[j][e]);
-          amax = fmaxf(amax, fabsf(s[j][e]));
+        for (int e = 0; e < 8; e += 2) {   // y = (s * rinv) * w on packed pairs
+          const float2 y = f2_unpack(f2_mul(f2_mul(f2_pack(s[j][e], s[j][e + 1]), r2), f2_pack(wf[j][e], wf[j][e + 1])));
+          s[j][e] = y.x;
+          s[j][e + 1] = y.y;
+          amax = fmaxf(amax, fmaxf(fabsf(y.x), fabsf(y.y)));
         }
       }
     }
