@@ -325,3 +325,55 @@ def test_flash_attn_with_kvcache_shapes(dt, b, sq, sk, h, hkv, d, ragged):
     _close(host(out), r_out, dt == "FP32")
     np.testing.assert_allclose(host(lse), r_lse, rtol=1e-4, atol=1e-4 if dt == "FP32" else 2e-3)
 
+
+
+def test_fp8_decode_partition_boundaries():
+    """Rows whose lengths end exactly on, just before and just after partition boundaries (the
+    last partition full, one row long, or one row short)."""
+    lens = [512, 1024, 513, 511, 1, 1536, 2047, 16]
+    case = make_fp8_case(seeded(31), len(lens), 32, 8, 128, 16, lens)
+    out, kc, vc = run_fp8(case, True, 512)
+    ref, rk, rv = oracle_fp8(case, True)
+    np.testing.assert_array_equal(host(kc), rk)
+    _close(host(out), ref, False)
+
+
+def test_fp8_decode_many_rows_plain_grid():
+    """1100 short rows (a grid of 1100 x 3 CTAs, most of them past their row's end)."""
+    rng = seeded(32)
+    lens = rng.integers(1, 40, 1100).tolist()
+    case = make_fp8_case(rng, 1100, 8, 1, 128, 16, lens)
+    out, kc, vc = run_fp8(case, True, 16)
+    ref, rk, rv = oracle_fp8(case, True)
+    np.testing.assert_array_equal(host(kc), rk)
+    _close(host(out), ref, False)
+
+
+def test_fp8_decode_repeated_calls_and_graph_replay():
+    """Repeated calls and replays of one captured launch (decode + merge as programmatic
+    dependents inside a CUDA graph) give the first call's result bit for bit."""
+    rng = seeded(33)
+    lens = rng.integers(100, 3000, 24).tolist()
+    case = make_fp8_case(rng, 24, 32, 8, 128, 16, lens)
+    bf = torch.bfloat16
+    u8 = lambda a: torch.from_numpy(np.ascontiguousarray(a)).cuda().view(torch.float8_e4m3fn)  # noqa: E731
+    args = (dev(case["q"], bf), u8(case["kc"]), u8(case["vc"]), dev(case["k_scale"]), dev(case["v_scale"]),
+            dev(case["lens"]), dev(case["bt"]))
+    first = _ops().paged_fp8_decode(*args)
+    ref, _, _ = oracle_fp8(case, False)
+    _close(host(first), ref, False)
+    for _ in range(70):
+        assert torch.equal(_ops().paged_fp8_decode(*args), first)
+    s = torch.cuda.Stream()
+    s.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(s):
+        _ops().paged_fp8_decode(*args)          # warm-up on the capture stream
+    torch.cuda.current_stream().wait_stream(s)
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g):
+        captured = _ops().paged_fp8_decode(*args)
+    for _ in range(5):
+        captured.zero_()
+        g.replay()
+        torch.cuda.synchronize()
+        assert torch.equal(captured, first)
