@@ -37,6 +37,13 @@ namespace {
 
 constexpr int kBM = 128;
 constexpr int kBK = 128;          // bytes of K per stage = one 128-byte swizzle row
+// k-blocks of B requested into L2 ahead of the shared-memory ring (single-wave, small-M launches)
+#ifndef KVB_GEMM_PREFETCH_1SM
+#define KVB_GEMM_PREFETCH_1SM 1
+#endif
+#ifndef KVB_GEMM_PREFETCH_2SM
+#define KVB_GEMM_PREFETCH_2SM 0
+#endif
 constexpr int kUmmaK = 32;        // K of one kind::i8 MMA
 constexpr int kEpiWarps = 8;      // two epilogue warps per TMEM lane quarter
 constexpr int kThreads = 64 + 32 * kEpiWarps;   // producer, MMA issuer, epilogue warps
@@ -54,6 +61,7 @@ struct GemmArgs {
   int64_t ldo;
   int out_dtype;         // KVB_BF16 / KVB_F16 / KVB_F32 / KVB_I32
   int n_blocks, m_blocks, tiles;
+  int m_fastest;         // tile order: M fastest over every M block (A stays in L2)
   // Fused all-gather: every output tile is also stored into these peer buffers (same layout,
   // columns offset by col_off).  nout == 0 for a plain GEMM.
   int nout;
@@ -95,6 +103,11 @@ __device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, i
       ::"r"(smem_u32(dst)), "l"(map), "r"(x), "r"(y), "r"(smem_u32(bar)), "l"(policy)
       : "memory");
 }
+// L2 prefetch of one tensor-map tile (no shared memory, no barrier).
+__device__ __forceinline__ void tma_prefetch_2d(const CUtensorMap* map, int x, int y) {
+  asm volatile("cp.async.bulk.prefetch.tensor.2d.L2.global.tile [%0, {%1, %2}];" ::"l"(map), "r"(x), "r"(y) : "memory");
+}
+
 __device__ __forceinline__ uint64_t policy_evict_last() {
   uint64_t p;
   asm volatile("createpolicy.fractional.L2::evict_last.b64 %0, 1.0;" : "=l"(p));
@@ -217,9 +230,17 @@ __device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&r)[32]) {
   asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
 }
 
-// Tile order: M fastest inside a group of 8 N blocks, so the CTAs running at the same time
-// share B tiles in L2 and A (which fits in L2) is re-read from L2.
+// Tile order.  When A fits in L2 with room to spare (m_fastest): M fastest over every M block,
+// so the CTAs running at the same time share a few B column blocks, each B byte comes from DRAM
+// once and A is read from L2 (M = 4096, K = 8192: 316 MB read from DRAM against 268 MB of
+// operands; 494 MB with the grouped order).  Otherwise N fastest inside groups of 8 N blocks,
+// so A streams from DRAM once per group and B's group stays in L2.
 __device__ __forceinline__ void tile_coords(const GemmArgs& g, int t, int& mb, int& nb) {
+  if (g.m_fastest) {
+    mb = t % g.m_blocks;
+    nb = t / g.m_blocks;
+    return;
+  }
   constexpr int kGroup = 8;
   const int per_group = kGroup * g.m_blocks;
   const int grp = t / per_group;
@@ -485,6 +506,18 @@ __global__ void __launch_bounds__(kThreads, 1) w8a8_gemm_kernel(const __grid_con
         tile_coords(g, t, mb, nb);
         const int ya = mb * kTileM + (int)crank * kBM, yb = nb * TN + (int)crank * kBRows;
         for (int kb = 0; kb < KB; ++kb, ++it) {
+          constexpr int kPrefetchAhead = k2Sm ? KVB_GEMM_PREFETCH_2SM : KVB_GEMM_PREFETCH_1SM;
+          if (kPrefetchAhead > 0 && g.m_blocks <= 2 && g.tiles <= tstride) {
+            // One wave of tiles streaming B from DRAM once: request k-block kb + kPrefetchAhead
+            // into L2 now, before its stage is free, so the DRAM stream is not bound by this
+            // SM's stage ring alone (M = 16, one CTA per SM: 42.9 -> 36.7 us at distance 1,
+            // 38.3 at 2; CTA pairs at M = 256 and launches of more than one wave run slower
+            // with it).
+            const int kp = kb + kPrefetchAhead;
+            for (int kq = kb == 0 ? STAGES : kp; kq <= kp && kq < KB; ++kq)
+#pragma unroll
+              for (int n = 0; n < NSUB; ++n) tma_prefetch_2d(&tmap_b, kq * kBK, yb + n * BN);
+          }
           const int s = it % STAGES;
           const uint32_t use = it / STAGES;
           if (use > 0 && !mbar_wait_bounded(&empty[s], (use - 1) & 1u)) {
@@ -851,6 +884,7 @@ int launch_gemm(const int8_t* a, const int8_t* b_nk, GemmArgs& g, void* const* d
   if (rc) return rc;
   g.m_blocks = (g.M + kTileM - 1) / kTileM;
   g.n_blocks = (g.N + BN * NSUB - 1) / (BN * NSUB);
+  g.m_fastest = (int64_t)g.m_blocks * kTileM * g.K <= (int64_t)48 << 20;   // A <= 48 MB of the 126 MB L2
   g.tiles = g.m_blocks * g.n_blocks;
   OutMaps om;
   memset(&om, 0, sizeof(om));

@@ -475,7 +475,11 @@ int launch_teams_any(const T* x, int64_t ngroups, int64_t gvec, float eps, int8_
 template <typename T, int WG>
 int launch_rolling(const T* x, int64_t ngroups, int64_t gvec, float eps, int8_t* q, float* scales, cudaStream_t st) {
   constexpr int kTeams = kTeamThreads / 32 / WG;
-  const int64_t grid = std::min<int64_t>((ngroups + kTeams - 1) / kTeams, 2 * (int64_t)sm_count());
+  // Two CTAs per SM at most, then as few CTAs as give every team the same number of rounds
+  // (2048 groups: 256 CTAs of 4 rounds each rather than 296 with a last round 46 % full).
+  int64_t grid = std::min<int64_t>((ngroups + kTeams - 1) / kTeams, 2 * (int64_t)sm_count());
+  const int64_t rounds = (ngroups + grid * kTeams - 1) / (grid * kTeams);
+  grid = (ngroups + kTeams * rounds - 1) / (kTeams * rounds);
   const bool full = gvec == 2 * WG * 32;
   cudaError_t e = full ? launch_pdl(group_quant_rolling_kernel<T, 2, WG, true>, dim3((unsigned)grid),
                                     dim3(kTeamThreads), 0, st, x, ngroups, (int)gvec, eps, q, scales)
