@@ -402,7 +402,8 @@ def gemm_benchmarks(torch, ops, hbm_peak):
         entry = {"workload": f"W8A8 GEMM M={M}, N={N}, K={K}, bf16 out (BASELINE config 3)",
                  "kernel": ("w8a8_gemm_kernel 256x256 tiles on CTA pairs (cta_group::2)" if M > 256 else
                             "w8a8_gemm_kernel 256x448 tiles on CTA pairs (two N=224 MMAs per k-step)" if M > 128
-                            else "w8a8_gemm_kernel 128x208 tiles, one CTA per SM"), "us_per_call": round(us, 2),
+                            else "w8a8_gemm_kernel 128x208 tiles, one CTA per SM, B prefetched into L2 one k-block "
+                            "ahead"), "us_per_call": round(us, 2),
                  "tops": round(ops_ / us / 1e6, 1), "bytes_per_call": nbytes,
                  "achieved_gbs": round(nbytes / us / 1e3, 1), "hbm_frac": round(nbytes / us / 1e3 / hbm_peak, 4)}
         if M == 4096:
@@ -413,6 +414,9 @@ def gemm_benchmarks(torch, ops, hbm_peak):
             entry["library"] = "torch._int_mm (cuBLASLt int8, int32 out, same shape)"
             entry["frac_of_library_int8"] = round(entry["tops"] / lib_tops, 4)
             entry["frac_of_nominal_4500_tops"] = round(entry["tops"] / 4500.0, 4)
+            # ncu dram__bytes_read + dram__bytes_write of one launch (committed summary)
+            entry["traffic_per_launch_bytes"] = profile_traffic("w8a8_gemm_c3.md")
+            entry["operand_bytes"] = M * K + N * K
         res.append(entry)
         del a, b
     # the gate+up projection (N = 57344 = 2 x 28672) with SwiGLU fused into the epilogue, against
