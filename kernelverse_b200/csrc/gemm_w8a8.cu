@@ -41,6 +41,7 @@ constexpr int kBK = 128;          // bytes of K per stage = one 128-byte swizzle
 #ifndef KVB_GEMM_PREFETCH_1SM
 #define KVB_GEMM_PREFETCH_1SM 1
 #endif
+constexpr int kPreWaitBlocks = 6;   // k-blocks of B prefetched into L2 before the programmatic wait (small M)
 #ifndef KVB_GEMM_PREFETCH_2SM
 #define KVB_GEMM_PREFETCH_2SM 0
 #endif
@@ -490,6 +491,18 @@ __global__ void __launch_bounds__(kThreads, 1) w8a8_gemm_kernel(const __grid_con
   // Launched as a programmatic dependent of the previous kernel in the stream: everything above
   // (barriers, TMEM, descriptor prefetch) overlaps that kernel's tail; nothing global is read or
   // written before it has completed.  Kernels after this one may be scheduled as SMs free up.
+  if (warp == 0 && lane == 0 && g.m_blocks <= 2 && tile0 < g.tiles) {
+    // B streams from DRAM once: the first k-blocks of this CTA's first tile start on their way
+    // into L2 during that tail (an L2 prefetch returns no data to the SM, so it may precede the
+    // wait: a line the previous kernel writes later is updated in L2 before any load reads it).
+    // M = 256: 53.9 -> 52.0 us.
+    int mb, nb;
+    tile_coords(g, tile0, mb, nb);
+    const int yb = nb * TN + (int)crank * kBRows;
+    for (int kq = 0; kq < KB && kq < kPreWaitBlocks; ++kq)
+#pragma unroll
+      for (int n = 0; n < NSUB; ++n) tma_prefetch_2d(&tmap_b, kq * kBK, yb + n * BN);
+  }
   pdl_wait();
   pdl_trigger();
 

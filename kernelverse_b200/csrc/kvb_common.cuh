@@ -188,6 +188,14 @@ __device__ __forceinline__ float block_reduce_1bar(float v, float* buf) {
 // run its own set-up, but it too reads and writes nothing global before its pdl_wait(), which
 // is what makes an early trigger safe.  Both return at once without a dependent launch.
 __device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+
+// Bulk prefetch of [src, src + bytes) into L2 (src and bytes multiples of 16).  It returns no
+// data to the SM and L2 is where every SM's writes meet, so issuing it before pdl_wait() is
+// safe: a line the previous grid writes afterwards is updated in L2, and the loads that read it
+// are issued after the wait.
+__device__ __forceinline__ void prefetch_l2_bulk(const void* src, uint32_t bytes) {
+  asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(src), "r"(bytes) : "memory");
+}
 __device__ __forceinline__ void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;"); }
 
 template <typename... KArgs, typename... Args>
