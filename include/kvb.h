@@ -362,7 +362,8 @@ KVB_API int kvb_batched_prefill_attention(const void* q, const void* k, const vo
  * The same with the kernel chosen (test hook, no reference counterpart): variant 0 = automatic
  * (tcgen05 for f16 / bf16 with head_dim a multiple of 16 in [64, 128], at least 128 query and
  * key tokens and a 16-byte-aligned out; otherwise the mma.sync kernel), 1 = the mma.sync
- * kernel, 2 = the tcgen05 kernel (KVB_E_SHAPE where it does not apply).
+ * kernel, 2 = the tcgen05 kernel with one 128-row query tile per CTA, 3 = the tcgen05 kernel
+ * with two query tiles per CTA (KVB_E_SHAPE where tcgen05 does not apply).
  */
 KVB_API int kvb_batched_prefill_attention_variant(const void* q, const void* k, const void* v, int dtype,
                                                   const int32_t* qo_indptr, const int32_t* kv_indptr, int batch,

@@ -393,7 +393,7 @@ int dispatch_prefill(const PrefillArgs& a, int tiles_ub, cudaStream_t st) {
 
 int prefill_tcgen05(const void* q, const void* k, const void* v, bool bf16, const int32_t* qo, const int32_t* kvp,
                     int batch, int64_t total_q, int64_t total_kv, int hq, int hkv, int D, float scale_log2, void* out,
-                    cudaStream_t st);
+                    int kernel, cudaStream_t st);
 
 }  // namespace kvb
 
@@ -418,7 +418,7 @@ extern "C" int kvb_batched_prefill_attention_variant(const void* q, const void* 
                                                      int64_t total_q, int64_t total_kv, int num_q_heads,
                                                      int num_kv_heads, int head_dim, float softmax_scale, void* out,
                                                      int variant, void* stream) {
-  if (variant < 0 || variant > 2) return set_error(KVB_E_ARG, "batched_prefill_attention: variant %d", variant);
+  if (variant < 0 || variant > 3) return set_error(KVB_E_ARG, "batched_prefill_attention: variant %d", variant);
   if (batch < 0 || total_q < 0 || total_kv < 0 || num_q_heads <= 0 || num_kv_heads <= 0 || head_dim <= 0)
     return set_error(KVB_E_ARG, "batched_prefill_attention: bad sizes");
   if (num_q_heads % num_kv_heads) return set_error(KVB_E_SHAPE, "batched_prefill_attention: num_q_heads must be a multiple of num_kv_heads");
@@ -443,10 +443,10 @@ extern "C" int kvb_batched_prefill_attention_variant(const void* q, const void* 
   // mma.sync kernel.
   const bool tc_ok = (dtype == KVB_BF16 || dtype == KVB_F16) && head_dim % 16 == 0 && head_dim >= 64 &&
                      total_q >= 128 && total_kv >= 128 && aligned16(out) && softmax_scale != 0.0f;
-  if (variant == 2 && !tc_ok) return set_error(KVB_E_SHAPE, "batched_prefill_attention: no tcgen05 kernel for this case");
+  if (variant >= 2 && !tc_ok) return set_error(KVB_E_SHAPE, "batched_prefill_attention: no tcgen05 kernel for this case");
   if (tc_ok && variant != 1)
     return prefill_tcgen05(q, k, v, dtype == KVB_BF16, qo_indptr, kv_indptr, batch, total_q, total_kv, num_q_heads,
-                           num_kv_heads, head_dim, a.scale_log2, out, st);
+                           num_kv_heads, head_dim, a.scale_log2, out, variant == 0 ? 0 : variant - 1, st);
   switch (dtype) {
     case KVB_BF16: return dispatch_prefill<__nv_bfloat16>(a, (int)tiles_ub, st);
     case KVB_F16: return dispatch_prefill<__half>(a, (int)tiles_ub, st);

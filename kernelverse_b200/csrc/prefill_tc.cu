@@ -474,6 +474,312 @@ __global__ void __launch_bounds__(kTcThreads, 1) prefill_tc_kernel(const __grid_
   }
 }
 
+// Two query tiles per CTA (ping-pong): rows [i0, i0 + 256) of one request and one query head as
+// tiles A = [i0, i0 + 128) and B = [i0 + 128, i0 + 256), sharing every K / V tile.  Each tile has
+// one S buffer and its O in tensor memory (S_A | O_A | S_B | O_B = 512 columns), its own group
+// of four softmax warps (warps 2-5: A, 6-9: B), and its chain S_j -> softmax -> PV_j -> S_{j+1};
+// the MMA lane interleaves the two chains, so one tile's exponentials overlap the other tile's
+// MMAs, and each K / V byte staged in shared memory serves 256 query rows.
+constexpr int kPpThreads = 320;            // producer, MMA, two softmax groups of four warps
+constexpr int kPpRing = 2;                 // K / V stages
+#ifndef KVB_PREFILL_PP_MIN_BLOCKS
+#define KVB_PREFILL_PP_MIN_BLOCKS 148
+#endif
+constexpr int kPpMinBlocks = KVB_PREFILL_PP_MIN_BLOCKS;   // (head, 256-row block) items from which auto picks it
+
+template <typename T, int DC>
+__global__ void __launch_bounds__(kPpThreads, 1) prefill_pp_kernel(const __grid_constant__ CUtensorMap tq,
+                                                                   const __grid_constant__ CUtensorMap tk,
+                                                                   const __grid_constant__ CUtensorMap tv,
+                                                                   const __grid_constant__ TcArgs a) {
+  constexpr bool kBf = std::is_same<T, __nv_bfloat16>::value;
+  constexpr uint32_t kOpBytes = DC * kChunkBytes;          // one Q / K / V tile
+  constexpr uint32_t kV0 = 0, kK0 = kPpRing * kOpBytes, kQ0 = 2 * kPpRing * kOpBytes;   // Q tile t at kQ0 + t * kOpBytes
+  constexpr uint32_t kTmemCols = 512;
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  const uint32_t sbase = smem_u32(smem);
+  // s_full / p_full / pv_done: one per query tile, one phase per key tile of that query tile.
+  __shared__ uint64_t q_full, k_full[kPpRing], v_full[kPpRing], kv_empty[kPpRing], s_full[2], p_full[2], pv_done[2],
+      mma_done;
+  __shared__ uint32_t tmem_base_s;
+  __shared__ volatile int s_abort;
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int h = blockIdx.x;
+  if (threadIdx.x == 0) {
+    mbar_init(&q_full, 1);
+    for (int s = 0; s < kPpRing; ++s) {
+      mbar_init(&k_full[s], 1);
+      mbar_init(&v_full[s], 1);
+      mbar_init(&kv_empty[s], 1);
+    }
+    for (int t = 0; t < 2; ++t) {
+      mbar_init(&s_full[t], 1);
+      mbar_init(&p_full[t], 4);
+      mbar_init(&pv_done[t], 1);
+    }
+    mbar_init(&mma_done, 1);
+    s_abort = 0;
+    fence_mbar_init();
+    asm volatile("prefetch.tensormap [%0];" ::"l"(&tq) : "memory");
+    asm volatile("prefetch.tensormap [%0];" ::"l"(&tk) : "memory");
+    asm volatile("prefetch.tensormap [%0];" ::"l"(&tv) : "memory");
+  }
+  pdl_trigger();
+  pdl_wait();            // launched as a programmatic dependent: global data from here on
+
+  // (request, 256-row block) of this CTA: request b's blocks, last first.
+  int b = -1, blk = 0;
+  {
+    int rem = (int)blockIdx.y;
+    for (int r = 0; r < a.batch; ++r) {
+      const int ql = a.qo[r + 1] - a.qo[r];
+      const int nb = ql > 0 ? (ql + 2 * kTcRows - 1) / (2 * kTcRows) : 0;
+      if (rem < nb) {
+        b = r;
+        blk = nb - 1 - rem;
+        break;
+      }
+      rem -= nb;
+    }
+  }
+  if (b < 0) return;
+  const int q0 = a.qo[b], ql = a.qo[b + 1] - q0;
+  const int k0 = a.kvp[b], kl = a.kvp[b + 1] - k0;
+  if (q0 < 0 || (int64_t)q0 + ql > a.total_q || k0 < 0 || kl < 0 || (int64_t)k0 + kl > a.total_kv) {
+    if (threadIdx.x == 0) atomicOr(&g_tu_status, kStatusBadIndptrTc);
+    return;
+  }
+  const int i0 = blk * 2 * kTcRows;
+  const int off = kl - ql;                                 // position of query row i = off + i
+  int nt[2];                                               // key tiles of query tile t (0: tile empty)
+  for (int t = 0; t < 2; ++t) {
+    const int rows = min(kTcRows, ql - (i0 + t * kTcRows));
+    const int last = min(off + i0 + t * kTcRows + rows - 1, kl - 1);   // last key the tile attends
+    nt[t] = (rows > 0 && last >= 0) ? last / kTcKeys + 1 : 0;
+  }
+  const int n = max(nt[0], nt[1]);                          // key tiles of the CTA
+  const bool two = ql - i0 > kTcRows;                        // tile B holds rows
+  const int kvh = h / a.group;
+  const int D = a.D;
+
+  if (warp == 1) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(&tmem_base_s)),
+                 "r"(kTmemCols)
+                 : "memory");
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = tmem_base_s;
+
+  if (warp == 0) {
+    // ---------------------------------------------------------------- TMA producer
+    if (lane == 0) {
+      mbar_arrive_expect_tx(&q_full, (two ? 2u : 1u) * kOpBytes);
+      for (int t = 0; t < (two ? 2 : 1); ++t)
+        for (int c = 0; c < DC; ++c)
+          tma_load_3d(sbase + kQ0 + t * kOpBytes + c * kChunkBytes, &tq, c * 64, h, q0 + i0 + t * kTcRows, &q_full);
+      int issued = 0;
+      for (int j = 0, s = 0, ph = 0; j < n; ++j) {            // stage s = j % kPpRing, ph = (j / kPpRing) & 1
+        if (j >= kPpRing && !mbar_wait_bounded(&kv_empty[s], ph ^ 1)) {
+          s_abort = 1;
+          break;
+        }
+        if (s_abort) break;
+        const int kt = k0 + j * kTcKeys;
+        mbar_arrive_expect_tx(&k_full[s], kOpBytes);
+        for (int c = 0; c < DC; ++c)
+          tma_load_3d(sbase + kK0 + s * kOpBytes + c * kChunkBytes, &tk, c * 64, kvh, kt, &k_full[s]);
+        mbar_arrive_expect_tx(&v_full[s], kOpBytes);
+        for (int c = 0; c < DC; ++c)
+          tma_load_3d(sbase + kV0 + s * kOpBytes + c * kChunkBytes, &tv, c * 64, kvh, kt, &v_full[s]);
+        issued = j + 1;
+        if (++s == kPpRing) {
+          s = 0;
+          ph ^= 1;
+        }
+      }
+      // every copy this CTA issued has landed before it exits
+      mbar_wait_bounded(&q_full, 0);
+      for (int j = issued > kPpRing ? issued - kPpRing : 0; j < issued; ++j) {
+        mbar_wait_bounded(&k_full[j % kPpRing], (j / kPpRing) & 1);
+        mbar_wait_bounded(&v_full[j % kPpRing], (j / kPpRing) & 1);
+      }
+    }
+  } else if (warp == 1) {
+    // ---------------------------------------------------------------- MMA issuer
+    if (lane == 0) {
+      constexpr uint32_t kIdS = idesc_f16(kTcRows, kTcKeys, kBf, false);
+      const uint32_t id_pv = idesc_f16(kTcRows, D, kBf, true);
+      const int ksteps = D / 16;
+      // S_j of tile t into its S buffer (K_j has landed; the caller has seen PV_{j-1} of the tile,
+      // which read the P this buffer held, complete)
+      auto issue_s = [&](int t, int j) -> bool {
+        const int s = j % kPpRing;
+        if (!mbar_wait_bounded(&k_full[s], (uint32_t)(j / kPpRing) & 1u)) return false;
+        tc_fence_after();
+        for (int ks = 0; ks < ksteps; ++ks) {
+          const uint32_t off_b = (uint32_t)(ks >> 2) * kChunkBytes + (uint32_t)(ks & 3) * 32u;
+          mma_f16(tmem + (uint32_t)t * 256u, desc_kmajor(sbase + kQ0 + t * kOpBytes + off_b),
+                  desc_kmajor(sbase + kK0 + s * kOpBytes + off_b), kIdS, ks > 0);
+        }
+        mma_commit(&s_full[t]);
+        return true;
+      };
+      bool ok = mbar_wait_bounded(&q_full, 0);
+      for (int t = 0; t < 2 && ok; ++t)
+        if (nt[t] > 0) ok = issue_s(t, 0);
+      for (int j = 0; j < n && ok && !s_abort; ++j) {
+        const int s = j % kPpRing;
+        for (int t = 0; t < 2 && ok; ++t) {
+          if (j >= nt[t]) continue;
+          if (!mbar_wait_bounded(&p_full[t], (uint32_t)j & 1u) ||
+              !mbar_wait_bounded(&v_full[s], (uint32_t)(j / kPpRing) & 1u)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t vs = sbase + kV0 + s * kOpBytes;
+#pragma unroll
+          for (int ks = 0; ks < kTcKeys / 16; ++ks)   // P_j: 16 keys = 8 packed columns of the tile's S buffer
+            mma_f16_ts(tmem + (uint32_t)t * 256u + 128u, tmem + (uint32_t)t * 256u + (uint32_t)ks * 8u,
+                       desc_mnmajor(vs + (uint32_t)ks * 2048u, kChunkBytes), id_pv, (j | ks) != 0);
+          mma_commit(&pv_done[t]);
+          if (j + 1 < nt[t]) {
+            // S_{j+1} overwrites the P that PV_j reads: wait for PV_j first
+            if (!mbar_wait_bounded(&pv_done[t], (uint32_t)j & 1u)) {
+              ok = false;
+              break;
+            }
+            ok = issue_s(t, j + 1);
+          }
+        }
+        mma_commit(&kv_empty[s]);              // K_j and V_j are free once the MMAs above complete
+      }
+      if (!ok) s_abort = 1;
+      mma_commit(&mma_done);                   // every MMA issued above has completed before TMEM is freed
+      mbar_wait_bounded(&mma_done, 0);
+    }
+  } else {
+    // ---------------------------------------------------------------- softmax (warps 2-5: tile A, 6-9: tile B)
+    const int t = (warp - 2) >> 2;                         // query tile of this warp
+    const int quarter = warp & 3;                          // TMEM lanes this warp may access
+    const int row = quarter * 32 + lane;                   // query row of the tile = TMEM lane
+    const int ti0 = i0 + t * kTcRows;                      // first query row of the tile
+    const int pos = off + ti0 + row;
+    const int nj = nt[t];
+    const uint32_t lane_addr = (uint32_t)(quarter * 32) << 16;
+    const uint32_t s_col = (uint32_t)t * 256u, o_col = s_col + 128u;
+    const float sc = a.scale_log2;
+    float m_used = -INFINITY, l = 0.0f;
+    bool ok = true;
+    for (int j = 0; j < nj; ++j) {
+      if (__shfl_sync(0xffffffffu, s_abort, 0) || !warp_wait(&s_full[t], (uint32_t)j & 1u)) {   // warp-uniform
+        ok = false;
+        break;
+      }
+      tc_fence_after();
+      const uint32_t sa = tmem + lane_addr + s_col;
+      const int kb = j * kTcKeys;
+      const bool mask = kb + kTcKeys - 1 > off + ti0 + quarter * 32;   // some key of the tile may pass a row
+      uint32_t r[128];
+      tmem_ld128(sa, r);
+      if (mask) {
+#pragma unroll
+        for (int i = 0; i < 128; ++i)
+          if (kb + i > pos) r[i] = __float_as_uint(sc >= 0.0f ? -INFINITY : INFINITY);
+      }
+      float mx;
+      if (sc >= 0.0f) {
+        float m4[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
+#pragma unroll
+        for (int i = 0; i < 128; ++i) m4[i & 3] = fmaxf(m4[i & 3], __uint_as_float(r[i]));
+        mx = fmaxf(fmaxf(m4[0], m4[1]), fmaxf(m4[2], m4[3]));
+      } else {
+        float m4[4] = {INFINITY, INFINITY, INFINITY, INFINITY};
+#pragma unroll
+        for (int i = 0; i < 128; ++i) m4[i & 3] = fminf(m4[i & 3], __uint_as_float(r[i]));
+        mx = fminf(fminf(m4[0], m4[1]), fminf(m4[2], m4[3]));
+      }
+      mx *= sc;
+      const bool grow = mx > m_used + kLazyMax;
+      const float alpha = grow ? ex2_approx(m_used - mx) : 1.0f;
+      if (grow) m_used = mx;
+      l *= alpha;
+      const float neg_m = -m_used;
+      float l4[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+#pragma unroll
+      for (int hf = 0; hf < 2; ++hf) {                    // 64 keys -> 32 packed columns at a time
+        uint32_t w[32];
+#pragma unroll
+        for (int i = 0; i < 64; i += 2) {
+          const float p0 = ex2_approx(fmaf(__uint_as_float(r[64 * hf + i]), sc, neg_m));
+          const float p1 = ex2_approx(fmaf(__uint_as_float(r[64 * hf + i + 1]), sc, neg_m));
+          l4[(i >> 1) & 3] += p0 + p1;
+          w[i >> 1] = pack2h<kBf>(p0, p1);
+        }
+        tmem_st32(sa + 32u * hf, w);
+      }
+      l += (l4[0] + l4[1]) + (l4[2] + l4[3]);
+      // O *= alpha where the max moved (whole warp, when any of its rows needs it), once PV_{j-1}
+      // has completed
+      if (j > 0 && __any_sync(0xffffffffu, alpha != 1.0f)) {
+        if (!warp_wait(&pv_done[t], (uint32_t)(j - 1) & 1u)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        for (int c = 0; c < (D + 31) / 32; ++c) {
+          uint32_t r2[32];
+          tmem_ld32(tmem + lane_addr + o_col + c * 32, r2);
+#pragma unroll
+          for (int i = 0; i < 32; ++i) r2[i] = __float_as_uint(__uint_as_float(r2[i]) * alpha);
+          tmem_st32(tmem + lane_addr + o_col + c * 32, r2);
+        }
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&p_full[t]);
+    }
+    if (!ok) s_abort = 1;
+    // O / l of the valid rows
+    if (ok && (nj == 0 || warp_wait(&pv_done[t], (uint32_t)(nj - 1) & 1u))) {
+      tc_fence_after();
+      const float inv = 1.0f / l;
+      const bool valid = ti0 + row < ql;
+      T* orow = reinterpret_cast<T*>(a.out) + ((int64_t)q0 + ti0 + row) * a.hq * D + (int64_t)h * D;
+      for (int c = 0; c < (D + 31) / 32; ++c) {
+        uint32_t r2[32];
+        if (nj > 0) tmem_ld32(tmem + lane_addr + o_col + c * 32, r2);
+        else
+#pragma unroll
+          for (int i = 0; i < 32; ++i) r2[i] = 0u;
+        uint32_t w[16];
+#pragma unroll
+        for (int i = 0; i < 32; i += 2)
+          w[i >> 1] = pack2h<kBf>(__uint_as_float(r2[i]) * inv, __uint_as_float(r2[i + 1]) * inv);
+        if (valid) {
+#pragma unroll
+          for (int u = 0; u < 4; ++u)
+            if (c * 32 + u * 8 < D)
+              *reinterpret_cast<uint4*>(orow + c * 32 + u * 8) = make_uint4(w[4 * u], w[4 * u + 1], w[4 * u + 2], w[4 * u + 3]);
+        }
+      }
+    } else {
+      s_abort = 1;
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(kTmemCols) : "memory");
+  }
+}
+
 PFN_cuTensorMapEncodeTiled_v12000 encode_tiled() {
   static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
   static std::once_flag once;
@@ -521,12 +827,31 @@ int launch_tc(const CUtensorMap& mq, const CUtensorMap& mk, const CUtensorMap& m
   return check_launch("prefill_tc_kernel");
 }
 
+template <typename T, int DC>
+int launch_pp(const CUtensorMap& mq, const CUtensorMap& mk, const CUtensorMap& mv, const TcArgs& a, int blocks_ub,
+              cudaStream_t st) {
+  constexpr size_t smem = (2 * kPpRing + 2) * (size_t)DC * kChunkBytes + 1024;
+  auto kern = prefill_pp_kernel<T, DC>;
+  static int set_dev = -1;
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (set_dev != dev) {
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    if (e != cudaSuccess) return set_error(KVB_E_LAUNCH, "batched_prefill_attention: smem attribute: %s", cudaGetErrorString(e));
+    set_dev = dev;
+  }
+  cudaError_t e = launch_pdl(kern, dim3((unsigned)a.hq, (unsigned)blocks_ub), dim3(kPpThreads), smem, st, mq, mk, mv, a);
+  if (e != cudaSuccess) return set_error(KVB_E_LAUNCH, "prefill_pp_kernel: %s", cudaGetErrorString(e));
+  return check_launch("prefill_pp_kernel");
+}
+
 }  // namespace
 
-// Host entry used by prefill.cu for 16-bit inputs with head_dim % 16 == 0 and <= 128.
+// Host entry used by prefill.cu for 16-bit inputs with head_dim % 16 == 0 and <= 128.  kernel: 0
+// = automatic, 1 = one query tile per CTA, 2 = two query tiles per CTA.
 int prefill_tcgen05(const void* q, const void* k, const void* v, bool bf16, const int32_t* qo, const int32_t* kvp,
                     int batch, int64_t total_q, int64_t total_kv, int hq, int hkv, int D, float scale_log2, void* out,
-                    cudaStream_t st) {
+                    int kernel, cudaStream_t st) {
   const int64_t tiles_ub = total_q / kTcRows + batch;
   if (tiles_ub > 65535) return set_error(KVB_E_SHAPE, "batched_prefill_attention: too many query tiles");
   CUtensorMap mq, mk, mv;
@@ -537,6 +862,18 @@ int prefill_tcgen05(const void* q, const void* k, const void* v, bool bf16, cons
   TcArgs a{};
   a.qo = qo; a.kvp = kvp; a.out = out; a.total_q = total_q; a.total_kv = total_kv;
   a.batch = batch; a.hq = hq; a.hkv = hkv; a.group = hq / hkv; a.D = D; a.scale_log2 = scale_log2;
+  // Two query tiles per CTA once the (head, 256-row block) items fill the SMs (bf16, 32 / 8 heads,
+  // D = 128: 118.0 -> 107.2 us at q_lens [2048, 1536, 1024, 512], 650 -> 593 us at [8192, 512,
+  // 128, 32], 106.4 -> 101.0 us for 4 x 512 queries on 4096-1024 keys); smaller inputs keep one
+  // tile per CTA for the parallelism.
+  const int64_t blocks_ub = total_q / (2 * kTcRows) + batch;
+  const bool pp = kernel == 2 || (kernel == 0 && (int64_t)hq * (total_q / (2 * kTcRows)) >= kPpMinBlocks);
+  if (pp) {
+    if (D <= 64) return bf16 ? launch_pp<__nv_bfloat16, 1>(mq, mk, mv, a, (int)blocks_ub, st)
+                             : launch_pp<__half, 1>(mq, mk, mv, a, (int)blocks_ub, st);
+    return bf16 ? launch_pp<__nv_bfloat16, 2>(mq, mk, mv, a, (int)blocks_ub, st)
+                : launch_pp<__half, 2>(mq, mk, mv, a, (int)blocks_ub, st);
+  }
   if (D <= 64) return bf16 ? launch_tc<__nv_bfloat16, 1>(mq, mk, mv, a, (int)tiles_ub, st)
                            : launch_tc<__half, 1>(mq, mk, mv, a, (int)tiles_ub, st);
   return bf16 ? launch_tc<__nv_bfloat16, 2>(mq, mk, mv, a, (int)tiles_ub, st)

@@ -334,7 +334,8 @@ def batched_prefill_attention(q, k, v, qo_indptr, kv_indptr, softmax_scale: Opti
     q, k, v = q.contiguous(), k.contiguous(), v.contiguous()
     qo_indptr, kv_indptr = qo_indptr.contiguous(), kv_indptr.contiguous()
     out = torch.empty((tq, hq, d), dtype=q.dtype, device=dev)
-    # _variant (tests): 0 = automatic kernel choice, 1 = the mma.sync kernel, 2 = the tcgen05 kernel
+    # _variant (tests): 0 = automatic kernel choice, 1 = the mma.sync kernel, 2 / 3 = the tcgen05
+    # kernel with one / two query tiles per CTA
     call("kvb_batched_prefill_attention_variant", _ptr(q), _ptr(k), _ptr(v), kvb_dtype(q.dtype), _ptr(qo_indptr),
          _ptr(kv_indptr), qo_indptr.numel() - 1, tq, tkv, hq, hkv, d, float(scale), _ptr(out), int(_variant),
          _stream(dev))

@@ -67,7 +67,8 @@ def test_prefill_golden(name):
     np.testing.assert_allclose(host(out), g["out"][0].astype(np.float32), rtol=rtol, atol=atol)
 
 
-KERNELS = [("FP32", 1), ("FP16", 1), ("BF16", 1), ("FP16", 2), ("BF16", 2)]   # (dtype, 1 = mma.sync / 2 = tcgen05)
+# (dtype, 1 = mma.sync / 2 = tcgen05, one query tile per CTA / 3 = tcgen05, two query tiles per CTA)
+KERNELS = [("FP32", 1), ("FP16", 1), ("BF16", 1), ("FP16", 2), ("BF16", 2), ("FP16", 3), ("BF16", 3)]
 
 
 @pytest.mark.parametrize("dt,variant", KERNELS)
@@ -83,12 +84,14 @@ def test_prefill_shapes(dt, variant, q_lens, kv_lens, hq, hkv, d):
     _check(got, ref, dt)
 
 
-@pytest.mark.parametrize("variant", [1, 2])
+@pytest.mark.parametrize("variant", [1, 2, 3])
 @pytest.mark.parametrize("q_lens,kv_lens", [([130, 1, 255], [130, 1, 400]), ([128, 128], [128, 1000]),
-                                            ([7, 300], [64, 300])])
+                                            ([7, 300], [64, 300]), ([256, 257, 129], [256, 300, 129]),
+                                            ([384, 100], [1000, 100])])
 def test_prefill_tile_edges(variant, q_lens, kv_lens):
-    """Query and key counts one past / at / below the 128-row tiles, one-token requests, and a
-    request whose queries see far more keys than queries (chunked prefill)."""
+    """Query and key counts one past / at / below the 128-row tiles and the 256-row blocks of the
+    two-tile kernel (a block whose second tile is empty or holds one row), one-token requests, and
+    requests whose queries see far more keys than queries (chunked prefill)."""
     got, ref = _run(q_lens, kv_lens, 8, 2, 128, "BF16", 901 + sum(kv_lens), variant=variant)
     _check(got, ref, "BF16")
 
@@ -107,7 +110,7 @@ def test_prefill_scale_and_empty_request():
     _check(got, ref, "FP32")
 
 
-@pytest.mark.parametrize("variant", [1, 2])
+@pytest.mark.parametrize("variant", [1, 2, 3])
 def test_prefill_long_sequence(variant):
     """One 4096-token request (up to 64 key tiles per query tile) beside a short one."""
     got, ref = _run([4096, 64], [4096, 64], 4, 1, 128, "BF16", 77, variant=variant)
@@ -118,7 +121,9 @@ def test_prefill_variants_agree_closely():
     """Both kernels on the same inputs: the same P rounding and float32 accumulation."""
     a, ref = _run([512, 384, 256, 128], [512, 384, 256, 128], 32, 8, 128, "BF16", 3, variant=1)
     b, _ = _run([512, 384, 256, 128], [512, 384, 256, 128], 32, 8, 128, "BF16", 3, variant=2)
+    c, _ = _run([512, 384, 256, 128], [512, 384, 256, 128], 32, 8, 128, "BF16", 3, variant=3)
     assert np.max(np.abs(a - b)) <= 1.6e-2
+    assert np.array_equal(b, c)             # the two tcgen05 kernels do the same arithmetic per row
     assert np.mean(np.abs(a - ref)) <= 2e-3 and np.mean(np.abs(b - ref)) <= 2e-3
 
 
