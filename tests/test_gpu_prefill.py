@@ -87,10 +87,10 @@ def test_prefill_shapes(dt, variant, q_lens, kv_lens, hq, hkv, d):
 @pytest.mark.parametrize("variant", [1, 2, 3])
 @pytest.mark.parametrize("q_lens,kv_lens", [([130, 1, 255], [130, 1, 400]), ([128, 128], [128, 1000]),
                                             ([7, 300], [64, 300]), ([256, 257, 129], [256, 300, 129]),
-                                            ([384, 100], [1000, 100])])
+                                            ([384, 100], [1000, 100]), ([513, 640, 385], [513, 700, 385])])
 def test_prefill_tile_edges(variant, q_lens, kv_lens):
     """Query and key counts one past / at / below the 128-row tiles and the 256-row blocks of the
-    two-tile kernel (a block whose second tile is empty or holds one row), one-token requests, and
+    two-tile kernel (blocks whose second tile is empty or holds one row), one-token requests, and
     requests whose queries see far more keys than queries (chunked prefill)."""
     got, ref = _run(q_lens, kv_lens, 8, 2, 128, "BF16", 901 + sum(kv_lens), variant=variant)
     _check(got, ref, "BF16")
@@ -123,7 +123,7 @@ def test_prefill_variants_agree_closely():
     b, _ = _run([512, 384, 256, 128], [512, 384, 256, 128], 32, 8, 128, "BF16", 3, variant=2)
     c, _ = _run([512, 384, 256, 128], [512, 384, 256, 128], 32, 8, 128, "BF16", 3, variant=3)
     assert np.max(np.abs(a - b)) <= 1.6e-2
-    assert np.array_equal(b, c)             # the two tcgen05 kernels do the same arithmetic per row
+    assert np.array_equal(b, c)             # the tcgen05 kernels with one and two tiles per CTA: same arithmetic per row
     assert np.mean(np.abs(a - ref)) <= 2e-3 and np.mean(np.abs(b - ref)) <= 2e-3
 
 
