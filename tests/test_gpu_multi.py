@@ -27,3 +27,17 @@ def test_tp_gemm_allgather_two_gpus():
     r = subprocess.run(cmd, capture_output=True, text=True, cwd=ROOT, timeout=400)
     assert r.returncode == 0, r.stdout[-3000:] + r.stderr[-3000:]
     assert "TP_OK" in r.stdout, r.stdout[-3000:] + r.stderr[-3000:]
+
+
+@pytest.mark.timeout(900)
+def test_tp_gemm_allgather_all_gpus():
+    """The same check with one rank per GPU of the box (4 or 8 on a multi-GPU box)."""
+    if not torch.cuda.is_available() or torch.cuda.device_count() < 4:
+        pytest.skip("needs four or more GPUs")
+    n = torch.cuda.device_count()
+    cmd = ["timeout", "-k", "30", "600", sys.executable, "-m", "torch.distributed.run", "--nnodes=1",
+           f"--nproc-per-node={n}", "--master-addr=127.0.0.1", f"--master-port={_port()}",
+           str(ROOT / "tests" / "mgpu" / "tp_gemm_check.py")]
+    r = subprocess.run(cmd, capture_output=True, text=True, cwd=ROOT, timeout=700)
+    assert r.returncode == 0, r.stdout[-3000:] + r.stderr[-3000:]
+    assert r.stdout.count("TP_OK") >= 1, r.stdout[-3000:] + r.stderr[-3000:]
