@@ -3,9 +3,10 @@
 Each function mirrors the forward() of the KernelVerse reference operator it
 replaces (same argument order, meaning, output structure, shapes and dtypes)
 and runs one or more sm_100a kernels on the current CUDA stream.  PyTorch is
-used only to allocate outputs (``torch.empty``) and to hand raw pointers to the
-C ABI; no arithmetic happens here and there is no CPU path: CPU tensors are
-rejected.
+used only to allocate outputs (``torch.empty``), to copy and to hand raw
+pointers to the C ABI; no arithmetic happens here and there is no CPU path: CPU
+tensors are rejected, except by ``add_rmsnorm_quant_host``, which streams host
+tensors through the GPU kernel.
 """
 from __future__ import annotations
 
@@ -153,6 +154,75 @@ def add_rmsnorm_quant(x: torch.Tensor, residual: torch.Tensor, weight: torch.Ten
     call("kvb_add_rmsnorm_quant", _ptr(x), _ptr(residual), _ptr(weight), kvb_dtype(x.dtype), rows, h, float(eps),
          _ptr(r_out), _ptr(codes), kvb_dtype(quant_dtype), _ptr(scales), _stream(dev))
     return r_out, codes, scales
+
+
+_pipe_streams = {}
+_pipe_buffers = {}
+
+
+def add_rmsnorm_quant_host(x: torch.Tensor, residual: torch.Tensor, weight: torch.Tensor, eps: float,
+                           quant_dtype: torch.dtype = torch.float8_e4m3fn, out=None, device=None,
+                           chunk_rows: int = 1024, nstreams: int = 3):
+    """:func:`add_rmsnorm_quant` for host-resident ``[..., H]`` tensors, through the GPU.
+
+    Rows travel in chunks of ``chunk_rows`` through ``nstreams`` CUDA streams: chunk i's copy in,
+    its kernel and its copy out are queued on stream ``i % nstreams``, so the copies in and out of
+    different chunks (one copy engine each way) and the kernels overlap.  Rows are independent, so
+    the results equal :func:`add_rmsnorm_quant`'s.  Inputs should be pinned for the copies to
+    overlap.  Returns host tensors ``(residual_out, codes, scales)`` (into ``out`` when given); they
+    are complete once the current stream's work is, like any non-blocking copy to the host.
+    """
+    if x.is_cuda or residual.is_cuda:
+        raise ValueError("add_rmsnorm_quant_host takes host tensors; use add_rmsnorm_quant for device tensors")
+    if x.shape != residual.shape or x.dtype != residual.dtype:
+        raise ValueError("x and residual must have the same shape and dtype")
+    dev = torch.device(device) if device is not None else torch.device("cuda", torch.cuda.current_device())
+    h = x.shape[-1]
+    rows = x.numel() // max(h, 1)
+    x2, r2 = x.contiguous().view(rows, h), residual.contiguous().view(rows, h)
+    if out is None:
+        pin = torch.cuda.is_available()
+        out = (torch.empty(x.shape, dtype=x.dtype, pin_memory=pin), torch.empty(x.shape, dtype=quant_dtype, pin_memory=pin),
+               torch.empty(x.shape[:-1], dtype=torch.float32, pin_memory=pin))
+    h_rout, h_codes, h_scales = (t.view(rows, h) if i < 2 else t.view(rows) for i, t in enumerate(out))
+    cur = torch.cuda.current_stream(dev)
+    key = (dev.index, nstreams)
+    if key not in _pipe_streams:
+        _pipe_streams[key] = [torch.cuda.Stream(dev) for _ in range(nstreams)]
+    streams = _pipe_streams[key]
+    dw = weight.to(dev, non_blocking=True).contiguous()
+    dw.record_stream(cur)
+    cr = max(1, min(chunk_rows, rows))
+    # Device chunk buffers, one set per stream, kept across calls: a call's streams start after
+    # the current stream (s.wait_stream) and the current stream waits for them at the end, so
+    # the previous call's chunks are done with a set before this call reuses it.
+    bkey = (dev.index, nstreams, cr, h, x.dtype, quant_dtype)
+    slots = _pipe_buffers.get(bkey)
+    if slots is None:
+        slots = [(torch.empty((cr, h), dtype=x.dtype, device=dev), torch.empty((cr, h), dtype=x.dtype, device=dev),
+                  torch.empty((cr, h), dtype=x.dtype, device=dev), torch.empty((cr, h), dtype=quant_dtype, device=dev),
+                  torch.empty((cr,), dtype=torch.float32, device=dev)) for _ in streams]
+        _pipe_buffers.clear()              # one configuration at a time
+        _pipe_buffers[bkey] = slots
+    for s in streams:
+        s.wait_stream(cur)
+        dw.record_stream(s)
+    for i, r0 in enumerate(range(0, rows, cr)):
+        r1 = min(rows, r0 + cr)
+        n = r1 - r0
+        s = streams[i % nstreams]
+        dx, dr, drout, dcodes, dscales = slots[i % nstreams]
+        with torch.cuda.stream(s):
+            dx[:n].copy_(x2[r0:r1], non_blocking=True)
+            dr[:n].copy_(r2[r0:r1], non_blocking=True)
+            call("kvb_add_rmsnorm_quant", _ptr(dx), _ptr(dr), _ptr(dw), kvb_dtype(x.dtype), n, h, float(eps),
+                 _ptr(drout), _ptr(dcodes), kvb_dtype(quant_dtype), _ptr(dscales), s.cuda_stream)
+            h_rout[r0:r1].copy_(drout[:n], non_blocking=True)
+            h_codes[r0:r1].copy_(dcodes[:n], non_blocking=True)
+            h_scales[r0:r1].copy_(dscales[:n], non_blocking=True)
+    for s in streams:
+        cur.wait_stream(s)
+    return out
 
 
 # --------------------------------------------------------------------------- paged KV cache
