@@ -276,13 +276,16 @@ def make_c2_inputs(torch, dev, seed: int, rows: int = M_ROWS, hidden: int = HIDD
 
 
 def time_region(torch, fn, steps: int, dist, world: int):
-    """Barrier + sync on both sides; CUDA events on the launching stream; max over ranks."""
+    """Barrier + sync on both sides; CUDA events on the launching stream; max over ranks.  The
+    steps are queued behind a device spin (before the start event), so the events time the
+    device work of the steps and not how fast a host shared by several ranks enqueues them."""
     stream = torch.cuda.current_stream()
     if world > 1:
         dist.barrier()
     torch.cuda.synchronize()
     t_wall0 = time.time()
     start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    _backlog(torch, steps)
     start.record(stream)
     for _ in range(steps):
         fn()
