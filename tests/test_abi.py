@@ -67,3 +67,15 @@ def test_ops_reject_cpu_tensors():
     from kernelverse_b200 import ops
     with pytest.raises(ValueError, match="CUDA tensors only"):
         ops.per_token_group_quant_int8(torch.zeros(2, 8), 8, 1e-6)
+
+
+def test_host_entry_argument_checks_need_no_gpu():
+    """The host-buffer entry of the fused add+RMSNorm+quant takes host tensors of one shape; both
+    checks run before any CUDA call."""
+    import torch
+    from kernelverse_b200 import ops
+    x = torch.zeros(4, 64, dtype=torch.bfloat16)
+    with pytest.raises(ValueError, match="same shape"):
+        ops.add_rmsnorm_quant_host(x, torch.zeros(4, 32, dtype=torch.bfloat16), torch.ones(64), 1e-6)
+    with pytest.raises(ValueError, match="same shape"):
+        ops.add_rmsnorm_quant_host(x, torch.zeros(4, 64, dtype=torch.float16), torch.ones(64), 1e-6)
