@@ -150,19 +150,20 @@ def test_fused_tiny_values_quantise_to_zero(kind):
         assert np.all(codes[small] == 0)
 
 
-@pytest.mark.parametrize("m,h,chunk", [(3000, 4096, 512), (7, 8192, 1024), (1024, 2048, 1024)])
-def test_fused_host_pipeline_matches_device_op(m, h, chunk):
+@pytest.mark.parametrize("m,h,chunk,qd", [(3000, 4096, 512, torch.float8_e4m3fn), (7, 8192, 1024, torch.float8_e4m3fn),
+                                         (1024, 2048, 1024, torch.float8_e4m3fn), (1500, 4096, 1024, torch.int8)])
+def test_fused_host_pipeline_matches_device_op(m, h, chunk, qd):
     """Host buffers in and out through row chunks on several streams (ragged last chunk, a single
-    short chunk, exact chunks): the results equal the device op's bit for bit."""
+    short chunk, exact chunks, int8 codes): the results equal the device op's bit for bit."""
     x, r, w = _c2_inputs(seeded(m + h + chunk), m, h)
     bf = torch.bfloat16
     hx = torch.from_numpy(x).to(bf).pin_memory()
     hr = torch.from_numpy(r).to(bf).pin_memory()
     hw = torch.from_numpy(w).to(bf)
-    ro, codes, scales = _ops().add_rmsnorm_quant_host(hx, hr, hw, 1e-6, chunk_rows=chunk)
+    ro, codes, scales = _ops().add_rmsnorm_quant_host(hx, hr, hw, 1e-6, quant_dtype=qd, chunk_rows=chunk)
     torch.cuda.synchronize()
-    assert not ro.is_cuda and not codes.is_cuda and not scales.is_cuda
-    d_ro, d_codes, d_scales = _ops().add_rmsnorm_quant(hx.cuda(), hr.cuda(), hw.cuda(), 1e-6)
+    assert not ro.is_cuda and not codes.is_cuda and not scales.is_cuda and codes.dtype == qd
+    d_ro, d_codes, d_scales = _ops().add_rmsnorm_quant(hx.cuda(), hr.cuda(), hw.cuda(), 1e-6, quant_dtype=qd)
     assert torch.equal(ro, d_ro.cpu())
     assert torch.equal(codes.view(torch.uint8), d_codes.cpu().view(torch.uint8))
     assert torch.equal(scales, d_scales.cpu())
