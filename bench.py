@@ -16,7 +16,8 @@ sharded across GPUs with no collective on the data path: weak scaling).
 * ``e2e``: the same metric through the public op with HOST buffers
   (``ops.add_rmsnorm_quant_host``): each step copies x, residual and weight from pinned
   host memory, runs the kernel and copies residual_out, codes and scales back, in row
-  chunks on three streams so the copies in and out overlap.
+  chunks through three stage streams (copy in, kernel, copy out) so the copies in and out
+  overlap.
 * ``roofline``: the fused kernel's achieved GB/s against the measured HBM copy
   bandwidth; ``traffic`` is the DRAM bytes of one launch from the committed ncu
   summary.
@@ -811,8 +812,8 @@ def main():
     h_scales = torch.empty((M_ROWS,), dtype=torch.float32).pin_memory()
 
     def e2e_step():
-        # host in, host out through the public op: row chunks stream through three CUDA streams,
-        # so the copies in and out (one copy engine each way) and the kernels overlap
+        # host in, host out through the public op: row chunks stream through one CUDA stream per
+        # stage, so the copies in and out (one copy engine each way) and the kernels overlap
         ops.add_rmsnorm_quant_host(hx, hr, hw, EPS, out=(h_rout, h_codes, h_scales))
 
     for _ in range(2):
@@ -852,7 +853,7 @@ def main():
                          "kernel": "add_rmsnorm_pipe_kernel<bf16,4,e4m3> (256 threads x 4 vectors per row)"},
             "e2e": {"value": round(e2e_tbs, 5), "unit": "TB/s", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
                     "ms_per_step": round(e2e_ms / e2e_steps, 4), "steps": e2e_steps,
-                    "path": "kernelverse_b200.ops.add_rmsnorm_quant_host (pinned host buffers, 1024-row chunks on 3 streams)"},
+                    "path": "kernelverse_b200.ops.add_rmsnorm_quant_host (pinned host buffers; 1024-row chunks, 256 and 512 at the ends; copy-in, kernel and copy-out streams)"},
             "gpu_launches": args.steps,
             "clocks": clocks,
             "cpu_baseline": cpu,

@@ -160,22 +160,41 @@ _pipe_streams = {}
 _pipe_buffers = {}
 
 
+def _row_chunks(rows: int, chunk: int, edge: int):
+    """Chunk sizes summing to ``rows``: ``edge, 2*edge, ...`` (below ``chunk``) at both ends when the
+    rows allow it, ``chunk`` in the middle and the remainder as the last middle chunk."""
+    ramp, c = [], max(1, edge)
+    while c < chunk:
+        ramp.append(c)
+        c *= 2
+    if 2 * sum(ramp) + chunk > rows:
+        ramp = []
+    mid = rows - 2 * sum(ramp)
+    middle = [chunk] * (mid // chunk) + ([mid % chunk] if mid % chunk else [])
+    return ramp + middle + ramp[::-1]
+
+
 def add_rmsnorm_quant_host(x: torch.Tensor, residual: torch.Tensor, weight: torch.Tensor, eps: float,
                            quant_dtype: torch.dtype = torch.float8_e4m3fn, out=None, device=None,
-                           chunk_rows: int = 1024, nstreams: int = 3):
+                           chunk_rows: int = 1024, edge_rows: int = 256, slots: int = 3):
     """:func:`add_rmsnorm_quant` for host-resident ``[..., H]`` tensors, through the GPU.
 
-    Rows travel in chunks of ``chunk_rows`` through ``nstreams`` CUDA streams: chunk i's copy in,
-    its kernel and its copy out are queued on stream ``i % nstreams``, so the copies in and out of
-    different chunks (one copy engine each way) and the kernels overlap.  Rows are independent, so
-    the results equal :func:`add_rmsnorm_quant`'s.  Inputs should be pinned for the copies to
-    overlap.  Returns host tensors ``(residual_out, codes, scales)`` (into ``out`` when given); they
-    are complete once the current stream's work is, like any non-blocking copy to the host.
+    Rows travel in chunks through three CUDA streams, one per stage: copies in, kernels, copies
+    out, chained chunk by chunk with events.  The copy-in stream only waits for a device buffer
+    slot (``slots`` of them, reused round robin) to be copied out, so the two copy engines run
+    side by side.  Chunks are ``chunk_rows`` rows, ramping up from ``edge_rows`` at the start and
+    back down at the end, so the first copy in and the last copy out, which run alone, are short.
+    Rows are independent, so the results equal :func:`add_rmsnorm_quant`'s.  Inputs should be
+    pinned for the copies to overlap.  Returns host tensors ``(residual_out, codes, scales)``
+    (into ``out`` when given); they are complete once the current stream's work is, like any
+    non-blocking copy to the host.
     """
     if x.is_cuda or residual.is_cuda:
         raise ValueError("add_rmsnorm_quant_host takes host tensors; use add_rmsnorm_quant for device tensors")
     if x.shape != residual.shape or x.dtype != residual.dtype:
         raise ValueError("x and residual must have the same shape and dtype")
+    if slots < 1:
+        raise ValueError("add_rmsnorm_quant_host needs at least one buffer slot")
     dev = torch.device(device) if device is not None else torch.device("cuda", torch.cuda.current_device())
     h = x.shape[-1]
     rows = x.numel() // max(h, 1)
@@ -186,41 +205,46 @@ def add_rmsnorm_quant_host(x: torch.Tensor, residual: torch.Tensor, weight: torc
                torch.empty(x.shape[:-1], dtype=torch.float32, pin_memory=pin))
     h_rout, h_codes, h_scales = (t.view(rows, h) if i < 2 else t.view(rows) for i, t in enumerate(out))
     cur = torch.cuda.current_stream(dev)
-    key = (dev.index, nstreams)
-    if key not in _pipe_streams:
-        _pipe_streams[key] = [torch.cuda.Stream(dev) for _ in range(nstreams)]
-    streams = _pipe_streams[key]
+    if dev.index not in _pipe_streams:
+        _pipe_streams[dev.index] = tuple(torch.cuda.Stream(dev) for _ in range(3))
+    s_in, s_run, s_out = _pipe_streams[dev.index]
     dw = weight.to(dev, non_blocking=True).contiguous()
-    dw.record_stream(cur)
+    dw.record_stream(s_run)
     cr = max(1, min(chunk_rows, rows))
-    # Device chunk buffers, one set per stream, kept across calls: a call's streams start after
-    # the current stream (s.wait_stream) and the current stream waits for them at the end, so
-    # the previous call's chunks are done with a set before this call reuses it.
-    bkey = (dev.index, nstreams, cr, h, x.dtype, quant_dtype)
-    slots = _pipe_buffers.get(bkey)
-    if slots is None:
-        slots = [(torch.empty((cr, h), dtype=x.dtype, device=dev), torch.empty((cr, h), dtype=x.dtype, device=dev),
-                  torch.empty((cr, h), dtype=x.dtype, device=dev), torch.empty((cr, h), dtype=quant_dtype, device=dev),
-                  torch.empty((cr,), dtype=torch.float32, device=dev)) for _ in streams]
+    # Device buffer slots kept across calls: the stage streams start after the current stream and
+    # the current stream waits for them at the end, so the previous call is done with every slot
+    # before this call reuses one.
+    bkey = (dev.index, slots, cr, h, x.dtype, quant_dtype)
+    bufs = _pipe_buffers.get(bkey)
+    if bufs is None:
+        bufs = [(torch.empty((cr, h), dtype=x.dtype, device=dev), torch.empty((cr, h), dtype=x.dtype, device=dev),
+                 torch.empty((cr, h), dtype=x.dtype, device=dev), torch.empty((cr, h), dtype=quant_dtype, device=dev),
+                 torch.empty((cr,), dtype=torch.float32, device=dev)) for _ in range(slots)]
         _pipe_buffers.clear()              # one configuration at a time
-        _pipe_buffers[bkey] = slots
-    for s in streams:
+        _pipe_buffers[bkey] = bufs
+    for s in (s_in, s_run, s_out):
         s.wait_stream(cur)
-        dw.record_stream(s)
-    for i, r0 in enumerate(range(0, rows, cr)):
-        r1 = min(rows, r0 + cr)
-        n = r1 - r0
-        s = streams[i % nstreams]
-        dx, dr, drout, dcodes, dscales = slots[i % nstreams]
-        with torch.cuda.stream(s):
+    copied_out = [None] * slots            # event: the slot's last chunk is back on the host
+    r1 = 0
+    for i, n in enumerate(_row_chunks(rows, cr, edge_rows)):
+        r0, r1 = r1, r1 + n
+        k = i % slots
+        dx, dr, drout, dcodes, dscales = bufs[k]
+        if copied_out[k] is not None:
+            s_in.wait_event(copied_out[k])
+        with torch.cuda.stream(s_in):
             dx[:n].copy_(x2[r0:r1], non_blocking=True)
             dr[:n].copy_(r2[r0:r1], non_blocking=True)
-            call("kvb_add_rmsnorm_quant", _ptr(dx), _ptr(dr), _ptr(dw), kvb_dtype(x.dtype), n, h, float(eps),
-                 _ptr(drout), _ptr(dcodes), kvb_dtype(quant_dtype), _ptr(dscales), s.cuda_stream)
+        s_run.wait_event(s_in.record_event())
+        call("kvb_add_rmsnorm_quant", _ptr(dx), _ptr(dr), _ptr(dw), kvb_dtype(x.dtype), n, h, float(eps),
+             _ptr(drout), _ptr(dcodes), kvb_dtype(quant_dtype), _ptr(dscales), s_run.cuda_stream)
+        s_out.wait_event(s_run.record_event())
+        with torch.cuda.stream(s_out):
             h_rout[r0:r1].copy_(drout[:n], non_blocking=True)
             h_codes[r0:r1].copy_(dcodes[:n], non_blocking=True)
             h_scales[r0:r1].copy_(dscales[:n], non_blocking=True)
-    for s in streams:
+        copied_out[k] = s_out.record_event()
+    for s in (s_in, s_run, s_out):
         cur.wait_stream(s)
     return out
 

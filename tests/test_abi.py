@@ -79,3 +79,18 @@ def test_host_entry_argument_checks_need_no_gpu():
         ops.add_rmsnorm_quant_host(x, torch.zeros(4, 32, dtype=torch.bfloat16), torch.ones(64), 1e-6)
     with pytest.raises(ValueError, match="same shape"):
         ops.add_rmsnorm_quant_host(x, torch.zeros(4, 64, dtype=torch.float16), torch.ones(64), 1e-6)
+    with pytest.raises(ValueError, match="buffer slot"):
+        ops.add_rmsnorm_quant_host(x, x.clone(), torch.ones(64), 1e-6, slots=0)
+
+
+@pytest.mark.parametrize("rows,chunk,edge", [(0, 1, 256), (1, 1, 256), (7, 7, 256), (1024, 1024, 256),
+                                             (1500, 1024, 256), (3000, 512, 256), (8192, 1024, 256),
+                                             (8192, 1024, 1), (5000, 1000, 300)])
+def test_host_entry_row_chunks(rows, chunk, edge):
+    """The host-buffer entry's row chunks cover every row once, none larger than the buffer slots,
+    short at both ends when the rows allow a ramp."""
+    from kernelverse_b200.ops import _row_chunks
+    sizes = _row_chunks(rows, chunk, edge)
+    assert sum(sizes) == rows and all(0 < n <= chunk for n in sizes)
+    if rows >= 4 * chunk and edge < chunk:
+        assert sizes[0] == edge and sizes[-1] == edge and max(sizes) == chunk
