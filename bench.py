@@ -626,6 +626,20 @@ def secondary_benchmarks(torch, ops, hbm_peak):
                 "us_per_call_host_issue": round(us_host, 3), "timing": "device events behind a device spin",
                 "bytes_per_call": nbytes})
     del flush
+    # the same shape through the per-tensor op (dynamic_scaled_int8_quant): amax pass, then the
+    # quantisation pass, which reads x again (from L2: 16.8 MB); bytes count x once
+    xs = [x] + [torch.roll(x, shifts=i, dims=0).contiguous() for i in range(1, 16)]
+    it = iter(range(1 << 30))
+    rot_t = lambda: ops.dynamic_scaled_int8_quant(xs[next(it) % 16])  # noqa: E731
+    us_t = time_fn(torch, rot_t, 320)
+    del xs
+    nbytes_t = 2048 * 4096 * 2 + 2048 * 4096 + 4 + 4
+    out.append({"workload": "per-tensor int8 quant (dynamic_scaled_int8_quant) bf16 [2048,4096]",
+                "kernel": "tensor_amax_kernel + tensor_quant_kernel (programmatic-dependent pair: per-CTA partial maxima, x into L2 before the wait)",
+                "us_per_call": round(us_t, 3), "achieved_gbs": round(nbytes_t / us_t / 1e3, 1),
+                "frac": round(nbytes_t / us_t / 1e3 / hbm_peak, 4),
+                "l2": "16 distinct inputs cycled back to back (269 MB > L2)", "timing": "device events behind a device spin",
+                "bytes_per_call": nbytes_t})
     # fourth config: paged FP8 KV write + GQA decode (one step = write the new token + attend)
     c = make_c4_inputs(torch, dev, 11)
     step = lambda: ops.paged_fp8_decode(c["q"], c["kc"], c["vc"], c["ks"], c["vs"], c["lens"], c["bt"],  # noqa: E731
@@ -659,8 +673,9 @@ def prefill_benchmarks(torch, ops, bf16_peak):
         flops = 4 * sum(n * (n + 1) // 2 for n in ql) * hq * d
         e = {"workload": f"batched_prefill_attention q_lens=kv_lens={ql}, 32/8 heads, D=128, "
                          f"{'bf16' if dt == torch.bfloat16 else 'fp32'}",
-             "kernel": ("prefill_tc_kernel (tcgen05 kind::f16, S and O in TMEM)" if dt == torch.bfloat16
-                        else "prefill_kernel (3xTF32 mma.sync m16n8k8)"),
+             "kernel": (("prefill_pp_kernel (tcgen05 kind::f16, two 128-row query tiles per CTA, S and O in TMEM)"
+                         if hq * (tq // 256) >= 148 else "prefill_tc_kernel (tcgen05 kind::f16, S and O in TMEM)")
+                        if dt == torch.bfloat16 else "prefill_kernel (3xTF32 mma.sync m16n8k8)"),
              "us_per_call": round(us, 2), "tflops": round(flops / us / 1e6, 1), "flops_per_call": flops}
         if dt == torch.bfloat16:
             e["frac_of_bf16_peak"] = round(flops / us / 1e6 / bf16_peak, 4)
@@ -696,7 +711,7 @@ def main():
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--profile-only", action="store_true",
                     help="run W warm-up + K steps of the headline kernel and exit (for ncu captures)")
-    ap.add_argument("--profile-workload", choices=["c1", "c2", "c4", "c3m16", "c3m256", "c3m4096", "prefill"],
+    ap.add_argument("--profile-workload", choices=["a1", "c1", "c2", "c4", "c3m16", "c3m256", "c3m4096", "prefill"],
                     default="c2",
                     help="workload that --profile-only runs")
     args = ap.parse_args()
@@ -746,6 +761,12 @@ def main():
         x1 = make_c1_inputs(torch, dev)
         for _ in range(args.warmup + args.steps):
             ops.per_token_group_quant_int8(x1, 4096, 1e-6)
+        torch.cuda.synchronize()
+        return
+    if args.profile_only and args.profile_workload == "a1":
+        x1 = make_c1_inputs(torch, dev)
+        for _ in range(args.warmup + args.steps):
+            ops.dynamic_scaled_int8_quant(x1)
         torch.cuda.synchronize()
         return
     if args.profile_only and args.profile_workload == "c4":

@@ -42,47 +42,83 @@ __device__ __forceinline__ float vec_amax(const Vec8<T>& v) {
   return m;
 }
 // ---------------------------------------------------------------- per-tensor
-// Pass 1: amax(|x|) -> *amax_bits (float bits; non-negative floats order like uint32).
+// Two kernels chained as programmatic dependents, with no state to zero between calls: pass 1
+// writes one partial amax per CTA, pass 2 reduces the partials and quantises, reading x again
+// (from L2 when x fits there, which it normally does right after pass 1).
+constexpr int kTensorThreads = 256;
+constexpr int kTensorMaxBlocks = 2048;    // partial maxima the workspace holds
+// Vec8s a thread keeps in flight: 8 of 16 bytes for 16-bit inputs, 4 of 32 for float.
+template <typename T> constexpr int tensor_unroll() { return sizeof(T) == 4 ? 4 : 8; }
+
+// Pass 1: partial[blockIdx.x] = amax(|x|) over the CTA's share of x.
 template <typename T>
-__global__ void __launch_bounds__(256) tensor_amax_kernel(const T* __restrict__ x, int64_t numel, int64_t nvec,
-                                                          unsigned int* __restrict__ amax_bits) {
+__global__ void __launch_bounds__(kTensorThreads, 4) tensor_amax_kernel(const T* __restrict__ x, int64_t numel,
+                                                                     int64_t nvec, float* __restrict__ partial) {
   __shared__ float scratch[32];
-  float m = 0.0f;
-  const int64_t stride = (int64_t)gridDim.x * blockDim.x;
-  for (int64_t v = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; v < nvec; v += stride) {
-    Vec8<T> a;
-    a.load(x + v * 8);
-    m = fmaxf(m, vec_amax(a));
+  constexpr int U = tensor_unroll<T>();
+  const int64_t stride = (int64_t)gridDim.x * kTensorThreads;
+  pdl_trigger();
+  if (threadIdx.x < U) {   // the CTA's first round of x into L2 while the previous kernel finishes
+    const int64_t v = (int64_t)blockIdx.x * kTensorThreads + threadIdx.x * stride;
+    if (v < nvec) prefetch_l2_bulk(x + v * 8, (uint32_t)(std::min<int64_t>(kTensorThreads, nvec - v) * Vec8<T>::kBytes));
   }
-  for (int64_t i = nvec * 8 + (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < numel; i += stride)
+  pdl_wait();
+  float m = 0.0f;
+  for (int64_t v = (int64_t)blockIdx.x * kTensorThreads + threadIdx.x; v < nvec; v += U * stride) {
+    Vec8<T> a[U];
+#pragma unroll
+    for (int u = 0; u < U; ++u)
+      if (v + u * stride < nvec) a[u].load(x + (v + u * stride) * 8);
+#pragma unroll
+    for (int u = 0; u < U; ++u)
+      if (v + u * stride < nvec) m = fmaxf(m, vec_amax(a[u]));
+  }
+  for (int64_t i = nvec * 8 + (int64_t)blockIdx.x * kTensorThreads + threadIdx.x; i < numel; i += stride)
     m = fmaxf(m, fabsf(Elem<T>::to_f(x[i])));
   m = block_reduce<true>(m, scratch);
-  if (threadIdx.x == 0) atomicMax(amax_bits, __float_as_uint(m));
+  if (threadIdx.x == 0) partial[blockIdx.x] = m;
 }
 
-// Pass 2: scale = max(float(T(amax / 127)), MIN_SCALING_FACTOR); q = round(clamp(x / scale)).
+// scale = max(float(T(amax / 127)), MIN_SCALING_FACTOR): amax / 127 is evaluated in float32
+// and rounded to the input dtype, as the reference's input-dtype arithmetic does
+// (dynamic_scaled_int8_quant.py:22).
 template <typename T>
-__global__ void __launch_bounds__(256) tensor_quant_kernel(const T* __restrict__ x, int64_t numel, int64_t nvec,
-                                                           const unsigned int* __restrict__ amax_bits,
-                                                           int8_t* __restrict__ q, float* __restrict__ scale_out,
-                                                           int32_t* __restrict__ azp_out) {
-  const float amax = __uint_as_float(*amax_bits);
-  // amax / 127 is evaluated in float32 and rounded to the input dtype, as the reference's
-  // input-dtype arithmetic does (dynamic_scaled_int8_quant.py:22).
-  const float s_in = Elem<T>::to_f(Elem<T>::from_f(__fdiv_rn(amax, kInt8Max)));
-  const float scale = fmaxf(s_in, kMinScalingFactor);
+__device__ __forceinline__ float tensor_scale(float amax) {
+  return fmaxf(Elem<T>::to_f(Elem<T>::from_f(__fdiv_rn(amax, kInt8Max))), kMinScalingFactor);
+}
+
+// Pass 2: amax = max over the npartial partials of pass 1; q = round(clamp(x / scale)).
+template <typename T>
+__global__ void __launch_bounds__(kTensorThreads, 4) tensor_quant_kernel(const T* __restrict__ x, int64_t numel,
+                                                                      int64_t nvec, const float* partial, int npartial,
+                                                                      int8_t* __restrict__ q,
+                                                                      float* __restrict__ scale_out,
+                                                                      int32_t* __restrict__ azp_out) {
+  __shared__ float scratch[32];
+  pdl_trigger();
+  pdl_wait();
+  float m = 0.0f;
+  for (int i = threadIdx.x; i < npartial; i += kTensorThreads) m = fmaxf(m, __ldcg(partial + i));
+  const float scale = tensor_scale<T>(block_reduce<true>(m, scratch));
   const Divisor d = make_divisor(scale);
+  const bool fast = fast_divisor(d);
   if (blockIdx.x == 0 && threadIdx.x == 0) {
     *scale_out = scale;
     if (azp_out) *azp_out = 0;
   }
-  const int64_t stride = (int64_t)gridDim.x * blockDim.x;
-  for (int64_t v = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; v < nvec; v += stride) {
-    Vec8<T> a;
-    a.load(x + v * 8);
-    reinterpret_cast<uint2*>(q)[v] = fast_divisor(d) ? quant8_fast(a, d) : quant8_checked(a, d);
+  constexpr int U = tensor_unroll<T>();
+  const int64_t stride = (int64_t)gridDim.x * kTensorThreads;
+  uint2* q8 = reinterpret_cast<uint2*>(q);
+  for (int64_t v = (int64_t)blockIdx.x * kTensorThreads + threadIdx.x; v < nvec; v += U * stride) {
+    Vec8<T> a[U];
+#pragma unroll
+    for (int u = 0; u < U; ++u)
+      if (v + u * stride < nvec) a[u].load(x + (v + u * stride) * 8);
+#pragma unroll
+    for (int u = 0; u < U; ++u)
+      if (v + u * stride < nvec) q8[v + u * stride] = fast ? quant8_fast(a[u], d) : quant8_checked(a[u], d);
   }
-  for (int64_t i = nvec * 8 + (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < numel; i += stride)
+  for (int64_t i = nvec * 8 + (int64_t)blockIdx.x * kTensorThreads + threadIdx.x; i < numel; i += stride)
     q[i] = quant_int8(Elem<T>::to_f(x[i]), d);
 }
 
@@ -417,21 +453,26 @@ int sm_count() {
   return n;
 }
 
+// CTAs of both per-tensor passes: enough for one unrolled round a thread, at most 4 a SM (all
+// resident at once) and kTensorMaxBlocks.
+int tensor_blocks(int64_t work, int unroll) {
+  const int64_t per_block = (int64_t)kTensorThreads * unroll;
+  const int64_t cap = std::min<int64_t>(kTensorMaxBlocks, (int64_t)sm_count() * 4);
+  return (int)std::max<int64_t>(1, std::min<int64_t>((work + per_block - 1) / per_block, cap));
+}
+
 template <typename T>
-int launch_tensor_quant(const void* xv, int64_t numel, int8_t* q, float* scale, int32_t* azp,
-                        unsigned int* amax, cudaStream_t st) {
+int launch_tensor_quant(const void* xv, int64_t numel, int8_t* q, float* scale, int32_t* azp, float* partial,
+                        cudaStream_t st) {
   const T* x = static_cast<const T*>(xv);
   const bool vec = aligned16(x) && aligned8(q);
   const int64_t nvec = vec ? numel / 8 : 0;
-  const int64_t work = nvec > 0 ? nvec : numel;
-  int blocks = (int)std::min<int64_t>((work + 255) / 256, (int64_t)sm_count() * 8);
-  if (blocks < 1) blocks = 1;
-  cudaError_t e = cudaMemsetAsync(amax, 0, sizeof(unsigned int), st);
-  if (e != cudaSuccess) return set_error(KVB_E_LAUNCH, "memset amax: %s", cudaGetErrorString(e));
-  tensor_amax_kernel<T><<<blocks, 256, 0, st>>>(x, numel, nvec, amax);
-  int rc = check_launch("tensor_amax_kernel");
-  if (rc) return rc;
-  tensor_quant_kernel<T><<<blocks, 256, 0, st>>>(x, numel, nvec, amax, q, scale, azp);
+  const int blocks = tensor_blocks(nvec > 0 ? nvec : numel, nvec > 0 ? tensor_unroll<T>() : 1);
+  cudaError_t e = launch_pdl(tensor_amax_kernel<T>, dim3(blocks), dim3(kTensorThreads), 0, st, x, numel, nvec, partial);
+  if (e != cudaSuccess) return set_error(KVB_E_LAUNCH, "tensor_amax_kernel: %s", cudaGetErrorString(e));
+  e = launch_pdl(tensor_quant_kernel<T>, dim3(blocks), dim3(kTensorThreads), 0, st, x, numel, nvec,
+                 static_cast<const float*>(partial), blocks, q, scale, azp);
+  if (e != cudaSuccess) return set_error(KVB_E_LAUNCH, "tensor_quant_kernel: %s", cudaGetErrorString(e));
   return check_launch("tensor_quant_kernel");
 }
 
@@ -538,16 +579,17 @@ int launch_group_quant(const void* xv, int64_t tokens, int64_t hidden, int64_t G
 
 using namespace kvb;
 
-extern "C" size_t kvb_dynamic_scaled_int8_quant_workspace_size(void) { return 256; }
+extern "C" size_t kvb_dynamic_scaled_int8_quant_workspace_size(void) { return kTensorMaxBlocks * sizeof(float); }
 
 extern "C" int kvb_dynamic_scaled_int8_quant(const void* x, int x_dtype, int64_t numel, int8_t* q, float* scale,
                                              int32_t* azp, void* workspace, size_t workspace_bytes, void* stream) {
   if (numel < 0) return set_error(KVB_E_ARG, "dynamic_scaled_int8_quant: numel < 0");
   if (!x || !q || !scale) return set_error(KVB_E_ARG, "dynamic_scaled_int8_quant: null pointer");
-  if (!workspace || workspace_bytes < sizeof(unsigned int))
-    return set_error(KVB_E_WORKSPACE, "dynamic_scaled_int8_quant: workspace of >= 4 bytes required");
+  if (!workspace || workspace_bytes < kvb_dynamic_scaled_int8_quant_workspace_size())
+    return set_error(KVB_E_WORKSPACE, "dynamic_scaled_int8_quant: workspace of >= %zu bytes required",
+                     kvb_dynamic_scaled_int8_quant_workspace_size());
   if (((uintptr_t)workspace & 3u) != 0) return set_error(KVB_E_ALIGN, "dynamic_scaled_int8_quant: workspace not 4-byte aligned");
-  unsigned int* amax = static_cast<unsigned int*>(workspace);
+  float* amax = static_cast<float*>(workspace);
   cudaStream_t st = as_stream(stream);
   switch (x_dtype) {
     case KVB_F32: return launch_tensor_quant<float>(x, numel, q, scale, azp, amax, st);
