@@ -26,6 +26,9 @@ sharded across GPUs with no collective on the data path: weak scaling).
   host threads -- imported from ``baseline/_ref`` (``baseline/install_ref.py``); the numpy
   port in ``oracle/`` when that install is absent.  Rank 0 at N=1 only.
 * ``secondary``: the other hot-path kernels at their BASELINE configs (N=1 only).
+* ``next_rows``: the reference operators beside those configs (v2 partition outputs, cache
+  writes, other quantisation schemes, multi-token and dense decode) at the largest 16-bit
+  entry of each one's dtype sweep, with algorithmic bytes and the fraction of HBM (N=1 only).
 * ``sharded_config5``: the fifth config at every N, including N=1: the column-sharded TP
   GEMM (fused all-gather, GEMM + NCCL, shard GEMM) and the batch-512 decode, each with the
   single-GPU time T1 measured in the same run and the efficiency T1 / (N T_N).
@@ -655,6 +658,156 @@ def secondary_benchmarks(torch, ops, hbm_peak):
     return out
 
 
+def _cycled(torch, make, nbytes: int, calls: int = 60, min_total: int = 280 << 20):
+    """Mean us per call cycling through enough seeded input sets (``make(i)`` -> a zero-argument
+    call) that together they exceed twice L2, so every call reads its inputs from HBM."""
+    n = max(1, -(-min_total // max(nbytes, 1)))
+    fns = [make(i) for i in range(n)]
+    it = iter(range(1 << 30))
+    us = time_fn(torch, lambda: fns[next(it) % n](), calls)
+    return us, n
+
+
+def next_row_benchmarks(torch, ops, hbm_peak):
+    """The reference operators beside the BASELINE configs (v2 partition outputs, the cache
+    writes, the other quantisation schemes, multi-token and dense decode), each at the largest
+    16-bit entry of the reference's dtype sweep for it, bytes counted as each op must move them."""
+    dev = torch.device("cuda")
+    bf = torch.bfloat16
+    out = []
+
+    def entry(workload, kernel, nbytes, make, calls=60):
+        try:
+            us, n = _cycled(torch, make, nbytes, calls)
+            out.append({"workload": workload, "kernel": kernel, "us_per_call": round(us, 2), "bytes_per_call": nbytes,
+                        "achieved_gbs": round(nbytes / us / 1e3, 1), "frac": round(nbytes / us / 1e3 / hbm_peak, 4),
+                        "l2": f"{n} input sets cycled" if n > 1 else "inputs larger than L2"})
+        except Exception as exc:   # recorded, not hidden: the line says which op failed and why
+            out.append({"workload": workload, "error": f"{type(exc).__name__}: {exc}"})
+        torch.cuda.empty_cache()
+
+    def gen(i):
+        return torch.Generator(device=dev).manual_seed(4000 + i)
+
+    # paged_attention_v2 with its partition outputs: B=8, L=2048, 32/8 heads, D=128, block 16,
+    # partition 256, bf16 (the longest sequence is read on the host once, outside the timing)
+    b, L, hq, hkv, d, bs, part = 8, 2048, 32, 8, 128, 16, 256
+    nblk = b * L // bs
+    pmax = L // part
+    v2_bytes = (2 * b * L * hkv * d * 2 + 2 * b * hq * d * 2 + 2 * b * hq * pmax * 2 + b * hq * pmax * d * 2
+                + nblk * 4 + b * 4)
+
+    def make_v2(i):
+        g = gen(i)
+        kc = torch.randn((nblk, hkv, bs, d), generator=g, device=dev).to(bf)
+        vc = torch.randn((nblk, hkv, bs, d), generator=g, device=dev).to(bf)
+        q = torch.randn((b, hq, d), generator=g, device=dev).to(bf)
+        bt = torch.randperm(nblk, generator=g, device=dev).to(torch.int32).view(b, L // bs)
+        lens = torch.full((b,), L, dtype=torch.int32, device=dev)
+        return lambda: ops._paged_attention(q, kc, vc, lens, bt, num_kv_heads=hkv, block_size=bs, num_blocks=nblk,
+                                            max_seq_len=L, scale=d ** -0.5, partition_size=part, v2=True)
+    entry("paged_attention_v2 (exp_sums, max_logits, tmp_out) B=8, L=2048, 32/8 heads, D=128, block 16, partition 256, bf16",
+          "paged_decode_kernel<bf16,128> + decode_merge_kernel (partition outputs)", v2_bytes, make_v2)
+
+    # flash_decoding_attention: B=8, Sq=1, S=4096, 32 heads, D=128, chunk 256, bf16
+    b, h, s, d, chunk = 8, 32, 4096, 128, 256
+    p = s // chunk
+    fd_bytes = 2 * b * h * s * d * 2 + 2 * b * h * d * 2 + 2 * b * h * p * 2 + b * h * p * d * 2
+
+    def make_fd(i):
+        g = gen(i)
+        kc = torch.randn((b, h, s, d), generator=g, device=dev).to(bf)
+        vc = torch.randn((b, h, s, d), generator=g, device=dev).to(bf)
+        q = torch.randn((b, h, 1, d), generator=g, device=dev).to(bf)
+        return lambda: ops.flash_decoding_attention(q, kc, vc, chunk, False)
+    entry("flash_decoding_attention B=8, Sq=1, S=4096, 32 heads, D=128, chunk 256, bf16",
+          "paged_decode_kernel<bf16,128> (one head per sequence) + decode_merge_kernel", fd_bytes, make_fd, calls=20)
+
+    # flash_attn_with_kvcache: B=4, Sq=16, Sk=4096, 16 heads, D=128, ragged cache lengths, bf16
+    b, sq, sk, h, d = 4, 16, 4096, 16, 128
+    lens_fa = torch.randint(sk // 4, sk + 1, (b,), generator=torch.Generator().manual_seed(77), dtype=torch.int32)
+    fa_bytes = int(lens_fa.sum()) * h * d * 2 * 2 + 2 * b * sq * h * d * 2 + b * h * sq * 4 + b * 4
+
+    def make_fa(i):
+        g = gen(i)
+        kc = torch.randn((b, sk, h, d), generator=g, device=dev).to(bf)
+        vc = torch.randn((b, sk, h, d), generator=g, device=dev).to(bf)
+        q = torch.randn((b, sq, h, d), generator=g, device=dev).to(bf)
+        lens = lens_fa.to(dev)
+        return lambda: ops.flash_attn_with_kvcache(q, kc, vc, lens)
+    entry(f"flash_attn_with_kvcache B=4, Sq=16, Sk=4096, 16 heads, D=128, cache lengths {lens_fa.tolist()}, bf16",
+          "paged_decode_kernel<bf16,128> (16 query tokens per sequence) + decode_merge_kernel", fa_bytes, make_fa)
+
+    # batched_decode_attention: B=16, L=4096, 32/8 heads, D=128, ragged lengths, bf16
+    b, L, hq, hkv, d = 16, 4096, 32, 8, 128
+    lens_bd = torch.randint(L // 4, L + 1, (b,), generator=torch.Generator().manual_seed(78), dtype=torch.int64)
+    bd_bytes = int(lens_bd.sum()) * hkv * d * 2 * 2 + 2 * b * hq * d * 2 + b * 8
+
+    def make_bd(i):
+        g = gen(i)
+        kc = torch.randn((b, L, hkv, d), generator=g, device=dev).to(bf)
+        vc = torch.randn((b, L, hkv, d), generator=g, device=dev).to(bf)
+        q = torch.randn((b, hq, d), generator=g, device=dev).to(bf)
+        lens = lens_bd.to(dev)
+        return lambda: ops.batched_decode_attention(q, kc, vc, lens)
+    entry(f"batched_decode_attention B=16, L=4096, 32/8 heads, D=128, lengths U[1024, 4096] (sum {int(lens_bd.sum())}), bf16",
+          "paged_decode_kernel<bf16,128> (dense cache) + decode_merge_kernel", bd_bytes, make_bd)
+
+    # paged_kv_cache_update: 1024 tokens into [2048 blocks, 16, 16 heads, 128] bf16, int64 slots
+    # with invalid (-1) entries; the op returns a new cache (copy + scatter)
+    nt, nb, bs, h, d = 1024, 2048, 16, 16, 128
+    kvu_bytes = 2 * nb * bs * h * d * 2 + nt * h * d * 2 + nt * 8
+
+    def make_kvu(i):
+        g = gen(i)
+        cache = torch.randn((nb, bs, h, d), generator=g, device=dev).to(bf)
+        tok = torch.randn((nt, h, d), generator=g, device=dev).to(bf)
+        slots = torch.randperm(nb * bs, generator=g, device=dev)[:nt]
+        slots[::7] = -1
+        return lambda: ops.paged_kv_cache_update(tok, cache, slots)
+    entry("paged_kv_cache_update 1024 tokens into [2048, 16, 16, 128] bf16 (every 7th slot -1), new cache returned",
+          "copy16_kernel + scatter_rows_kernel", kvu_bytes, make_kvu)
+
+    # kv_cache_write: B=4, 8 heads, max_seq_len 4096, 256 new tokens, D=128, per-batch positions, bf16
+    b, h, smax, w, d = 4, 8, 4096, 256, 128
+    kvw_bytes = 2 * 2 * b * h * smax * d * 2 + 2 * b * h * w * d * 2 + b * w * 8
+
+    def make_kvw(i):
+        g = gen(i)
+        kc = torch.randn((b, h, smax, d), generator=g, device=dev).to(bf)
+        vc = torch.randn((b, h, smax, d), generator=g, device=dev).to(bf)
+        k = torch.randn((b, h, w, d), generator=g, device=dev).to(bf)
+        v = torch.randn((b, h, w, d), generator=g, device=dev).to(bf)
+        pos = torch.stack([torch.randperm(smax, generator=g, device=dev)[:w] for _ in range(b)])
+        return lambda: ops.kv_cache_write(kc, vc, k, v, pos)
+    entry("kv_cache_write B=4, 8 heads, max_seq_len 4096, 256 new tokens, D=128, per-batch positions, bf16, new caches returned",
+          "copy16_kernel x2 + kv_write_rows_kernel", kvw_bytes, make_kvw)
+
+    # static_scaled_int8_quant: float32 [8192, 4096] (the reference's largest 2-D shape)
+    m, k = 8192, 4096
+    sq_bytes = m * k * 4 + m * k + 8
+
+    def make_sq(i):
+        g = gen(i)
+        x = torch.randn((m, k), generator=g, device=dev) * 3
+        sc = torch.tensor([0.05], device=dev)
+        return lambda: ops.static_scaled_int8_quant(x, sc)
+    entry("static_scaled_int8_quant float32 [8192, 4096], scale 0.05, no azp", "static_quant_kernel<float>",
+          sq_bytes, make_sq)
+
+    # per_token_group_quant_int8 with group 128: bf16 [4096, 4096]
+    m, k, grp = 4096, 4096, 128
+    gq_bytes = m * k * 2 + m * k + m * (k // grp) * 4
+
+    def make_gq(i):
+        g = gen(i)
+        x = torch.randn((m, k), generator=g, device=dev).to(bf)
+        return lambda: ops.per_token_group_quant_int8(x, grp, 1e-6)
+    entry("per_token_group_quant_int8 bf16 [4096, 4096], group 128", "group quant (groups of <= 256 in warp shuffles)",
+          gq_bytes, make_gq)
+    return out
+
+
 def prefill_benchmarks(torch, ops, bf16_peak):
     """Packed causal prefill (batched_prefill_attention) at the reference's default shape and
     its long full-prefill sweep point; FLOPs count the causal (q, k) pairs only."""
@@ -848,6 +1001,7 @@ def main():
     if world == 1 and not args.no_secondary:
         secondary = (secondary_benchmarks(torch, ops, hbm_peak) + gemm_benchmarks(torch, ops, hbm_peak) +
                      prefill_benchmarks(torch, ops, bf16_peak))
+    next_rows = next_row_benchmarks(torch, ops, hbm_peak) if world == 1 and not args.no_secondary else None
     sharded = None
     if not args.no_secondary:
         sharded = sharded_benchmarks(torch, ops, dist, world, rank, hbm_peak)
@@ -882,6 +1036,8 @@ def main():
         }
         if secondary:
             line["secondary"] = secondary
+        if next_rows:
+            line["next_rows"] = next_rows
         if sharded:
             line["sharded_config5"] = sharded
         emit(line)

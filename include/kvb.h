@@ -285,6 +285,13 @@ KVB_API int kvb_kv_cache_write(const void* key, const void* value, const void* k
 KVB_API size_t kvb_paged_attention_workspace_size(int batch, int num_q_heads, int head_dim, int max_partitions);
 
 /*
+ * The partition size kvb_paged_attention uses for partition_size 0: 512 tokens, halved down to
+ * 64 while sequences * ceil(max_seq_len / size) is below two per SM of the current device.
+ * A caller sizes the workspace with ceil(max_seq_len / that size) partitions.
+ */
+KVB_API int kvb_paged_attention_auto_partition(int sequences, int64_t max_seq_len);
+
+/*
  * GQA decode attention over a paged KV cache, split over partitions of the sequence.
  * Replaces operators/attention/paged_attention_v1/paged_attention_v1.py:27-92 and, with the
  * v2 outputs, operators/attention/paged_attention_v2/paged_attention_v2.py:28-175.
@@ -302,7 +309,9 @@ KVB_API size_t kvb_paged_attention_workspace_size(int batch, int num_q_heads, in
  * k_new / v_new [B, Hkv, D] (new_dtype, optional, e4m3 caches only): each sequence's newest
  * token (position seq_len - 1) is first quantised (e4m3(clamp(x / scale[h]))) and written
  * to its slot, and the attention uses the written codes.
- * partition_size: tokens per split-KV partition (multiple of 16; 0 = 512).
+ * partition_size: tokens per split-KV partition (multiple of 16; 0 = automatic:
+ * kvb_paged_attention_auto_partition(batch, max_seq_len), or 512 when the workspace was
+ * sized for 512-token partitions).
  * exp_sums, max_logits [B, Hq, max_partitions] and tmp_out [B, Hq, max_partitions, D]
  * (out_dtype, optional, all or none): the v2 partition outputs; then out uses the v2
  * normalisation (global_sum + 1e-6) and max_partitions must equal

@@ -42,6 +42,7 @@ SIGNATURES = {
     "kvb_paged_fp8_kv_write": (_I, [_P, _I, _P, _P, _I, _P, _I64, _I64, _I, _I, _P]),
     "kvb_kv_cache_write": (_I, [_P, _P, _P, _P, _P, _P, _P, _I, _I, _I, _I64, _I64, _I64, _I64, _I64, _P]),
     "kvb_paged_attention_workspace_size": (_SZ, [_I, _I, _I, _I]),
+    "kvb_paged_attention_auto_partition": (_I, [_I, _I64]),
     "kvb_flash_attn_with_kvcache_workspace_size": (_SZ, [_I, _I, _I, _I, _I64]),
     "kvb_flash_attn_with_kvcache": (_I, [_P, _P, _P, _I, _P, _I, _I, _I, _I64, _I, _I, _I, _F, _P, _P, _P, _SZ, _P]),
     "kvb_paged_attention": (_I, [_P, _I, _P, _P, _I, _P, _P, _P, _I, _P, _I64, _I, _I, _I, _I, _I, _I64, _I64, _F,

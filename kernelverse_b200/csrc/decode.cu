@@ -128,8 +128,10 @@ struct DecodeArgs {
   float sm_scale;
   int batch, hq, hkv, group, bs, part, pmax, tiles_per_kv, stages;
   int q_dtype, new_dtype, sl64, v2_dtype;
-  int qtok;                 // query tokens per cached sequence: query row b reads sequence b / qtok
+  int qtok;                 // CTA rows per cached sequence: CTA row b reads sequence b / qtok
   int hc;                   // KV heads per CTA (hkv, or a divisor of it with the heads split over grid.z)
+  int fold;                 // query rows per CTA row: CTA row b serves query rows b*fold .. b*fold+fold-1,
+                            // each KV head's tile holding group * fold (query row, head) pairs
 };
 
 // Length of the cached sequence that query row b attends to.
@@ -232,18 +234,23 @@ __global__ void __launch_bounds__(MAXT, MAXT <= 288 ? 2 : 1) paged_decode_kernel
         const int64_t t1 = t_end < t0 + kChunk ? t_end : t0 + kChunk;   // rows past the end are not copied
         mbar_arrive_expect_tx(&full[s], 2u * (uint32_t)(t1 - t0) * srow);
         if (srow != row_bytes) {
-          // Heads split over CTAs: each token row's slice of this CTA's heads, one copy each.
-          for (int64_t t = t0; t < t1; ++t) {
+          // Heads split over CTAs: each token row's slice of this CTA's heads, one copy each; the
+          // block is looked up once per run of rows inside it.
+          for (int64_t t = t0; t < t1;) {
+            const int64_t n = min(t1 - t, (int64_t)a.bs - t % a.bs);
             const int64_t row = token_row(a, b, t);
-            const size_t doff = (size_t)(t - t0) * srow;
             if (row < 0) {
               atomicOr(&g_tu_status, kStatusBadIndex);
               asm volatile("mbarrier.complete_tx.relaxed.cta.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(&full[s])),
-                           "r"(2 * srow) : "memory");
+                           "r"(2 * (uint32_t)n * srow) : "memory");
             } else {
-              bulk_g2s(kstage(s) + doff, kc + row * row_bytes + head_off, srow, &full[s], pol);
-              bulk_g2s(vstage(s) + doff, vc + row * row_bytes + head_off, srow, &full[s], pol);
+              for (int64_t j = 0; j < n; ++j) {
+                const size_t doff = (size_t)(t + j - t0) * srow;
+                bulk_g2s(kstage(s) + doff, kc + (row + j) * row_bytes + head_off, srow, &full[s], pol);
+                bulk_g2s(vstage(s) + doff, vc + (row + j) * row_bytes + head_off, srow, &full[s], pol);
+              }
             }
+            t += n;
           }
           continue;
         }
@@ -275,9 +282,11 @@ __global__ void __launch_bounds__(MAXT, MAXT <= 288 ? 2 : 1) paged_decode_kernel
   const int g = lane >> 2, c = lane & 3;
   const int kvl = warp / a.tiles_per_kv, nt = warp % a.tiles_per_kv;   // KV head within this CTA's group
   const int kvh = h0 + kvl;
-  const int qn = nt * 8 + g;                         // this lane's query head within the group (B operand col)
-  const bool qvalid = qn < a.group;
-  const int qhead = kvh * a.group + qn;
+  const int qn = nt * 8 + g;                         // this lane's query within the tile group (B operand col)
+  const bool qvalid = qn < a.group * a.fold;
+  const int qtq = qn / a.group;                      // its query row within the CTA row (0 without folding)
+  const int qhead = kvh * a.group + (qn - qtq * a.group);
+  const int64_t qrow = (int64_t)b * a.fold + qtq;
   // Q as the B operand of QK, permuted: slab j, regs (b0, b1) = dims (D/4)c + 4j + {0,1 | 2,3}.
   uint32_t qf[SLABS][2];
 #pragma unroll
@@ -285,7 +294,7 @@ __global__ void __launch_bounds__(MAXT, MAXT <= 288 ? 2 : 1) paged_decode_kernel
     float q4[4];
 #pragma unroll
     for (int e = 0; e < 4; ++e)
-      q4[e] = qvalid ? load_any(a.q, a.q_dtype, ((int64_t)b * a.hq + qhead) * D + (D / 4) * c + 4 * j + e) : 0.0f;
+      q4[e] = qvalid ? load_any(a.q, a.q_dtype, (qrow * a.hq + qhead) * D + (D / 4) * c + 4 * j + e) : 0.0f;
     qf[j][0] = pack2(q4[0], q4[1], BF);
     qf[j][1] = pack2(q4[2], q4[3], BF);
   }
@@ -465,10 +474,11 @@ __global__ void __launch_bounds__(MAXT, MAXT <= 288 ? 2 : 1) paged_decode_kernel
 #pragma unroll
   for (int e = 0; e < 2; ++e) {
     const int hn = nt * 8 + 2 * c + e;
-    if (hn >= a.group) continue;
-    const int h = kvh * a.group + hn;
+    if (hn >= a.group * a.fold) continue;
+    const int tq = hn / a.group;
+    const int h = kvh * a.group + (hn - tq * a.group);
     const float m = e ? m1 : m0, l = e ? l1 : l0;
-    const int64_t pi = ((int64_t)b * a.hq + h) * a.pmax + p;
+    const int64_t pi = (((int64_t)b * a.fold + tq) * a.hq + h) * a.pmax + p;
     if (g == 0) {
       a.m_part[pi] = m;
       a.l_part[pi] = l;
@@ -711,7 +721,7 @@ int launch_decode_t(DecodeArgs& a, size_t smem, cudaStream_t st) {
     attr_smem = smem;
   }
   const int threads = (a.hc * a.tiles_per_kv + 1) * 32;
-  dim3 grid(a.pmax, a.batch, a.hkv / a.hc);
+  dim3 grid(a.pmax, a.batch / a.fold, a.hkv / a.hc);
   cudaError_t e = launch_pdl(kern, grid, dim3(threads), smem, st, a);
   if (e != cudaSuccess) return set_error(KVB_E_LAUNCH, "paged_decode_kernel: %s", cudaGetErrorString(e));
   return check_launch("paged_decode_kernel");
@@ -735,6 +745,20 @@ int launch_decode_d(DecodeArgs& a, int head_dim, size_t smem, cudaStream_t st) {
 }  // namespace kvb
 
 using namespace kvb;
+
+extern "C" int kvb_paged_attention_auto_partition(int sequences, int64_t max_seq_len) {
+  // 512-token partitions, halved down to 64 while the grid has fewer (sequence, partition) CTAs
+  // than two for each SM of the current device (148 when there is none)
+  int dev = 0, sms = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess ||
+      sms <= 0) {
+    cudaGetLastError();
+    sms = 148;
+  }
+  int part = 512;
+  while (part > 64 && (int64_t)std::max(sequences, 1) * ((max_seq_len + part - 1) / part) < 2 * (int64_t)sms) part /= 2;
+  return part;
+}
 
 extern "C" size_t kvb_paged_attention_workspace_size(int batch, int num_q_heads, int head_dim, int max_partitions) {
   const size_t n = (size_t)batch * num_q_heads * max_partitions;
@@ -768,9 +792,16 @@ static int paged_attention_impl(const void* query, int q_dtype, const void* key_
   if ((k_new || v_new) && (!k_new || !v_new || cache_dtype != KVB_E4M3 || !is_float_dtype(new_dtype)))
     return set_error(KVB_E_ARG, "paged_attention: the fused write needs k_new, v_new and an e4m3 cache");
   const int group = num_q_heads / num_kv_heads;
-  const int tiles = (group + 7) / 8;
   if (qtok < 1 || batch % qtok) return set_error(KVB_E_ARG, "paged_attention: batch must be a multiple of qtok");
   if ((k_new || v_new) && qtok != 1) return set_error(KVB_E_ARG, "paged_attention: the fused write needs one query per sequence");
+  // Query rows of one sequence folded into one CTA row (tensor-core kernels, no v2 outputs): the
+  // largest divisor of qtok whose (query row, head) pairs per KV head fill at most 16 tiles of 8,
+  // so those rows read the sequence's K/V once between them.
+  int fold = 1;
+  if (cache_dtype != KVB_F32 && qtok > 1 && !exp_sums)
+    for (int f = qtok; f > 1; --f)
+      if (qtok % f == 0 && (group * f + 7) / 8 <= 16) { fold = f; break; }
+  const int tiles = (group * fold + 7) / 8;
   // KV heads per CTA (tensor-core kernels): all of them when their (kv head, 8-query) tiles fit
   // 16 consumer warps and two 16-token stages of their K/V fit in shared memory; else the
   // largest divisor of num_kv_heads whose tiles fit 8 warps and whose stages fit (heads split
@@ -789,7 +820,14 @@ static int paged_attention_impl(const void* query, int q_dtype, const void* key_
       }
     }
   }
-  int part = partition_size > 0 ? partition_size : 512;
+  int part = partition_size;
+  if (part <= 0) {
+    // automatic: smaller partitions for small grids, unless the workspace was sized for 512
+    part = kvb_paged_attention_auto_partition(batch / qtok, max_seq_len);
+    const int64_t pm = std::max<int64_t>(1, (max_seq_len + part - 1) / part);
+    if (pm > 12288 || kvb_paged_attention_workspace_size(batch, num_q_heads, head_dim, (int)pm) > workspace_bytes)
+      part = 512;
+  }
   if (part % kChunk) return set_error(KVB_E_SHAPE, "paged_attention: partition_size must be a multiple of 16");
   const int64_t pmax64 = (max_seq_len + part - 1) / part;
   if (pmax64 > 12288)
@@ -828,7 +866,7 @@ static int paged_attention_impl(const void* query, int q_dtype, const void* key_
   a.sm_scale = sm_scale;
   a.batch = batch; a.hq = num_q_heads; a.hkv = num_kv_heads; a.group = group; a.bs = block_size; a.part = part;
   a.pmax = pmax; a.tiles_per_kv = tiles; a.stages = stages;
-  a.qtok = qtok; a.hc = hc;
+  a.qtok = qtok / fold; a.hc = hc; a.fold = fold;
   a.q_dtype = q_dtype; a.new_dtype = new_dtype; a.sl64 = seq_lens_dtype == KVB_I64; a.v2_dtype = out_dtype;
   const size_t smem = stage_bytes * stages;
   cudaStream_t st = as_stream(stream);
@@ -886,7 +924,8 @@ extern "C" int kvb_paged_attention(const void* query, int q_dtype, const void* k
 
 extern "C" size_t kvb_flash_attn_with_kvcache_workspace_size(int batch, int seq_len_q, int num_heads, int head_dim,
                                                              int64_t seq_len_k) {
-  const int64_t pmax = seq_len_k > 0 ? (seq_len_k + 511) / 512 : 1;
+  const int part = kvb_paged_attention_auto_partition(batch, seq_len_k);
+  const int64_t pmax = seq_len_k > 0 ? (seq_len_k + part - 1) / part : 1;
   return kvb_paged_attention_workspace_size(batch * seq_len_q, num_heads, head_dim, (int)pmax);
 }
 

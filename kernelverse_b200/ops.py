@@ -328,7 +328,8 @@ def _paged_attention(query, key_cache, value_cache, seq_lens, block_table, *, nu
     b, hq, d = query.shape
     out_dtype = out_dtype or query.dtype
     out = torch.empty((b, hq, d), dtype=out_dtype, device=dev)
-    part = partition_size if partition_size else 512
+    # partition_size 0: the library's automatic size (smaller partitions for small grids)
+    part = partition_size if partition_size else _lib.lib().kvb_paged_attention_auto_partition(b, int(max_seq_len))
     pmax = max(1, -(-int(max_seq_len) // part))
     es = ml = tmp = None
     if v2:
