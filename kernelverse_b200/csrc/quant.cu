@@ -178,29 +178,37 @@ __global__ void __launch_bounds__(256) static_quant_kernel(const T* __restrict__
 }
 
 // ---------------------------------------------------------------- per-group, small groups
-// One 8-element vector per thread; a group of G = 8*L elements spans L consecutive lanes
-// (L a power of two <= 32), so its amax is an L-lane shuffle reduction.
-template <typename T>
+// 8-element vectors, one per lane of a warp sub-chunk; a group of G = 8*L elements spans L
+// consecutive lanes (L a power of two <= 32), so its amax is an L-lane shuffle reduction.
+// Each warp takes U sub-chunks of 32 vectors per step (whole groups, since lanes divides 32) and
+// issues all their loads before reducing any, so U loads per thread are in flight.
+template <typename T, int U>
 __global__ void __launch_bounds__(256) group_quant_subwarp_kernel(const T* __restrict__ x, int64_t nvec, int lanes,
                                                                   float eps, int8_t* __restrict__ q,
                                                                   float* __restrict__ scales) {
-  const int64_t stride = (int64_t)gridDim.x * blockDim.x;
+  const int lane = threadIdx.x & 31;
+  const int64_t nwarps = (int64_t)gridDim.x * (blockDim.x >> 5);
   // The loop bound is warp-uniform so every lane joins each shuffle.
-  for (int64_t base = (int64_t)blockIdx.x * blockDim.x + (threadIdx.x & ~31); base < nvec; base += stride) {
-    const int64_t v = base + (threadIdx.x & 31);
-    const bool live = v < nvec;
-    Vec8<T> a;
-    float m = 0.0f;
-    if (live) {
-      a.load_stream(x + v * 8);
-      m = vec_amax(a);
-    }
-    m = group_max(m, lanes);
-    const float scale = fmaxf(__fdiv_rn(m, kInt8Max), eps);
-    if (live) {
-      const Divisor d = make_divisor(scale);
-      reinterpret_cast<uint2*>(q)[v] = fast_divisor(d) ? quant8_fast(a, d) : quant8_checked(a, d);
-      if ((v & (lanes - 1)) == 0) scales[v / lanes] = scale;
+  for (int64_t w = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5); w * 32 * U < nvec; w += nwarps) {
+    const int64_t v0 = w * 32 * U + lane;
+    Vec8<T> a[U];
+    float m[U];
+#pragma unroll
+    for (int u = 0; u < U; ++u)
+      if (v0 + u * 32 < nvec) a[u].load_stream(x + (v0 + u * 32) * 8);
+#pragma unroll
+    for (int u = 0; u < U; ++u) m[u] = v0 + u * 32 < nvec ? vec_amax(a[u]) : 0.0f;
+#pragma unroll
+    for (int u = 0; u < U; ++u) m[u] = group_max(m[u], lanes);
+#pragma unroll
+    for (int u = 0; u < U; ++u) {
+      const int64_t v = v0 + u * 32;
+      if (v < nvec) {
+        const float scale = fmaxf(__fdiv_rn(m[u], kInt8Max), eps);
+        const Divisor d = make_divisor(scale);
+        reinterpret_cast<uint2*>(q)[v] = fast_divisor(d) ? quant8_fast(a[u], d) : quant8_checked(a[u], d);
+        if ((v & (lanes - 1)) == 0) scales[v / lanes] = scale;
+      }
     }
   }
 }
@@ -555,8 +563,9 @@ int launch_group_quant(const void* xv, int64_t tokens, int64_t hidden, int64_t G
     const int64_t lanes = G / 8;
     if (lanes <= 32 && (lanes & (lanes - 1)) == 0) {
       const int64_t nvec = tokens * hidden / 8;
-      int blocks = (int)std::min<int64_t>((nvec + 255) / 256, (int64_t)sm_count() * 8);
-      group_quant_subwarp_kernel<T><<<blocks, 256, 0, st>>>(x, nvec, (int)lanes, eps, q, scales);
+      constexpr int U = sizeof(T) == 4 ? 2 : 4;   // 64 bytes of x a thread in flight
+      int blocks = (int)std::min<int64_t>((nvec + 256 * U - 1) / (256 * U), (int64_t)sm_count() * 8);
+      group_quant_subwarp_kernel<T, U><<<blocks, 256, 0, st>>>(x, nvec, (int)lanes, eps, q, scales);
       return check_launch("group_quant_subwarp_kernel");
     }
     if (sizeof(T) == 2 && lanes >= 64 && lanes <= 1024)
