@@ -94,3 +94,12 @@ def test_host_entry_row_chunks(rows, chunk, edge):
     assert sum(sizes) == rows and all(0 < n <= chunk for n in sizes)
     if rows >= 4 * chunk and edge < chunk:
         assert sizes[0] == edge and sizes[-1] == edge and max(sizes) == chunk
+
+
+@pytest.mark.parametrize("seqs,max_len,part", [(64, 8192, 512), (512, 8192, 512), (16, 4096, 128), (4, 4096, 64),
+                                               (1, 100, 64), (8, 2048, 64), (0, 0, 64)])
+def test_auto_partition_rule_needs_no_gpu(seqs, max_len, part):
+    """partition_size 0: 512 tokens, halved down to 64 while sequences x partitions is below two
+    per SM (148 SMs when no device answers, as here)."""
+    from kernelverse_b200 import _lib
+    assert _lib.lib().kvb_paged_attention_auto_partition(seqs, max_len) == part

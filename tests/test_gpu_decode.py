@@ -310,9 +310,13 @@ def test_flash_attn_with_kvcache_golden(name):
 @pytest.mark.parametrize("dt", ["FP32", "BF16", "FP16"])
 @pytest.mark.parametrize("b,sq,sk,h,hkv,d,ragged", [(4, 1, 2048, 16, 16, 128, False), (2, 16, 2048, 16, 16, 64, True),
                                                     (8, 1, 4096, 32, 32, 128, True), (2, 32, 1000, 32, 8, 128, False),
-                                                    (3, 5, 333, 8, 2, 64, True)])
+                                                    (3, 5, 333, 8, 2, 64, True), (2, 32, 700, 32, 4, 128, True),
+                                                    (2, 24, 500, 24, 2, 64, True)])
 def test_flash_attn_with_kvcache_shapes(dt, b, sq, sk, h, hkv, d, ragged):
-    """Query tokens per sequence, ragged lengths, GQA, and 32 KV heads (split over CTAs)."""
+    """Query tokens per sequence, ragged lengths, GQA, and 32 KV heads (split over CTAs).  The
+    16-bit kernels fold a sequence's query tokens into one CTA row: all of them, or (group 8 x
+    32 tokens, group 12 x 24 tokens) the largest divisor that fits, two or three CTA rows a
+    sequence."""
     rng = seeded(b * 1000 + sq * 10 + h)
     q = rng.standard_normal((b, sq, h, d)).astype(np.float32)
     k = rng.standard_normal((b, sk, hkv, d)).astype(np.float32)
